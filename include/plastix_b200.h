@@ -1,0 +1,155 @@
+/*
+ * plastix_b200.h — C ABI of the B200 (sm_100a) per-connection hot path.
+ *
+ * Every entry point takes plain device pointers and sizes, enqueues its
+ * kernels on the context's stream and returns a status code (PLX_OK = 0).
+ * Nothing here synchronises the stream except plx_ctx_sync().
+ * The failing call's message is available from plx_last_error() on the same
+ * host thread.
+ *
+ * Data layout (the reference's SoA field arrays, reference
+ * include/plastix/conn.hpp:31-36 and include/plastix/unit_state.hpp:38-44,
+ * mirrored into device memory):
+ *   connection fields  FromId u32, ToId u32, Dead u8 (bool), Weight f32, ...
+ *                      one array per field, indexed by connection id;
+ *   unit fields        Activation f32, ...   one array per field.
+ * The sweeps require the connections to be sorted by ToId (stable). The
+ * reference accumulates ForwardAcc[ToId] in connection-index order
+ * (include/plastix/plastix.hpp:133-141); a stable dst sort keeps that order
+ * inside each destination, so the per-destination sums reproduce the
+ * reference bit for bit for rows of up to PLX_SEQ_ROW_MAX connections.
+ */
+#ifndef PLASTIX_B200_H
+#define PLASTIX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define PLX_OK 0
+#define PLX_ERR_ARG 1         /* invalid argument (null, misaligned, size)  */
+#define PLX_ERR_CUDA 2        /* CUDA runtime error                          */
+#define PLX_ERR_CAPACITY 3    /* size exceeds a documented maximum           */
+#define PLX_ERR_TIMEOUT 4     /* a bounded device-side wait expired          */
+#define PLX_ERR_UNSUPPORTED 5 /* option not implemented                      */
+
+/* Rows (destination units) with at most this many connections are summed
+ * strictly left to right, exactly like the reference loop. Longer rows use a
+ * fixed-shape deterministic reduction (32-connection chunks folded in order). */
+#define PLX_SEQ_ROW_MAX 256
+
+/* ---- library / context ------------------------------------------------- */
+
+/* Replaces plastix::version() (reference src/plastix.cpp:5): "0.1.0". */
+const char* plx_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* plx_last_error(void);
+
+typedef struct plx_ctx plx_ctx;
+
+/* Creates a context on `device` that enqueues on `stream` (a cudaStream_t;
+ * NULL = the legacy default stream). Allocates one device status word. */
+int plx_ctx_create(int device, void* stream, plx_ctx** out);
+int plx_ctx_destroy(plx_ctx* ctx);
+int plx_ctx_set_stream(plx_ctx* ctx, void* stream);
+/* Wall-clock limit of every bounded device-side wait (default 2 s). */
+int plx_ctx_set_timeout_ns(plx_ctx* ctx, uint64_t timeout_ns);
+int plx_ctx_num_sms(plx_ctx* ctx, int* out);
+/* Waits for the stream, then reads and clears the device status word:
+ * PLX_ERR_TIMEOUT if a bounded wait expired since the last sync. */
+int plx_ctx_sync(plx_ctx* ctx);
+
+/* ---- CSR view of dst-sorted connections -------------------------------- */
+
+/* row_ptr[r] = first connection whose ToId >= row_base + r, r in [0,n_rows];
+ * to_id must be sorted ascending and lie in [row_base, row_base + n_rows).
+ * Derived index over the reference's ToId field (conn.hpp:13). */
+int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id, uint64_t n_edges,
+                    uint32_t row_base, uint32_t n_rows, uint32_t* row_ptr);
+
+/* Size (in u32 words) of the sweep plan for n_edges connections. */
+uint64_t plx_csr_plan_words(uint64_t n_edges, uint32_t n_rows);
+/* Builds the tile plan (row ownership per edge tile, list of rows longer
+ * than 2048 connections) used by every sweep over this row_ptr, validates
+ * row_ptr, and reports the number of long rows in *n_long_out (for
+ * plx_csr.n_long). Synchronises the stream. */
+int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                 uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
+                 uint32_t* n_long_out);
+
+typedef struct plx_csr {
+  const uint32_t* row_ptr; /* n_rows + 1 entries, row_ptr[0] == 0          */
+  const uint32_t* plan;    /* from plx_csr_plan                             */
+  uint64_t n_edges;        /* == row_ptr[n_rows], < 2^32 - 2^16             */
+  uint32_t n_rows;
+  uint32_t n_long;         /* value reported by plx_csr_plan               */
+} plx_csr;
+
+/* ---- forward sweep (Map / Combine / Apply) ----------------------------- */
+
+/* Apply kinds (the unit-side policy run once per destination row). */
+#define PLX_APPLY_IDENTITY 0  /* act = acc            traits.hpp:115-117   */
+#define PLX_APPLY_SIGMOID 1   /* act = 1/(1+exp(-acc))  mlp_xor.cpp:24-26  */
+#define PLX_APPLY_TANH 2      /* act = tanh(acc)      manual_fcc Apply      */
+#define PLX_APPLY_IPC_ERROR 3 /* err = x - acc        ipc_multilayer.cpp:147-150 */
+
+/* One forward sweep with the default Map/Combine (w * act[src], +), then
+ * Apply per row. Replaces Network::DoForwardPass, Pipeline branch
+ * (plastix.hpp:133-148) and one level of the Topological branch
+ * (plastix.hpp:112-130) for a contiguous range of destination units.
+ *   from_id   [n_edges]  FromId field (absolute unit ids)
+ *   weight    [n_edges]  Weight field
+ *   dead      [n_edges]  Dead field, or NULL when no connection is dead
+ *   act_src              Activation array indexed by FromId, act_src_len
+ *                        entries (an out-of-range FromId reads 0 and makes
+ *                        plx_ctx_sync report PLX_ERR_ARG)
+ *   act_dst   [n_rows]   Activation of the rows (written; not for IPC_ERROR)
+ *   value     [n_rows]   IPC_ERROR only: value-node x of each row (read)
+ *   err_out   [n_rows]   IPC_ERROR only: eps = x - acc (written)
+ * Connection arrays must be 16-byte aligned. */
+int plx_sweep_forward(plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id,
+                      const float* weight, const uint8_t* dead,
+                      const float* act_src, uint32_t act_src_len,
+                      int apply_kind, float* act_dst, const float* value,
+                      float* err_out);
+
+/* Forward sweep fused with the per-connection Hebbian trace rule
+ *   acc = sum w*act[src];  post = acc (identity Apply);
+ *   trace' = decay*trace + act[src]*post;  w' = w + rate*trace'
+ * in one pass over the connection SoA. Replaces DoForwardPass followed by
+ * DoUpdateConnectionState (plastix.hpp:133-148, :238-245) for that rule.
+ * Reads w_in/trace_in and writes w_out/trace_out (distinct buffers; the sweep
+ * re-reads neighbouring rows' old weights). act_dst receives post. */
+int plx_sweep_forward_hebbian(plx_ctx* ctx, const plx_csr* csr,
+                              const uint32_t* from_id, const uint8_t* dead,
+                              const float* act_src, uint32_t act_src_len,
+                              const float* w_in, float* w_out,
+                              const float* trace_in,
+                              float* trace_out, float decay, float rate,
+                              float* act_dst);
+
+/* Update kinds for plx_sweep_update (per-connection, reads a per-row value). */
+#define PLX_UPDATE_GRADIENT 1 /* w -= rate * post[dst] * act[src]
+                                 (mlp_xor.cpp:51-56, linear_regression.cpp:31-36) */
+#define PLX_UPDATE_HEBBIAN 2  /* w += rate * post[dst] * act[src]
+                                 (ipc_multilayer.cpp:183-190)                 */
+
+/* Per-connection weight update over dst-sorted connections; replaces the
+ * UpdateIncomingConnection sweep of DoUpdateConnectionState
+ * (plastix.hpp:238-245) for the two rules above. post is indexed by row.
+ * w_out may equal w_in. */
+int plx_sweep_update(plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id,
+                     const uint8_t* dead, const float* act_src,
+                     uint32_t act_src_len, const float* post, int update_kind,
+                     float rate, const float* w_in, float* w_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PLASTIX_B200_H */

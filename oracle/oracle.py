@@ -1,0 +1,164 @@
+"""numpy front end of the oracle (test infrastructure only).
+
+Loads ``oracle/libplx_oracle.so`` (the C restatement) and, when present,
+``oracle/_ref/libplx_ref.so`` (the reference compiled from its own sources).
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use
+this module; it is the checker, never the thing measured or shipped.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "libplx_oracle.so"
+REF_SO = HERE / "_ref" / "libplx_ref.so"
+
+_orc = None
+_ref = None
+
+
+def _p(a: Optional[np.ndarray]):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(c_void_p)
+
+
+def orc() -> ctypes.CDLL:
+    global _orc
+    if _orc is None:
+        if not ORACLE_SO.exists():
+            from oracle import build as _b
+            _b.build_oracle()
+        L = ctypes.CDLL(str(ORACLE_SO))
+        L.oracle_forward_pipeline.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p,
+                                              c_void_p, c_void_p, c_uint64, c_uint64,
+                                              c_int, c_void_p, c_void_p, c_void_p]
+        L.oracle_update_hebbian_trace.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p,
+                                                  c_void_p, c_void_p, c_void_p, c_float,
+                                                  c_float]
+        L.oracle_update_post.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_int, c_float, c_void_p]
+        L.oracle_step_hebbian.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_uint64, c_uint64, c_float,
+                                          c_float, c_void_p]
+        L.oracle_gather.argtypes = [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32]
+        L.oracle_survivors.argtypes = [c_void_p, c_uint64, c_void_p]
+        L.oracle_survivors.restype = c_uint64
+        L.oracle_stable_sort_u32.argtypes = [c_void_p, c_uint64, c_void_p]
+        L.oracle_sort_unique_u64.argtypes = [c_void_p, c_uint64, c_void_p]
+        L.oracle_sort_unique_u64.restype = c_uint64
+        _orc = L
+    return _orc
+
+
+def ref() -> Optional[ctypes.CDLL]:
+    """The reference build, or None when it was not built here."""
+    global _ref
+    if _ref is None and REF_SO.exists():
+        L = ctypes.CDLL(str(REF_SO))
+        L.ref_version.restype = ctypes.c_char_p
+        L.ref_sweep_run.argtypes = [c_uint64, c_uint64, c_uint64, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_int, c_float, c_float,
+                                    c_void_p, c_void_p, c_void_p]
+        L.ref_sweep_shards_create.argtypes = [c_uint64, c_uint64, c_uint64, c_void_p,
+                                              c_void_p, c_void_p, c_int, c_float, c_float]
+        L.ref_sweep_shards_create.restype = c_void_p
+        L.ref_sweep_shards_step.argtypes = [c_void_p, c_void_p]
+        L.ref_sweep_shards_destroy.argtypes = [c_void_p]
+        _ref = L
+    return _ref
+
+
+# ---------------------------------------------------------------------------
+# Forward / update (unit arrays are absolute: inputs then destinations)
+# ---------------------------------------------------------------------------
+def forward_pipeline(from_id, to_id, w, act, num_input, apply=0, dead=None, value=None):
+    """Returns (act, err) after one Pipeline DoForwardPass. act is copied."""
+    act = np.array(act, dtype=np.float32, copy=True)
+    n_units = act.size
+    acc = np.zeros(n_units, np.float32)
+    err = np.zeros(n_units, np.float32) if apply == 3 else None
+    value = None if value is None else np.ascontiguousarray(value, np.float32)
+    orc().oracle_forward_pipeline(from_id.size, _p(from_id), _p(to_id), _p(dead), _p(w),
+                                  _p(act), n_units, num_input, apply, _p(value), _p(err),
+                                  _p(acc))
+    return act, err
+
+
+def step_hebbian(from_id, to_id, w, trace, act, num_input, decay, rate, sweeps=1,
+                 dead=None):
+    """`sweeps` Pipeline DoSteps of the Hebbian trace workload. Returns new
+    (w, trace, act) arrays; act keeps the inputs in [0, num_input)."""
+    w = np.array(w, np.float32, copy=True)
+    trace = np.array(trace, np.float32, copy=True)
+    act = np.array(act, np.float32, copy=True)
+    acc = np.zeros(act.size, np.float32)
+    for _ in range(sweeps):
+        orc().oracle_step_hebbian(from_id.size, _p(from_id), _p(to_id), _p(dead), _p(w),
+                                  _p(trace), _p(act), act.size, num_input, decay, rate,
+                                  _p(acc))
+    return w, trace, act
+
+
+def update_post(from_id, to_id, act, post, w, kind, rate, dead=None):
+    w = np.array(w, np.float32, copy=True)
+    orc().oracle_update_post(from_id.size, _p(from_id), _p(to_id), _p(dead), _p(act),
+                             _p(np.ascontiguousarray(post, np.float32)), kind, rate, _p(w))
+    return w
+
+
+# ---------------------------------------------------------------------------
+# Permutations (SOAAllocator::Gather semantics)
+# ---------------------------------------------------------------------------
+def survivors(keep: np.ndarray) -> np.ndarray:
+    keep = np.ascontiguousarray(keep, np.uint8)
+    perm = np.empty(keep.size, np.uint64)
+    m = orc().oracle_survivors(_p(keep), keep.size, _p(perm))
+    return perm[:m]
+
+
+def gather(perm: np.ndarray, field: np.ndarray) -> np.ndarray:
+    perm = np.ascontiguousarray(perm, np.uint64)
+    field = np.ascontiguousarray(field)
+    out = np.empty(perm.size, field.dtype)
+    orc().oracle_gather(_p(perm), perm.size, _p(field), _p(out), field.itemsize)
+    return out
+
+
+def stable_sort_perm_u32(keys: np.ndarray) -> np.ndarray:
+    keys = np.ascontiguousarray(keys, np.uint32)
+    perm = np.empty(keys.size, np.uint64)
+    if orc().oracle_stable_sort_u32(_p(keys), keys.size, _p(perm)) != 0:
+        raise MemoryError("oracle_stable_sort_u32")
+    return perm
+
+
+def sort_unique_u64(bits: np.ndarray) -> np.ndarray:
+    bits = np.array(bits, np.uint64, copy=True)
+    out = np.empty(bits.size, np.uint64)
+    m = orc().oracle_sort_unique_u64(_p(bits), bits.size, _p(out))
+    return out[:m]
+
+
+# ---------------------------------------------------------------------------
+# The reference itself
+# ---------------------------------------------------------------------------
+def ref_sweep_run(n_src, n_dst, from_id, to_id, w, trace, act_in, sweeps, decay, rate):
+    L = ref()
+    if L is None:
+        raise FileNotFoundError(f"{REF_SO} was not built")
+    n = from_id.size
+    w_out = np.empty(n, np.float32)
+    e_out = np.empty(n, np.float32)
+    a_out = np.empty(n_dst, np.float32)
+    rc = L.ref_sweep_run(n_src, n_dst, n, _p(from_id), _p(to_id), _p(w), _p(trace),
+                         _p(act_in), sweeps, decay, rate, _p(w_out), _p(e_out), _p(a_out))
+    if rc != 0:
+        raise RuntimeError("ref_sweep_run failed")
+    return w_out, e_out, a_out

@@ -1,0 +1,188 @@
+/*
+ * plx_oracle.c — CPU restatement of the Plastix per-connection hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the checker for the sm_100a kernels:
+ * only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load
+ * it. The product library (plastix_b200/libplastix_b200.so) never calls it.
+ *
+ * Every function restates one loop of the reference (paths relative to the
+ * reference project) with the same evaluation order and single-precision
+ * rounding: built with -O2 -ffp-contract=off on x86-64 (SSE, no FMA), as the
+ * reference is. Parity of this restatement with the reference itself is pinned
+ * by tests/test_oracle_pins.py against oracle/_ref (the reference headers
+ * compiled by oracle/build_ref.py) and the committed fixtures in tests/golden/.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define APPLY_IDENTITY 0
+#define APPLY_SIGMOID 1
+#define APPLY_TANH 2
+#define APPLY_IPC_ERROR 3
+
+static float apply_value(int kind, float acc, float value) {
+  switch (kind) {
+    case APPLY_SIGMOID: /* examples/mlp-xor/mlp_xor.cpp:24-26 */
+      return 1.0f / (1.0f + expf(-acc));
+    case APPLY_TANH: /* examples/manual-fcc/manual_fcc.cpp Apply */
+      return tanhf(acc);
+    case APPLY_IPC_ERROR: /* examples/ipc-multilayer/ipc_multilayer.cpp:147-150 */
+      return value - acc;
+    default: /* include/plastix/traits.hpp:115-117 */
+      return acc;
+  }
+}
+
+/*
+ * Network::DoForwardPass, Pipeline branch (include/plastix/plastix.hpp:133-148)
+ * with DefaultForwardPass Map/Combine (traits.hpp:110-114):
+ *   for C in connection order: skip Dead; Acc[To] = Acc[To] + W[C]*Act[From]
+ *   for I in [num_input, n_units): Apply(Acc[I]); Acc[I] = 0
+ * `act` is the whole Activation array; for IPC_ERROR the result goes to
+ * err[I] (ErrorTag) and Activation is left alone, as in the iPC example.
+ * fwd_acc must hold n_units zeros on entry (the reference resets it after
+ * each Apply) and holds zeros again on return.
+ */
+void oracle_forward_pipeline(uint64_t n_conn, const uint32_t* from,
+                             const uint32_t* to, const uint8_t* dead,
+                             const float* w, float* act, uint64_t n_units,
+                             uint64_t num_input, int apply_kind,
+                             const float* value, float* err, float* fwd_acc) {
+  for (uint64_t c = 0; c < n_conn; ++c) {
+    if (dead && dead[c]) continue;
+    fwd_acc[to[c]] = fwd_acc[to[c]] + w[c] * act[from[c]];
+  }
+  for (uint64_t i = num_input; i < n_units; ++i) {
+    float v = apply_value(apply_kind, fwd_acc[i], value ? value[i] : 0.0f);
+    if (apply_kind == APPLY_IPC_ERROR) err[i] = v;
+    else act[i] = v;
+    fwd_acc[i] = 0.0f;
+  }
+}
+
+/*
+ * DoUpdateConnectionState (plastix.hpp:238-245) with the per-connection
+ * Hebbian trace rule used by the single-layer sweep workload:
+ *   UpdateIncomingConnection: E = decay*E + Act[From]*Act[To]; W += rate*E
+ */
+void oracle_update_hebbian_trace(uint64_t n_conn, const uint32_t* from,
+                                 const uint32_t* to, const uint8_t* dead,
+                                 const float* act, float* w, float* trace,
+                                 float decay, float rate) {
+  for (uint64_t c = 0; c < n_conn; ++c) {
+    if (dead && dead[c]) continue;
+    trace[c] = decay * trace[c] + act[from[c]] * act[to[c]];
+    w[c] += rate * trace[c];
+  }
+}
+
+/*
+ * DoUpdateConnectionState with the gradient rule of mlp_xor.cpp:51-56 and
+ * linear_regression.cpp:31-36 (kind 1: W -= rate*Post[To]*Act[From]) or the
+ * iPC Hebbian rule of ipc_multilayer.cpp:183-190 (kind 2:
+ * W += rate*Post[To]*Act[From]). Post is a per-unit array.
+ */
+void oracle_update_post(uint64_t n_conn, const uint32_t* from,
+                        const uint32_t* to, const uint8_t* dead,
+                        const float* act, const float* post, int kind,
+                        float rate, float* w) {
+  for (uint64_t c = 0; c < n_conn; ++c) {
+    if (dead && dead[c]) continue;
+    if (kind == 1) w[c] -= rate * post[to[c]] * act[from[c]];
+    else w[c] += rate * post[to[c]] * act[from[c]];
+  }
+}
+
+/*
+ * One sweep of the single-layer workload through DoStep in Pipeline mode:
+ * DoForwardPass (identity Apply) followed by the Hebbian trace update.
+ * act holds n_units entries; inputs are act[0, num_input).
+ */
+void oracle_step_hebbian(uint64_t n_conn, const uint32_t* from,
+                         const uint32_t* to, const uint8_t* dead, float* w,
+                         float* trace, float* act, uint64_t n_units,
+                         uint64_t num_input, float decay, float rate,
+                         float* fwd_acc) {
+  oracle_forward_pipeline(n_conn, from, to, dead, w, act, n_units, num_input,
+                          APPLY_IDENTITY, NULL, NULL, fwd_acc);
+  oracle_update_hebbian_trace(n_conn, from, to, dead, act, w, trace, decay,
+                              rate);
+}
+
+/* ---- permutation machinery (SOAAllocator::Gather, alloc.hpp:145-156) ---- */
+
+/* dst[i] = src[perm[i]] for i < n, elements of `elem` bytes. */
+void oracle_gather(const uint64_t* perm, uint64_t n, const void* src,
+                   void* dst, uint32_t elem) {
+  const unsigned char* s = (const unsigned char*)src;
+  unsigned char* d = (unsigned char*)dst;
+  for (uint64_t i = 0; i < n; ++i)
+    memcpy(d + i * elem, s + perm[i] * elem, elem);
+}
+
+/*
+ * Survivor permutation of DoPruneConnections' tombstones
+ * (plastix.hpp:280-297 marks Dead; no compaction exists in the reference):
+ * the increasing ids with keep[c] != 0. Returns the survivor count.
+ */
+uint64_t oracle_survivors(const uint8_t* keep, uint64_t n, uint64_t* perm) {
+  uint64_t m = 0;
+  for (uint64_t c = 0; c < n; ++c)
+    if (keep[c]) perm[m++] = c;
+  return m;
+}
+
+/*
+ * Stable sort permutation by 32-bit key (counting sort on 16-bit halves,
+ * LSD), the order std::stable_sort of ids by key produces. Used for the
+ * re-sort by ToId and for SortConnectionsByLevel's stable counting sort by
+ * SrcLevel (plastix.hpp:553-577).
+ */
+int oracle_stable_sort_u32(const uint32_t* key, uint64_t n, uint64_t* perm) {
+  uint64_t* tmp = (uint64_t*)malloc((n ? n : 1) * sizeof(uint64_t));
+  uint64_t* cnt = (uint64_t*)calloc(65537, sizeof(uint64_t));
+  if (!tmp || !cnt) {
+    free(tmp);
+    free(cnt);
+    return -1;
+  }
+  for (uint64_t i = 0; i < n; ++i) perm[i] = i;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int sh = 16 * pass;
+    memset(cnt, 0, 65537 * sizeof(uint64_t));
+    for (uint64_t i = 0; i < n; ++i) cnt[((key[perm[i]] >> sh) & 0xFFFF) + 1]++;
+    for (int b = 0; b < 65536; ++b) cnt[b + 1] += cnt[b];
+    for (uint64_t i = 0; i < n; ++i) {
+      uint32_t d = (key[perm[i]] >> sh) & 0xFFFF;
+      tmp[cnt[d]++] = perm[i];
+    }
+    memcpy(perm, tmp, n * sizeof(uint64_t));
+  }
+  free(tmp);
+  free(cnt);
+  return 0;
+}
+
+/*
+ * DoAddConnections phases 2-3 (plastix.hpp:411-432): sort the packed
+ * CompactEdge bits (From | To<<32) ascending and keep the first of each run
+ * of equal values. Sorts `bits` in place; returns the unique count written to
+ * `out`.
+ */
+static int cmp_u64(const void* a, const void* b) {
+  uint64_t x = *(const uint64_t*)a, y = *(const uint64_t*)b;
+  return x < y ? -1 : (x > y ? 1 : 0);
+}
+
+uint64_t oracle_sort_unique_u64(uint64_t* bits, uint64_t n, uint64_t* out) {
+  qsort(bits, n, sizeof(uint64_t), cmp_u64);
+  uint64_t m = 0, prev = UINT64_MAX;
+  for (uint64_t i = 0; i < n; ++i) {
+    if (bits[i] == prev) continue;
+    prev = bits[i];
+    out[m++] = bits[i];
+  }
+  return m;
+}

@@ -1,0 +1,171 @@
+// ref_harness.cpp — drives the REFERENCE implementation (its own headers,
+// compiled from the reference tree by oracle/build_ref.py) on arrays handed
+// over from Python, so the oracle restatement and the CPU baseline can be
+// checked against the reference itself.
+//
+// TEST INFRASTRUCTURE ONLY (oracle side). Networks are built through the
+// reference's LayerBuilder extension point (include/plastix/layers.hpp:48-51)
+// and stepped with the reference's unmodified Network::Do* loops. The only
+// change to the reference sources is made by the build recipe: the fixed
+// allocator capacities of include/plastix/plastix.hpp:82 become the two
+// functions below, so the BASELINE-size networks fit.
+#include <cstddef>
+#include <cstdint>
+
+static std::size_t g_unit_cap = 4096;
+static std::size_t g_conn_cap = 4096 * 4;
+std::size_t plx_ref_unit_capacity() { return g_unit_cap; }
+std::size_t plx_ref_conn_capacity() { return g_conn_cap; }
+
+#include <plastix/plastix.hpp>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <span>
+#include <thread>
+#include <vector>
+
+namespace {
+
+struct TraceTag {};
+
+float g_decay = 0.9f;
+float g_rate = 1e-3f;
+
+// The single-layer sweep workload's rule: trace decay + Hebbian product.
+struct HebbianTraceConn {
+  static void UpdateIncomingConnection(auto &U, size_t DstId, size_t SrcId,
+                                       auto &C, size_t ConnId, auto &) {
+    float &E = plastix::GetField<TraceTag>(C, ConnId);
+    E = g_decay * E +
+        plastix::GetActivation(U, SrcId) * plastix::GetActivation(U, DstId);
+    plastix::GetWeight(C, ConnId) += g_rate * E;
+  }
+  static void UpdateOutgoingConnection(auto &, size_t, size_t, auto &, size_t,
+                                       auto &) {}
+};
+
+struct SweepTraits : plastix::DefaultNetworkTraits<> {
+  using UpdateConn = HebbianTraceConn;
+  using ExtraConnFields =
+      plastix::ConnFieldList<plastix::alloc::SOAField<plastix::WeightTag, float>,
+                             plastix::alloc::SOAField<TraceTag, float>>;
+  static constexpr plastix::Propagation Model = plastix::Propagation::Pipeline;
+};
+using SweepNet = plastix::Network<SweepTraits>;
+
+// Builds one layer of `num_dst` units fed by an explicit connection list
+// (ToId values are absolute unit ids).
+struct EdgeListLayer {
+  size_t NumDst;
+  const uint32_t *From;
+  const uint32_t *To;
+  const float *W;
+  const float *Trace;
+  uint64_t N;
+  uint32_t ToOffset;  // subtracted from To (shards renumber their rows)
+
+  template <typename UA, typename CA>
+  plastix::UnitRange operator()(UA &U, CA &C, plastix::UnitRange Prev) const {
+    uint16_t NewLevel = plastix::GetLevel(U, Prev.Begin) + 1;
+    plastix::UnitRange Units = U.AllocateMany(NumDst);
+    for (auto Id : Units.Ids()) plastix::GetLevel(U, Id) = NewLevel;
+    for (uint64_t I = 0; I < N; ++I) {
+      auto Id = C.Allocate();
+      plastix::GetField<plastix::ToIdTag>(C, Id) = To[I] - ToOffset;
+      plastix::GetField<plastix::FromIdTag>(C, Id) = From[I];
+      plastix::GetField<plastix::SrcLevelTag>(C, Id) = 0;
+      plastix::GetWeight(C, Id) = W[I];
+      if constexpr (requires { plastix::GetField<TraceTag>(C, Id); })
+        plastix::GetField<TraceTag>(C, Id) = Trace ? Trace[I] : 0.0f;
+    }
+    return Units;
+  }
+};
+
+struct SweepShard {
+  std::unique_ptr<SweepNet> Net;
+  size_t NumSrc;
+};
+
+}  // namespace
+
+extern "C" {
+
+const char *ref_version() { return plastix::version(); }
+
+// Runs `sweeps` DoStep calls of the single-layer workload. Connections must be
+// given in the order the reference should hold them. Outputs: final weights,
+// traces and the destination activations.
+int ref_sweep_run(uint64_t n_src, uint64_t n_dst, uint64_t n_conn,
+                  const uint32_t *from, const uint32_t *to, const float *w0,
+                  const float *trace0, const float *act_in, int sweeps,
+                  float decay, float rate, float *w_out, float *trace_out,
+                  float *act_out) {
+  g_decay = decay;
+  g_rate = rate;
+  g_unit_cap = n_src + n_dst + 1;
+  g_conn_cap = n_conn + 1;
+  SweepNet Net(n_src, EdgeListLayer{n_dst, from, to, w0, trace0, n_conn, 0});
+  for (int S = 0; S < sweeps; ++S)
+    Net.DoStep(std::span<const float>(act_in, n_src));
+  auto &CA = Net.GetConnAlloc();
+  auto &UA = Net.GetUnitAlloc();
+  if (CA.Size() != n_conn) return -1;
+  for (uint64_t C = 0; C < n_conn; ++C) {
+    w_out[C] = plastix::GetWeight(CA, C);
+    trace_out[C] = plastix::GetField<TraceTag>(CA, C);
+  }
+  for (uint64_t I = 0; I < n_dst; ++I)
+    act_out[I] = plastix::GetActivation(UA, n_src + I);
+  return 0;
+}
+
+// CPU baseline: `n_threads` independent reference networks, each owning a
+// contiguous range of destination rows (the connections are dst-sorted, so a
+// shard is a contiguous connection range). Returns an opaque handle.
+void *ref_sweep_shards_create(uint64_t n_src, uint64_t n_dst, uint64_t n_conn,
+                              const uint32_t *from, const uint32_t *to,
+                              const float *w0, int n_threads, float decay,
+                              float rate) {
+  g_decay = decay;
+  g_rate = rate;
+  auto *Shards = new std::vector<SweepShard>();
+  uint64_t Begin = 0;
+  for (int T = 0; T < n_threads; ++T) {
+    uint64_t RowEnd = n_dst * (uint64_t)(T + 1) / (uint64_t)n_threads;
+    uint32_t RowBegin = (uint32_t)(n_dst * (uint64_t)T / (uint64_t)n_threads);
+    uint64_t End = Begin;
+    while (End < n_conn && to[End] < n_src + RowEnd) ++End;
+    g_unit_cap = n_src + (RowEnd - RowBegin) + 1;
+    g_conn_cap = (End - Begin) + 1;
+    SweepShard Sh;
+    Sh.NumSrc = n_src;
+    Sh.Net = std::make_unique<SweepNet>(
+        n_src, EdgeListLayer{RowEnd - RowBegin, from + Begin, to + Begin,
+                             w0 + Begin, nullptr, End - Begin, RowBegin});
+    Shards->push_back(std::move(Sh));
+    Begin = End;
+  }
+  return Shards;
+}
+
+// One DoStep on every shard, shards in parallel threads.
+void ref_sweep_shards_step(void *handle, const float *act_in) {
+  auto *Shards = static_cast<std::vector<SweepShard> *>(handle);
+  std::vector<std::thread> Threads;
+  for (auto &Sh : *Shards)
+    Threads.emplace_back([&Sh, act_in] {
+      Sh.Net->DoStep(std::span<const float>(act_in, Sh.NumSrc));
+    });
+  for (auto &T : Threads) T.join();
+}
+
+// The reference allocators never unmap their arenas (alloc.hpp has no
+// destructor); the shards are released but their arenas stay mapped.
+void ref_sweep_shards_destroy(void *handle) {
+  delete static_cast<std::vector<SweepShard> *>(handle);
+}
+
+}  // extern "C"

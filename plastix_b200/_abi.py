@@ -1,0 +1,97 @@
+"""ctypes bindings of ``libplastix_b200.so`` (declared in include/plastix_b200.h).
+
+The library is the product: there is no Python or CPU fallback. Loading
+fails with an ImportError-style exception when the shared library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libplastix_b200.so")
+
+PLX_OK = 0
+PLX_ERR_ARG = 1
+PLX_ERR_CUDA = 2
+PLX_ERR_CAPACITY = 3
+PLX_ERR_TIMEOUT = 4
+PLX_ERR_UNSUPPORTED = 5
+
+APPLY_IDENTITY = 0
+APPLY_SIGMOID = 1
+APPLY_TANH = 2
+APPLY_IPC_ERROR = 3
+
+UPDATE_GRADIENT = 1
+UPDATE_HEBBIAN = 2
+
+SEQ_ROW_MAX = 256
+
+
+class PlxError(RuntimeError):
+    def __init__(self, code: int, where: str, message: str):
+        super().__init__(f"{where} failed with status {code}: {message}")
+        self.code = code
+
+
+class Csr(ctypes.Structure):
+    _fields_ = [("row_ptr", c_void_p), ("plan", c_void_p), ("n_edges", c_uint64),
+                ("n_rows", c_uint32), ("n_long", c_uint32)]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "plx_version": (c_char_p, []),
+    "plx_last_error": (c_char_p, []),
+    "plx_ctx_create": (c_int, [c_int, c_void_p, POINTER(c_void_p)]),
+    "plx_ctx_destroy": (c_int, [c_void_p]),
+    "plx_ctx_set_stream": (c_int, [c_void_p, c_void_p]),
+    "plx_ctx_set_timeout_ns": (c_int, [c_void_p, c_uint64]),
+    "plx_ctx_num_sms": (c_int, [c_void_p, POINTER(c_int)]),
+    "plx_ctx_sync": (c_int, [c_void_p]),
+    "plx_csr_row_ptr": (c_int, [c_void_p, c_void_p, c_uint64, c_uint32, c_uint32, c_void_p]),
+    "plx_csr_plan_words": (c_uint64, [c_uint64, c_uint32]),
+    "plx_csr_plan": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p, c_uint64,
+                             POINTER(c_uint32)]),
+    "plx_sweep_forward": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_uint32, c_int, c_void_p, c_void_p, c_void_p]),
+    "plx_sweep_forward_hebbian": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p,
+                                          c_void_p, c_uint32, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_float, c_float, c_void_p]),
+    "plx_sweep_update": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p, c_void_p,
+                                 c_uint32, c_void_p, c_int, c_float, c_void_p, c_void_p]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loads it on first use)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m plastix_b200.build` "
+                "(there is no CPU fallback)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def check(code: int, where: str) -> None:
+    if code != PLX_OK:
+        msg = lib().plx_last_error().decode(errors="replace")
+        raise PlxError(code, where, msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)

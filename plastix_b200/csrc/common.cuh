@@ -1,0 +1,170 @@
+// Shared device helpers for the sm_100a kernels: error plumbing, the
+// mbarrier / bulk-copy (TMA, non-tensor) primitives used by the streaming
+// sweeps, and bounded waits that record a status instead of hanging.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/plastix_b200.h"
+
+namespace plx {
+
+// ---------------------------------------------------------------------------
+// Host-side error reporting (thread-local message, int status codes).
+// ---------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+
+#define PLX_TRY_CUDA(expr)                                                     \
+  do {                                                                         \
+    cudaError_t plx_e_ = (expr);                                               \
+    if (plx_e_ != cudaSuccess) return ::plx::check_cuda(plx_e_, #expr);        \
+  } while (0)
+
+#define PLX_CHECK_ARG(cond, ...)                                               \
+  do {                                                                         \
+    if (!(cond)) return ::plx::set_error(PLX_ERR_ARG, __VA_ARGS__);            \
+  } while (0)
+
+#define PLX_LAUNCH_CHECK(what)                                                 \
+  do {                                                                         \
+    cudaError_t plx_e_ = cudaGetLastError();                                   \
+    if (plx_e_ != cudaSuccess) return ::plx::check_cuda(plx_e_, what);         \
+  } while (0)
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Device status word values (written by kernels whose waits time out).
+enum DeviceStatus : int32_t {
+  kStatusOk = 0,
+  kStatusTimeout = 1,   // a bounded wait expired
+  kStatusBadIndex = 2,  // a connection named a unit outside the given array
+  kStatusBadPlan = 3,   // a sweep was given an invalid plan
+};
+
+// ---------------------------------------------------------------------------
+// Device primitives
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(count)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async (bulk copy) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+          smem_addr(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the given phase parity, giving up after `timeout_ns` of wall
+// time. Returns false on timeout (the caller records the status and skips the
+// work that depended on the data).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
+                                                  uint32_t parity,
+                                                  uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 63u) == 63u && global_timer_ns() - t0 > timeout_ns)
+      return false;
+  }
+}
+
+// Bulk (non-tensor) asynchronous copy global -> shared, completion signalled
+// on `bar` through the transaction count. dst, src and bytes must be 16-byte
+// multiples / aligned.
+__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src_gmem,
+                                          uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem_addr(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Bulk asynchronous copy shared -> global (bulk-group completion).
+__device__ __forceinline__ void bulk_store(void* dst_gmem, const void* src_smem,
+                                           uint32_t bytes) {
+  asm volatile(
+      "cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+          dst_gmem),
+      "r"(smem_addr(src_smem)), "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before subsequent
+// async-proxy (bulk store) reads of the same shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void record_status(int32_t* status, int32_t code) {
+  if (status) atomicCAS(status, kStatusOk, code);
+}
+
+template <typename T>
+__device__ __forceinline__ T ldg_nc(const T* p) {
+  return __ldg(p);
+}
+
+}  // namespace plx
+
+// Opaque context: one device, one stream, a device status word.
+struct plx_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 0;
+  int32_t* d_status = nullptr;  // device word written by bounded waits
+  uint64_t timeout_ns = 2000000000ull;
+};

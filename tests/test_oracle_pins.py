@@ -1,0 +1,107 @@
+"""Pins the oracle restatement: against the reference's own tests' known
+answers, the committed golden fixtures (made by the reference itself), and --
+where it was built here -- the reference compiled from its sources."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from plastix_b200 import workloads
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def fc_edges(layers):
+    """Connections of FullyConnected builders in reference order
+    (include/plastix/layers.hpp:56-76: dst-major, src-inner)."""
+    frm, to = [], []
+    begin, size = 0, layers[0]
+    nxt = size
+    for n in layers[1:]:
+        for u in range(nxt, nxt + n):
+            for s in range(begin, begin + size):
+                frm.append(s)
+                to.append(u)
+        begin, size = nxt, n
+        nxt += n
+    return np.array(frm, np.uint32), np.array(to, np.uint32), nxt
+
+
+def test_forward_identity_known_answer(orc):
+    # reference tests/test_plastix.cpp:127-141 (ForwardPassIdentity)
+    f, t, n = fc_edges([2, 1])
+    act = np.zeros(n, np.float32)
+    act[:2] = [3.0, 5.0]
+    out, _ = orc.forward_pipeline(f, t, np.ones(f.size, np.float32), act, 2)
+    assert out[2] == 8.0 and out[0] == 3.0 and out[1] == 5.0
+
+
+def test_pipeline_multilayer_known_answer(orc):
+    # reference tests/test_plastix_pipeline.cpp:249-267
+    f, t, n = fc_edges([2, 2, 1])
+    act = np.zeros(n, np.float32)
+    act[:2] = 1.0
+    w = np.ones(f.size, np.float32)
+    act, _ = orc.forward_pipeline(f, t, w, act, 2)
+    assert list(act[2:]) == [2.0, 2.0, 0.0]
+    act, _ = orc.forward_pipeline(f, t, w, act, 2)
+    assert act[4] == 4.0
+
+
+def test_three_layer_pipeline_known_answer(orc):
+    # reference tests/test_plastix_pipeline.cpp:269-283
+    f, t, n = fc_edges([3, 2, 2, 1])
+    act = np.zeros(n, np.float32)
+    act[:3] = 1.0
+    w = np.ones(f.size, np.float32)
+    outs = []
+    for _ in range(3):
+        act, _ = orc.forward_pipeline(f, t, w, act, 3)
+        outs.append(act[-1])
+    assert outs == [0.0, 0.0, 12.0]
+
+
+def test_gather_known_answer(orc):
+    # reference tests/test_alloc.cpp:51-83: Gather applies a permutation
+    perm = np.array([3, 1, 2, 0], np.uint64)
+    assert list(orc.gather(perm, np.array([0, 10, 20, 30], np.int32))) == [30, 10, 20, 0]
+
+
+def test_sort_unique_matches_reference_dedup(orc):
+    # plastix.hpp:411-432; reference tests/test_plastix.cpp:1112-1127
+    bits = np.array([5, 3, 5, 1, 3, 3], np.uint64)
+    assert list(orc.sort_unique_u64(bits)) == [1, 3, 5]
+
+
+def test_stable_sort_is_stable(orc):
+    keys = np.array([2, 1, 2, 0, 1, 70000, 0], np.uint32)
+    perm = orc.stable_sort_perm_u32(keys)
+    assert list(perm) == list(np.argsort(keys, kind="stable"))
+
+
+def test_golden_sweep_fixture(orc):
+    fx = np.load(GOLDEN / "sweep_hebbian_small.npz")
+    L = workloads.sparse_layer(int(fx["n_src"]), int(fx["n_dst"]), int(fx["n_edges"]),
+                               seed=int(fx["seed"]))
+    act = np.concatenate([L.act_in, np.zeros(L.n_dst, np.float32)])
+    w, e, a = orc.step_hebbian(L.from_id, L.to_id, L.weight, L.trace, act, L.n_src,
+                               float(fx["decay"]), float(fx["rate"]),
+                               sweeps=int(fx["sweeps"]))
+    np.testing.assert_array_equal(w, fx["w"])
+    np.testing.assert_array_equal(e, fx["trace"])
+    np.testing.assert_array_equal(a[L.n_src:], fx["act"])
+
+
+@pytest.mark.parametrize("seed,n_src,n_dst,n_edges", [(1, 64, 32, 500), (2, 1000, 300, 20000)])
+def test_oracle_matches_reference_build(orc, seed, n_src, n_dst, n_edges):
+    if orc.ref() is None:
+        pytest.skip("reference build not present (only built where the reference tree is)")
+    L = workloads.sparse_layer(n_src, n_dst, n_edges, seed=seed)
+    w_r, e_r, a_r = orc.ref_sweep_run(n_src, n_dst, L.from_id, L.to_id, L.weight,
+                                      L.trace, L.act_in, 5, 0.9, 1e-3)
+    act = np.concatenate([L.act_in, np.zeros(n_dst, np.float32)])
+    w, e, a = orc.step_hebbian(L.from_id, L.to_id, L.weight, L.trace, act, n_src, 0.9,
+                               1e-3, sweeps=5)
+    np.testing.assert_array_equal(w, w_r)
+    np.testing.assert_array_equal(e, e_r)
+    np.testing.assert_array_equal(a[n_src:], a_r)

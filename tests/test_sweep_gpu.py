@@ -1,0 +1,196 @@
+"""K1 parity: the sm_100a sweeps against the oracle on the same seeded inputs.
+
+Bit-exact where the reference order is reproduced (rows of up to
+PLX_SEQ_ROW_MAX connections, identity/IPC Apply, all per-connection updates);
+rtol 1e-5 (atol 1e-6) where the device uses a different but deterministic
+reduction order (longer rows) or CUDA's expf/tanhf (sigmoid/tanh Apply).
+"""
+import numpy as np
+import pytest
+import torch
+
+from plastix_b200 import _abi, workloads
+from plastix_b200.runtime import (DstCsr, HebbianSweepLayer, sweep_forward,
+                                  sweep_update)
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def ids(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.uint32).view(np.int32)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def run_hebbian(ctx, L, sweeps, decay=0.9, rate=1e-3, dead=None):
+    layer = HebbianSweepLayer(ctx, L.n_src, L.n_dst, ids(L.from_id), ids(L.to_id),
+                              dev(L.weight), dev(L.trace), decay=decay, rate=rate,
+                              dead=None if dead is None else dev(dead))
+    act = dev(L.act_in)
+    for _ in range(sweeps):
+        out = layer.step(act)
+    ctx.sync()
+    return host(layer.weight), host(layer.trace), host(out)
+
+
+def oracle_hebbian(orc, L, sweeps, decay=0.9, rate=1e-3, dead=None):
+    act = np.concatenate([L.act_in, np.zeros(L.n_dst, np.float32)])
+    w, e, a = orc.step_hebbian(L.from_id, L.to_id, L.weight, L.trace, act, L.n_src,
+                               decay, rate, sweeps=sweeps, dead=dead)
+    return w, e, a[L.n_src:]
+
+
+@pytest.mark.parametrize("n_src,n_dst,n_edges,seed", [
+    (1000, 200, 12345, 1),        # ragged tail, several tiles
+    (4096, 4096, 2048 * 3, 2),    # exact tile multiple
+    (50000, 20000, 300001, 3),    # many tiles, short rows
+    (8, 3, 7, 4),                 # fewer edges than one bulk vector
+    (1 << 14, 1 << 10, 1 << 16, 5),
+])
+def test_fused_hebbian_bit_exact(ctx, orc, n_src, n_dst, n_edges, seed):
+    L = workloads.sparse_layer(n_src, n_dst, n_edges, seed=seed)
+    got = run_hebbian(ctx, L, sweeps=4)
+    want = oracle_hebbian(orc, L, sweeps=4)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+
+
+def test_fused_hebbian_golden_fixture(ctx):
+    from pathlib import Path
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "sweep_hebbian_small.npz")
+    L = workloads.sparse_layer(int(fx["n_src"]), int(fx["n_dst"]), int(fx["n_edges"]),
+                               seed=int(fx["seed"]))
+    w, e, a = run_hebbian(ctx, L, int(fx["sweeps"]), float(fx["decay"]), float(fx["rate"]))
+    np.testing.assert_array_equal(w, fx["w"])
+    np.testing.assert_array_equal(e, fx["trace"])
+    np.testing.assert_array_equal(a, fx["act"])
+
+
+def test_fused_hebbian_dead_connections(ctx, orc):
+    L = workloads.sparse_layer(3000, 500, 40000, seed=11)
+    dead = (np.random.default_rng(3).random(L.from_id.size) < 0.2).astype(np.uint8)
+    got = run_hebbian(ctx, L, 3, dead=dead)
+    want = oracle_hebbian(orc, L, 3, dead=dead)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+
+
+@pytest.mark.parametrize("lens", [
+    [0, 0, 5, 0, 3000, 0, 1, 2047, 2048, 2049, 0],   # wide + long rows, empty rows
+    [257] * 40 + [256] * 40,                          # warp rows vs thread rows
+    [10000],                                          # one long row (many tiles)
+    [0] * 100,                                        # no connections at all
+    [1] * 5000 + [4100] + [3] * 700,                  # long row amid short rows
+])
+def test_row_shapes(ctx, orc, lens):
+    L = workloads.sparse_layer_rows(777, lens, seed=len(lens))
+    got = run_hebbian(ctx, L, 2)
+    want = oracle_hebbian(orc, L, 2)
+    exact = max(lens) <= _abi.SEQ_ROW_MAX
+    for g, w in zip(got, want):
+        if exact:
+            np.testing.assert_array_equal(g, w)
+        else:
+            np.testing.assert_allclose(g, w, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("apply", [_abi.APPLY_IDENTITY, _abi.APPLY_SIGMOID,
+                                   _abi.APPLY_TANH, _abi.APPLY_IPC_ERROR])
+@pytest.mark.parametrize("with_dead", [False, True])
+def test_forward_apply_kinds(ctx, orc, apply, with_dead):
+    L = workloads.sparse_layer_rows(5000, list(np.random.default_rng(9).integers(0, 300, 900)),
+                                    seed=21)
+    dead = (np.random.default_rng(4).random(L.from_id.size) < 0.1).astype(np.uint8) \
+        if with_dead else None
+    value = np.random.default_rng(5).random(L.n_dst, dtype=np.float32)
+    csr = DstCsr(ctx, ids(L.to_id), L.n_src, L.n_dst)
+    act_src = dev(L.act_in)
+    act_dst = torch.zeros(L.n_dst, device="cuda")
+    err = torch.zeros(L.n_dst, device="cuda")
+    sweep_forward(ctx, csr, ids(L.from_id), dev(L.weight), act_src, act_dst, apply=apply,
+                  dead=None if dead is None else dev(dead), value=dev(value), err_out=err)
+    ctx.sync()
+    act = np.concatenate([L.act_in, np.zeros(L.n_dst, np.float32)])
+    full_value = np.concatenate([np.zeros(L.n_src, np.float32), value])
+    want_act, want_err = orc.forward_pipeline(L.from_id, L.to_id, L.weight, act, L.n_src,
+                                              apply=apply, dead=dead, value=full_value)
+    got = host(err) if apply == _abi.APPLY_IPC_ERROR else host(act_dst)
+    want = want_err[L.n_src:] if apply == _abi.APPLY_IPC_ERROR else want_act[L.n_src:]
+    if apply in (_abi.APPLY_IDENTITY, _abi.APPLY_IPC_ERROR):
+        np.testing.assert_array_equal(got, want)
+    else:
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("kind", [_abi.UPDATE_GRADIENT, _abi.UPDATE_HEBBIAN])
+def test_update_kinds(ctx, orc, kind):
+    L = workloads.sparse_layer_rows(3000, list(np.random.default_rng(2).integers(0, 600, 700)),
+                                    seed=8)
+    post = np.random.default_rng(6).normal(size=L.n_dst).astype(np.float32)
+    csr = DstCsr(ctx, ids(L.to_id), L.n_src, L.n_dst)
+    w = dev(L.weight)
+    sweep_update(ctx, csr, ids(L.from_id), dev(L.act_in), dev(post), w, w, kind=kind,
+                 rate=0.5)
+    ctx.sync()
+    full_post = np.concatenate([np.zeros(L.n_src, np.float32), post])
+    want = orc.update_post(L.from_id, L.to_id, L.act_in, full_post, L.weight, kind, 0.5)
+    np.testing.assert_array_equal(host(w), want)
+
+
+def test_pipeline_multilayer_known_answer(ctx):
+    # reference tests/test_plastix_pipeline.cpp:249-267, all rows in one sweep:
+    # 2 inputs -> 2 hidden -> 1 output, weights 1, Pipeline (snapshot) semantics.
+    frm = np.array([0, 1, 0, 1, 2, 3], np.uint32)
+    to = np.array([2, 2, 3, 3, 4, 4], np.uint32)
+    csr = DstCsr(ctx, ids(to), 2, 3)
+    act = torch.tensor([1.0, 1.0, 0.0, 0.0, 0.0], device="cuda")
+    w = torch.ones(6, device="cuda")
+    for expect in ([2.0, 2.0, 0.0], [2.0, 2.0, 4.0]):
+        snapshot = act.clone()
+        sweep_forward(ctx, csr, ids(frm), w, snapshot, act[2:])
+        ctx.sync()
+        assert host(act[2:]).tolist() == expect
+
+
+def test_out_of_range_source_is_reported(ctx):
+    frm = np.array([0, 1, 99], np.uint32)
+    to = np.array([2, 2, 2], np.uint32)
+    csr = DstCsr(ctx, ids(to), 2, 1)
+    act = torch.ones(3, device="cuda")
+    out = torch.zeros(1, device="cuda")
+    sweep_forward(ctx, csr, ids(frm), torch.ones(3, device="cuda"), act, out)
+    with pytest.raises(_abi.PlxError) as e:
+        ctx.sync()
+    assert e.value.code == _abi.PLX_ERR_ARG
+    ctx.sync()  # status cleared
+
+
+def test_invalid_row_ptr_rejected(ctx):
+    with pytest.raises(_abi.PlxError):
+        DstCsr.from_row_ptr(ctx, torch.tensor([0, 5, 3, 6], dtype=torch.int32))
+
+
+def test_full_size_sweep_matches_oracle(ctx, orc):
+    """The 64M-connection single-layer workload, one fused sweep, compared
+    bit for bit with the oracle over the whole layer."""
+    n_src = n_dst = 1 << 20
+    n = 1 << 26
+    from_id, to_id, w, act = workloads.sparse_layer_device(n_src, n_dst, n, 1234, "cuda")
+    layer = HebbianSweepLayer(ctx, n_src, n_dst, from_id, to_id, w)
+    out = layer.step(act)
+    ctx.sync()
+    f, t = host(from_id).view(np.uint32), host(to_id).view(np.uint32)
+    a_full = np.concatenate([host(act), np.zeros(n_dst, np.float32)])
+    ww, ee, aa = orc.step_hebbian(f, t, host(w), np.zeros(n, np.float32), a_full, n_src,
+                                  0.9, 1e-3)
+    np.testing.assert_array_equal(host(out), aa[n_src:])
+    np.testing.assert_array_equal(host(layer.weight), ww)
+    np.testing.assert_array_equal(host(layer.trace), ee)
