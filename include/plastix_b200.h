@@ -39,7 +39,9 @@ extern "C" {
 
 /* Rows (destination units) with at most this many connections are summed
  * strictly left to right, exactly like the reference loop. Longer rows use a
- * fixed-shape deterministic reduction (32-connection chunks folded in order). */
+ * fixed deterministic order: 32 lane-strided partial sums (every 32nd
+ * connection) folded in lane order; rows over 2048 connections use 256
+ * thread-strided partial sums. */
 #define PLX_SEQ_ROW_MAX 256
 
 /* ---- library / context ------------------------------------------------- */
@@ -72,23 +74,26 @@ int plx_ctx_sync(plx_ctx* ctx);
 int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id, uint64_t n_edges,
                     uint32_t row_base, uint32_t n_rows, uint32_t* row_ptr);
 
-/* Size (in u32 words) of the sweep plan for n_edges connections. */
-uint64_t plx_csr_plan_words(uint64_t n_edges, uint32_t n_rows);
-/* Builds the tile plan (row ownership per edge tile, list of rows longer
- * than 2048 connections) used by every sweep over this row_ptr, validates
- * row_ptr, and reports the number of long rows in *n_long_out (for
- * plx_csr.n_long). Synchronises the stream. */
-int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
-                 uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
-                 uint32_t* n_long_out);
-
 typedef struct plx_csr {
   const uint32_t* row_ptr; /* n_rows + 1 entries, row_ptr[0] == 0          */
   const uint32_t* plan;    /* from plx_csr_plan                             */
   uint64_t n_edges;        /* == row_ptr[n_rows], < 2^32 - 2^16             */
   uint32_t n_rows;
-  uint32_t n_long;         /* value reported by plx_csr_plan               */
+  uint32_t n_wide;         /* rows with PLX_SEQ_ROW_MAX < length <= 2048    */
+  uint32_t n_long;         /* rows longer than 2048                         */
+  uint32_t n_short;        /* rows of at most PLX_SEQ_ROW_MAX (incl. empty) */
 } plx_csr;
+
+/* Size (in u32 words) of the sweep plan for n_edges connections. */
+uint64_t plx_csr_plan_words(uint64_t n_edges, uint32_t n_rows);
+
+/* Validates row_ptr, classifies the rows (short / wide / long) and builds the
+ * tile plan every sweep over this row_ptr uses. Fills *out (row_ptr, plan,
+ * sizes and row counts). row_ptr must be 16-byte aligned. Synchronises the
+ * stream. The plan stays valid while row_ptr is unchanged. */
+int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                 uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
+                 plx_csr* out);
 
 /* ---- forward sweep (Map / Combine / Apply) ----------------------------- */
 

@@ -37,7 +37,8 @@ class PlxError(RuntimeError):
 
 class Csr(ctypes.Structure):
     _fields_ = [("row_ptr", c_void_p), ("plan", c_void_p), ("n_edges", c_uint64),
-                ("n_rows", c_uint32), ("n_long", c_uint32)]
+                ("n_rows", c_uint32), ("n_wide", c_uint32), ("n_long", c_uint32),
+                ("n_short", c_uint32)]
 
 
 # name -> (restype, argtypes)
@@ -53,7 +54,7 @@ _SIGNATURES = {
     "plx_csr_row_ptr": (c_int, [c_void_p, c_void_p, c_uint64, c_uint32, c_uint32, c_void_p]),
     "plx_csr_plan_words": (c_uint64, [c_uint64, c_uint32]),
     "plx_csr_plan": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p, c_uint64,
-                             POINTER(c_uint32)]),
+                             c_void_p]),
     "plx_sweep_forward": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_uint32, c_int, c_void_p, c_void_p, c_void_p]),
     "plx_sweep_forward_hebbian": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p,

@@ -5,42 +5,63 @@
 //   DoForwardPass, one Topological level      :112-130
 //   DoUpdateConnectionState (incoming sweep)  :238-245
 //
-// Design (B200): persistent CTAs walk fixed edge tiles of S connections.
-// Thread 0 streams each tile's SoA slices (FromId, Weight, [Trace], [Dead])
-// into a ring of shared-memory stages with 1-D bulk copies (TMA engine,
-// mbarrier transaction counts), NSTAGE-2 tiles ahead of the compute. Per tile:
-//   A  edge-parallel gather act[FromId] into shared memory (L2-resident),
-//   B  per destination row, fold w*act strictly left to right (one thread per
-//      row; rows longer than PLX_SEQ_ROW_MAX use a warp and 33-edge chunks),
-//      run Apply, write the row output, broadcast the row value to its edges,
-//   C  edge-parallel per-connection update in shared memory,
-// and thread 0 bulk-stores the updated Weight/Trace slices.
-// A row that crosses a tile boundary is summed by every tile it touches (the
-// pieces outside the tile are re-read from global memory, which is why the
-// fused variant reads w_in and writes w_out); only the tile that holds the
-// row's first connection writes its output. Rows longer than 2048
-// connections are summed beforehand by k_long_rows.
+// Design (B200):
+// * Rows (destination units) are classified once per connectivity by
+//   plx_csr_plan: short rows (<= PLX_SEQ_ROW_MAX connections), wide rows
+//   (<= 2048) and long rows.
+// * Short rows are swept by k_sweep, a persistent warp-specialised kernel
+//   over fixed edge tiles of S connections. A producer warp streams each
+//   tile's SoA slices (FromId, Weight, [Trace], [Dead]) and the tile's slice
+//   of row_ptr into a ring of shared-memory stages with 1-D bulk copies (TMA
+//   engine, mbarrier transaction counts). Consumer warps then
+//     A  gather act[FromId] (L2-resident) into shared memory, plus the
+//        pieces of the two boundary rows that lie outside the tile (halo),
+//     B  fold w*act of each short row strictly left to right (one thread per
+//        row: bit-exact with the reference), run Apply, write the row output
+//        and broadcast the row value to the row's connections,
+//     C  apply the per-connection update in shared memory,
+//   and bulk-store the updated Weight/Trace slices. A row crossing a tile
+//   boundary is summed by both tiles from the halo; only the tile holding
+//   its first connection writes its output, each tile updates its own part.
+//   Because of that re-read, the fused variant reads w_in and writes w_out.
+// * Wide rows are summed by k_wide_rows (one warp per row, coalesced
+//   lane-strided fold, deterministic) and long rows by k_long_rows (one CTA
+//   per row) before k_sweep; k_sweep then only updates their connections.
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 
 namespace plx {
 
-constexpr uint32_t kPlanG = 256;        // plan granularity (edges per block)
-constexpr uint32_t kLongRow = 2048;     // rows longer than this: k_long_rows
-constexpr uint32_t kWideChunk = 33;     // chunk length of the warp fold
-constexpr uint32_t kMaxWideChunks = 64; // ceil(2048 / 33) <= 64
-constexpr uint32_t kPlanMagic = 0x504C4E31u;  // "PLN1"
+constexpr uint32_t kPlanG = 256;                // plan granularity (edges)
+constexpr uint32_t kSeqMax = PLX_SEQ_ROW_MAX;   // short-row limit
+constexpr uint32_t kLongRow = 2048;             // wide-row limit
+constexpr uint32_t kHalo = kSeqMax;             // max out-of-tile piece of a short row
+constexpr uint32_t kPlanMagic = 0x504C4E32u;    // "PLN2"
+constexpr uint32_t kPlanHdr = 8;
 
-// plan layout (u32 words):
-//   [0] magic (0 when row_ptr failed validation)  [1] n_blocks  [2] n_long
-//   [3 .. 3+n_blocks]  first row whose start >= b*kPlanG (last = n_rows)
-//   [4+n_blocks ..]    ids of rows longer than kLongRow
+// Plan layout (u32 words):
+//   [0] magic (0 when row_ptr failed validation)  [1] n_blocks
+//   [2] n_wide  [3] n_long  [4] n_short  [5] max_wide  [6] max_long
+//   [8 + 3b + 0]  first row f whose start >= b*kPlanG (b = n_blocks: n_rows)
+//   [8 + 3b + 1]  row_ptr[f-1]: start of the last row starting before b*kPlanG
+//   [8 + 3b + 2]  row_ptr[f]:   its end (0 and 0 when f == 0)
+//   for b in [0, n_blocks]; then max_wide wide-row ids, then max_long
+//   long-row ids.
 __host__ __device__ inline uint64_t plan_blocks(uint64_t n_edges) {
   uint64_t b = (n_edges + kPlanG - 1) / kPlanG;
   return b ? b : 1;
 }
-
+__host__ __device__ inline uint64_t plan_max_wide(uint64_t n_edges) {
+  return n_edges / (kSeqMax + 1) + 1;
+}
+__host__ __device__ inline uint64_t plan_max_long(uint64_t n_edges) {
+  return n_edges / (kLongRow + 1) + 1;
+}
+__host__ __device__ inline uint64_t plan_wide_off(uint64_t nb) {
+  return kPlanHdr + 3 * (nb + 1);
+}
 __host__ __device__ inline uint64_t min_u64(uint64_t x, uint64_t y) {
   return x < y ? x : y;
 }
@@ -98,42 +119,61 @@ __global__ void k_plan_blocks(const uint32_t* __restrict__ row_ptr,
   const uint64_t nb = plan_blocks(n_edges);
   uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
   if (b > nb) return;
-  if (b == nb) {
-    plan[3 + b] = n_rows;
-    return;
+  uint32_t lo = n_rows;
+  if (b < nb) {
+    const uint64_t key = b * kPlanG;
+    lo = 0;
+    uint32_t hi = n_rows;  // first row r in [0, n_rows] with start >= key
+    while (lo < hi) {
+      uint32_t mid = (lo + hi) >> 1;
+      if ((uint64_t)__ldg(row_ptr + mid) < key) lo = mid + 1;
+      else hi = mid;
+    }
   }
-  const uint64_t key = b * kPlanG;
-  uint32_t lo = 0, hi = n_rows;  // first row r in [0, n_rows] with start >= key
-  while (lo < hi) {
-    uint32_t mid = (lo + hi) >> 1;
-    if ((uint64_t)__ldg(row_ptr + mid) < key) lo = mid + 1;
-    else hi = mid;
-  }
-  plan[3 + b] = lo;
+  uint32_t* e = plan + kPlanHdr + 3 * b;
+  e[0] = lo;
+  e[1] = lo ? row_ptr[lo - 1] : 0u;
+  e[2] = lo ? row_ptr[lo] : 0u;
 }
 
-// Validates row_ptr (monotone, row_ptr[0]==0, row_ptr[n_rows]==n_edges) and
-// lists the long rows. Any violation clears the magic word so that every
-// sweep using this plan stops and reports a bad-plan status.
+// Validates row_ptr (monotone, row_ptr[0]==0, row_ptr[n_rows]==n_edges),
+// counts short rows and lists wide and long rows (list order is irrelevant:
+// each row is reduced independently). Any violation clears the magic word so
+// every sweep using this plan stops and reports a bad-plan status.
 __global__ void k_plan_rows(const uint32_t* __restrict__ row_ptr,
                             uint32_t n_rows, uint64_t n_edges,
-                            uint32_t* __restrict__ plan, uint64_t max_long) {
+                            uint32_t* __restrict__ plan) {
   const uint64_t nb = plan_blocks(n_edges);
+  const uint64_t max_wide = plan_max_wide(n_edges);
+  const uint64_t max_long = plan_max_long(n_edges);
+  uint32_t* wide = plan + plan_wide_off(nb);
+  uint32_t* lng = wide + max_wide;
   uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
   if (r == 0) {
     if (row_ptr[0] != 0 || row_ptr[n_rows] != (uint32_t)n_edges) plan[0] = 0;
   }
-  if (r >= n_rows) return;
-  const uint32_t a = row_ptr[r], b = row_ptr[r + 1];
-  if (b < a || b > n_edges) {
-    plan[0] = 0;
-    return;
+  bool is_short = false;
+  if (r < n_rows) {
+    const uint32_t a = row_ptr[r], b = row_ptr[r + 1];
+    if (b < a || b > n_edges) {
+      plan[0] = 0;
+    } else {
+      const uint32_t len = b - a;
+      if (len <= kSeqMax) {
+        is_short = true;
+      } else if (len <= kLongRow) {
+        uint32_t slot = atomicAdd(&plan[2], 1u);
+        if (slot < max_wide) wide[slot] = (uint32_t)r;
+        else plan[0] = 0;
+      } else {
+        uint32_t slot = atomicAdd(&plan[3], 1u);
+        if (slot < max_long) lng[slot] = (uint32_t)r;
+        else plan[0] = 0;
+      }
+    }
   }
-  if (b - a > kLongRow) {
-    uint32_t slot = atomicAdd(&plan[2], 1u);
-    if (slot < max_long) plan[4 + nb + slot] = (uint32_t)r;
-    else plan[0] = 0;
-  }
+  const uint32_t m = __ballot_sync(0xffffffffu, is_short);
+  if ((threadIdx.x & 31) == 0 && m) atomicAdd(&plan[4], (uint32_t)__popc(m));
 }
 
 // ---------------------------------------------------------------------------
@@ -166,41 +206,83 @@ __device__ __forceinline__ float stored_post(uint32_t r, const SweepArgs& a) {
   else return a.act_dst[r];
 }
 
-__device__ __forceinline__ float gather_act(const SweepArgs& a, uint32_t s) {
-  if (s >= a.act_src_len) {
-    record_status(a.status, kStatusBadIndex);
-    return 0.0f;
-  }
-  return __ldg(a.act_src + s);
+// Gathers act[s]; an out-of-range id reads 0 and sets `bad`.
+__device__ __forceinline__ float gather_act(const SweepArgs& a, uint32_t s,
+                                            bool& bad) {
+  const bool ok = s < a.act_src_len;
+  bad |= !ok;
+  return ok ? __ldg(a.act_src + s) : 0.0f;
 }
 
-// Product of one connection read straight from global memory (pieces of a
-// row outside the current tile).
+// w*act of connection k read straight from global memory.
 template <bool DEAD>
-__device__ __forceinline__ float global_term(const SweepArgs& a, uint32_t k) {
+__device__ __forceinline__ float global_term(const SweepArgs& a, uint32_t k,
+                                             bool& bad) {
+  const float w = __ldg(a.w_in + k);
+  const uint32_t s = __ldg(a.src + k);
+  const float p = __fmul_rn(w, gather_act(a, s, bad));
   if constexpr (DEAD) {
     if (__ldg(a.dead + k)) return 0.0f;
   }
-  return __fmul_rn(__ldg(a.w_in + k), gather_act(a, __ldg(a.src + k)));
+  return p;
 }
 
 // ---------------------------------------------------------------------------
-// Long rows (> kLongRow): one CTA per row, deterministic order: thread t folds
-// connections t, t+NT, ... then thread 0 folds the NT partials in order.
+// Wide rows (kSeqMax < len <= kLongRow): one warp per row. Order: lane l folds
+// connections rs+l, rs+l+32, ... left to right; then the 32 lane partials are
+// folded in lane order.
+// ---------------------------------------------------------------------------
+template <int APPLY, bool DEAD>
+__global__ void __launch_bounds__(256) k_wide_rows(SweepArgs a) {
+  const uint32_t* plan = a.plan;
+  if (plan[0] != kPlanMagic) return;
+  const uint64_t nb = plan[1];
+  const uint32_t n_wide = plan[2];
+  const uint32_t* wide = plan + plan_wide_off(nb);
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
+  bool bad = false;
+  for (uint32_t i = gw; i < n_wide; i += nw) {
+    const uint32_t r = wide[i];
+    const uint32_t rs = a.row_ptr[r], re = a.row_ptr[r + 1];
+    float acc = 0.0f;
+    uint32_t k = rs + lane;
+    for (; k + 96 < re; k += 128) {
+      float p[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = global_term<DEAD>(a, k + 32 * j, bad);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc = __fadd_rn(acc, p[j]);
+    }
+    for (; k < re; k += 32) acc = __fadd_rn(acc, global_term<DEAD>(a, k, bad));
+    float tot = 0.0f;
+#pragma unroll
+    for (int l = 0; l < 32; ++l) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, acc, l));
+    if (lane == 0) apply_row<APPLY>(tot, r, a, true);
+  }
+  if (bad) record_status(a.status, kStatusBadIndex);
+}
+
+// ---------------------------------------------------------------------------
+// Long rows (> kLongRow): one CTA per row. Order: thread t folds connections
+// rs+t, rs+t+256, ... then thread 0 folds the 256 partials in order.
 // ---------------------------------------------------------------------------
 template <int APPLY, bool DEAD>
 __global__ void __launch_bounds__(256) k_long_rows(SweepArgs a) {
   __shared__ float part[256];
   const uint32_t* plan = a.plan;
   if (plan[0] != kPlanMagic) return;
-  const uint64_t nb = plan_blocks(a.n_edges);
-  const uint32_t n_long = plan[2];
+  const uint64_t nb = plan[1];
+  const uint32_t n_long = plan[3];
+  const uint32_t* lng = plan + plan_wide_off(nb) + plan_max_wide(a.n_edges);
+  bool bad = false;
   for (uint32_t i = blockIdx.x; i < n_long; i += gridDim.x) {
-    const uint32_t r = plan[4 + nb + i];
+    const uint32_t r = lng[i];
     const uint32_t rs = a.row_ptr[r], re = a.row_ptr[r + 1];
     float acc = 0.0f;
     for (uint32_t k = rs + threadIdx.x; k < re; k += blockDim.x)
-      acc = __fadd_rn(acc, global_term<DEAD>(a, k));
+      acc = __fadd_rn(acc, global_term<DEAD>(a, k, bad));
     part[threadIdx.x] = acc;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -210,37 +292,110 @@ __global__ void __launch_bounds__(256) k_long_rows(SweepArgs a) {
     }
     __syncthreads();
   }
+  if (bad) record_status(a.status, kStatusBadIndex);
 }
 
 // ---------------------------------------------------------------------------
 // The tile sweep
 // ---------------------------------------------------------------------------
-template <int S, int NSTAGE, int NT, bool DEAD, bool TRACE>
-struct SweepSmem {
-  static constexpr uint32_t kStageBytes =
-      S * 4u /*src*/ + S * 4u /*w*/ + (TRACE ? S * 4u : 0u) + (DEAD ? S : 0u);
-  static constexpr uint32_t kOffA = NSTAGE * kStageBytes;
-  static constexpr uint32_t kOffPost = kOffA + S * 4u;
-  static constexpr uint32_t kOffWide = kOffPost + S * 4u;
-  static constexpr uint32_t kOffBar = kOffWide + (NT / 32) * kMaxWideChunks * 4u;
-  static constexpr uint32_t kBytes = kOffBar + NSTAGE * 8u + 16u;
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Named barrier that also ORs a predicate across the participating threads.
+__device__ __forceinline__ bool named_or(uint32_t id, uint32_t n, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+constexpr uint32_t kHaloCap = kHalo + 4;  // halo slice incl. alignment slack
+
+// Folds buf[lo, hi) (shared memory) into acc strictly left to right, loading
+// eight values ahead of the additions.
+__device__ __forceinline__ float fold_range(const float* buf, uint32_t lo,
+                                            uint32_t hi, float acc) {
+  uint32_t q = lo;
+  for (; q + 8 <= hi; q += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = buf[q + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+  }
+  for (; q < hi; ++q) acc = __fadd_rn(acc, buf[q]);
+  return acc;
+}
+
+// buf[lo, hi) = v, with float4 stores for the aligned middle.
+__device__ __forceinline__ void fill_range(float* buf, uint32_t lo, uint32_t hi,
+                                           float v) {
+  uint32_t q = lo;
+  for (; q < hi && (q & 3u); ++q) buf[q] = v;
+  const float4 v4 = make_float4(v, v, v, v);
+  for (; q + 4 <= hi; q += 4) *reinterpret_cast<float4*>(buf + q) = v4;
+  for (; q < hi; ++q) buf[q] = v;
+}
+
+template <int S_, int NSTAGE_, int NCW_, bool FOLD, bool UPD, bool TRACE, bool DEAD>
+struct SweepLayout {
+  static constexpr int S = S_, NSTAGE = NSTAGE_, NCW = NCW_;
+  static constexpr uint32_t NCT = NCW * 32;  // consumer threads
+  static constexpr uint32_t NT = NCT + 32;   // + one producer warp
+  // row_ptr slice capacity (u32): update sweeps target rows of >= 4
+  // connections; forward sweeps also cover graphs of ~1-2 per row. Tiles with
+  // more rows read row_ptr from global memory instead.
+  static constexpr uint32_t RCAP = (UPD ? S / 4 : S) + 16;
+  static constexpr uint32_t kWideCap = 64;   // wide rows touching one tile
+  // per stage
+  static constexpr uint32_t kOffW = S * 4u;
+  static constexpr uint32_t kOffE = kOffW + S * 4u;
+  static constexpr uint32_t kOffDead = kOffE + (TRACE ? S * 4u : 0u);
+  static constexpr uint32_t kOffRp = kOffDead + (DEAD ? S : 0u);
+  static constexpr uint32_t kOffHalo = kOffRp + RCAP * 4u;  // pre src,w; post src,w
+  static constexpr uint32_t kStage = kOffHalo + (FOLD ? 4u * kHaloCap * 4u : 0u);
+  // shared by all stages
+  static constexpr uint32_t kPost = NSTAGE * kStage;
+  // s_post holds the products w*act (fold input), then the row value.
+  static constexpr uint32_t kHaloP = kPost + S * 4u;
+  static constexpr uint32_t kWide = kHaloP + (FOLD ? 2u * kHaloCap * 4u : 0u);
+  static constexpr uint32_t kMeta = kWide + kWideCap * 4u + 16u;
+  static constexpr uint32_t kBar = kMeta + NSTAGE * 32u;
+  static constexpr uint32_t kBytes = kBar + 2u * NSTAGE * 8u;
+  static_assert(kStage % 16 == 0 && kPost % 16 == 0 && kOffHalo % 16 == 0,
+                "16-byte stage alignment");
 };
 
-template <int S, int NSTAGE, int NT, bool FOLD, int APPLY, int UPD, bool TRACE,
-          bool DEAD>
-__global__ void __launch_bounds__(NT) k_sweep(SweepArgs a) {
-  static_assert(S % kPlanG == 0, "tile must be a multiple of the plan block");
-  static_assert(NSTAGE >= 3, "need at least 3 stages");
-  constexpr int LOOK = NSTAGE - 2;
-  constexpr int NWARPS = NT / 32;
+template <class L, bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
+__global__ void __launch_bounds__(L::NT) k_sweep(SweepArgs a) {
+  constexpr int S = L::S, NSTAGE = L::NSTAGE;
+  constexpr uint32_t NCT = L::NCT;
   constexpr uint32_t kBlocksPerTile = S / kPlanG;
-  using L = SweepSmem<S, NSTAGE, NT, DEAD, TRACE>;
+  constexpr uint32_t kPer = S / NCT;  // tile connections per consumer thread
+  static_assert(S % kPlanG == 0, "tile must be a multiple of the plan block");
+  static_assert(S % NCT == 0 && kPer <= 16, "tile/consumer ratio");
+  static_assert(S >= 2 * kSeqMax, "a short row must not span a whole tile");
 
   extern __shared__ __align__(128) unsigned char smem[];
-  float* s_a = reinterpret_cast<float*>(smem + L::kOffA);
-  float* s_post = reinterpret_cast<float*>(smem + L::kOffPost);
-  float* s_wide = reinterpret_cast<float*>(smem + L::kOffWide);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  float* s_post = reinterpret_cast<float*>(smem + L::kPost);
+  float* s_haloP = reinterpret_cast<float*>(smem + L::kHaloP);
+  uint32_t* s_wide = reinterpret_cast<uint32_t*>(smem + L::kWide);
+  uint32_t* s_wide_n = s_wide + L::kWideCap;
+  uint32_t* s_meta = reinterpret_cast<uint32_t*>(smem + L::kMeta);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* done = full + NSTAGE;
 
   const uint32_t* __restrict__ plan = a.plan;
   if (plan[0] != kPlanMagic) {
@@ -249,189 +404,327 @@ __global__ void __launch_bounds__(NT) k_sweep(SweepArgs a) {
   }
   const uint64_t nb = plan[1];
   const uint64_t n_edges = a.n_edges;
+  const uint32_t n_rows = a.n_rows;
   const uint32_t n_tiles = (uint32_t)((nb + kBlocksPerTile - 1) / kBlocksPerTile);
+  const uint32_t my_tiles =
+      blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
 
-  auto stage_src = [&](int st) {
-    return reinterpret_cast<uint32_t*>(smem + st * L::kStageBytes);
-  };
-  auto stage_w = [&](int st) {
-    return reinterpret_cast<float*>(smem + st * L::kStageBytes + S * 4u);
-  };
-  auto stage_e = [&](int st) {
-    return reinterpret_cast<float*>(smem + st * L::kStageBytes + S * 8u);
-  };
-  auto stage_dead = [&](int st) {
-    return reinterpret_cast<uint8_t*>(smem + st * L::kStageBytes + S * 8u +
-                                      (TRACE ? S * 4u : 0u));
-  };
+  auto stage = [&](int st) { return smem + st * L::kStage; };
 
   if (tid == 0) {
-    for (int s = 0; s < NSTAGE; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&done[s], 1);
+    }
     mbar_init_fence();
   }
   __syncthreads();
 
-  // Thread 0: stream tile `t` into stage `st`.
-  auto issue = [&](uint32_t t, int st) {
-    const uint64_t ts = (uint64_t)t * S;
-    const uint32_t n = (uint32_t)min_u64(S, n_edges > ts ? n_edges - ts : 0);
-    const uint32_t n4 = n & ~3u, n16 = n & ~15u;
-    uint32_t* ssrc = stage_src(st);
-    float* sw = stage_w(st);
-    for (uint32_t k = n4; k < n; ++k) {
-      ssrc[k] = a.src[ts + k];
-      sw[k] = a.w_in[ts + k];
-      if constexpr (TRACE) stage_e(st)[k] = a.e_in[ts + k];
+  // ======================= producer warp ===================================
+  // Streams tile i into stage i % NSTAGE once the consumers are done with the
+  // tile that used the stage before; for update sweeps it also bulk-stores
+  // that finished tile, so consumers never wait on stores.
+  if (warp == 0) {
+    if (lane != 0) return;
+    bool timed_out = false;
+    for (uint32_t i = 0; i < my_tiles + NSTAGE; ++i) {
+      const int st = (int)(i % NSTAGE);
+      unsigned char* sb = stage(st);
+      if (i >= (uint32_t)NSTAGE) {
+        const uint32_t j = i - NSTAGE;  // tile leaving this stage
+        if (j >= my_tiles) continue;
+        if (!mbar_wait_bounded(&done[st], (j / NSTAGE) & 1u, a.timeout_ns)) {
+          timed_out = true;
+          break;
+        }
+        if constexpr (UPD != kUpdNone) {
+          const uint64_t js = (uint64_t)(blockIdx.x + j * gridDim.x) * S;
+          const uint32_t jn4 = (uint32_t)min_u64(S, n_edges - js) & ~3u;
+          if (jn4) {
+            bulk_store(a.w_out + js, sb + L::kOffW, jn4 * 4u);
+            if constexpr (TRACE) bulk_store(a.e_out + js, sb + L::kOffE, jn4 * 4u);
+          }
+          bulk_commit();
+          bulk_wait_read<0>();
+        }
+      }
+      if (i >= my_tiles) continue;
+      const uint32_t t = blockIdx.x + i * gridDim.x;
+      const uint64_t ts = (uint64_t)t * S;
+      const uint32_t n = (uint32_t)min_u64(S, n_edges - ts);
+      const uint64_t te = ts + n;
+      const uint32_t b0 = t * kBlocksPerTile;
+      const uint32_t b1 = (uint32_t)min_u64((uint64_t)b0 + kBlocksPerTile, nb);
+      const uint32_t* P0 = plan + kPlanHdr + 3 * b0;
+      const uint32_t* P1 = plan + kPlanHdr + 3 * b1;
+      const uint32_t o_begin = P0[0], o_end = P1[0];
+      const uint32_t rp_lo = o_begin ? o_begin - 1 : 0u;
+      const uint32_t rp_a = rp_lo & ~3u;
+      const uint32_t rp_cnt = o_end + 1 - rp_a;  // row_ptr[rp_a .. o_end]
+      const bool rp_ok = rp_cnt <= L::RCAP;
+      // Halo extents of the two boundary rows (short rows only).
+      uint32_t pre_lo = (uint32_t)ts, pre_shift = 0, pre_len = 0, post_len = 0;
+      if (FOLD && n > 0) {
+        if (o_begin > 0 && P0[2] > ts && P0[2] - P0[1] <= kSeqMax) {
+          pre_lo = P0[1] & ~3u;
+          pre_shift = P0[1] - pre_lo;
+          pre_len = (uint32_t)ts - P0[1];
+        }
+        if (o_end > o_begin && P1[2] > te && P1[2] - P1[1] <= kSeqMax)
+          post_len = P1[2] - (uint32_t)te;
+      }
+      uint32_t* s_src = reinterpret_cast<uint32_t*>(sb);
+      float* s_w = reinterpret_cast<float*>(sb + L::kOffW);
+      float* s_e = reinterpret_cast<float*>(sb + L::kOffE);
+      uint8_t* s_dead = sb + L::kOffDead;
+      uint32_t* s_rp = reinterpret_cast<uint32_t*>(sb + L::kOffRp);
+      uint32_t* h_src = reinterpret_cast<uint32_t*>(sb + L::kOffHalo);
+      float* h_w = reinterpret_cast<float*>(h_src + kHaloCap);
+      uint32_t* g_src = reinterpret_cast<uint32_t*>(h_w + kHaloCap);
+      float* g_w = reinterpret_cast<float*>(g_src + kHaloCap);
+      const uint32_t n4 = n & ~3u, n16 = n & ~15u;
+      const uint32_t rp4 = rp_ok ? (rp_cnt & ~3u) : 0u;
+      const uint32_t pre_cnt = pre_len ? (uint32_t)ts - pre_lo : 0u;  // multiple of 4
+      const uint32_t post4 = post_len & ~3u;
+      for (uint32_t k = n4; k < n; ++k) {
+        s_src[k] = a.src[ts + k];
+        s_w[k] = a.w_in[ts + k];
+        if constexpr (TRACE) s_e[k] = a.e_in[ts + k];
+      }
+      if constexpr (DEAD) {
+        for (uint32_t k = n16; k < n; ++k) s_dead[k] = a.dead[ts + k];
+      }
+      if (rp_ok)
+        for (uint32_t k = rp4; k < rp_cnt; ++k) s_rp[k] = a.row_ptr[rp_a + k];
+      for (uint32_t k = post4; k < post_len; ++k) {
+        g_src[k] = a.src[te + k];
+        g_w[k] = a.w_in[te + k];
+      }
+      uint32_t* m = s_meta + st * 8;
+      m[0] = o_begin;
+      m[1] = o_end;
+      m[2] = rp_a;
+      m[3] = rp_ok ? 1u : 0u;
+      m[4] = pre_shift;
+      m[5] = pre_len;
+      m[6] = post_len;
+      const uint32_t bytes = n4 * 4u * (TRACE ? 3u : 2u) + (DEAD ? n16 : 0u) +
+                             rp4 * 4u + (pre_cnt + post4) * 8u;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&full[st], bytes);
+      if (n4) {
+        bulk_load(s_src, a.src + ts, n4 * 4u, &full[st]);
+        bulk_load(s_w, a.w_in + ts, n4 * 4u, &full[st]);
+        if constexpr (TRACE) bulk_load(s_e, a.e_in + ts, n4 * 4u, &full[st]);
+      }
+      if constexpr (DEAD) {
+        if (n16) bulk_load(s_dead, a.dead + ts, n16, &full[st]);
+      }
+      if (rp4) bulk_load(s_rp, a.row_ptr + rp_a, rp4 * 4u, &full[st]);
+      if (pre_cnt) {
+        bulk_load(h_src, a.src + pre_lo, pre_cnt * 4u, &full[st]);
+        bulk_load(h_w, a.w_in + pre_lo, pre_cnt * 4u, &full[st]);
+      }
+      if (post4) {
+        bulk_load(g_src, a.src + te, post4 * 4u, &full[st]);
+        bulk_load(g_w, a.w_in + te, post4 * 4u, &full[st]);
+      }
     }
-    if constexpr (DEAD) {
-      for (uint32_t k = n16; k < n; ++k) stage_dead(st)[k] = a.dead[ts + k];
-    }
-    const uint32_t bytes =
-        n4 * 4u * (TRACE ? 3u : 2u) + (DEAD ? n16 : 0u);
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&bars[st], bytes);
-    if (n4) {
-      bulk_load(ssrc, a.src + ts, n4 * 4u, &bars[st]);
-      bulk_load(sw, a.w_in + ts, n4 * 4u, &bars[st]);
-      if constexpr (TRACE) bulk_load(stage_e(st), a.e_in + ts, n4 * 4u, &bars[st]);
-    }
-    if constexpr (DEAD) {
-      if (n16) bulk_load(stage_dead(st), a.dead + ts, n16, &bars[st]);
-    }
-  };
-
-  const uint32_t my_tiles =
-      blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  if (tid == 0) {
-    for (uint32_t j = 0; j < (uint32_t)LOOK && j < my_tiles; ++j)
-      issue(blockIdx.x + j * gridDim.x, (int)(j % NSTAGE));
+    if (timed_out) record_status(a.status, kStatusTimeout);
+    if constexpr (UPD != kUpdNone) bulk_wait_all<0>();
+    return;
   }
 
-  for (uint32_t i = 0; i < my_tiles; ++i) {
-    const uint32_t t = blockIdx.x + i * gridDim.x;
+  // ======================= consumer warps ==================================
+  // Software pipeline: the gathers of tile i+1 are issued before tile i is
+  // folded and updated, and written to shared memory after it, so their L2
+  // latency overlaps the fold.
+  constexpr uint32_t HMAX = (2 * kHalo + NCT - 1) / NCT;  // halo connections per thread
+  const uint32_t ctid = tid - 32u;
+  const uint32_t cwarp = warp - 1u;
+  bool bad = false;
+
+  struct Geo {
+    uint32_t ts, n_in, te, o_begin, o_end, rp_a, pre_shift, pre_len, post_len;
+    bool rp_ok, has_head;
+  };
+  auto rp_at = [&](int st, const Geo& g, uint32_t r) -> uint32_t {
+    const uint32_t* s_rp = reinterpret_cast<const uint32_t*>(stage(st) + L::kOffRp);
+    return g.rp_ok ? s_rp[r - g.rp_a] : a.row_ptr[r];
+  };
+  auto load_geo = [&](uint32_t i) -> Geo {
     const int st = (int)(i % NSTAGE);
-    if (tid == 0 && i + LOOK < my_tiles) {
-      if constexpr (UPD != kUpdNone) bulk_wait_read<1>();
-      issue(t + LOOK * gridDim.x, (int)((i + LOOK) % NSTAGE));
+    const uint32_t* m = s_meta + st * 8;
+    const uint64_t ts64 = (uint64_t)(blockIdx.x + i * gridDim.x) * S;
+    Geo g;
+    g.ts = (uint32_t)ts64;
+    g.n_in = (uint32_t)min_u64(S, n_edges - ts64);
+    g.te = g.ts + g.n_in;
+    g.o_begin = m[0];
+    g.o_end = m[1];
+    g.rp_a = m[2];
+    g.rp_ok = m[3] != 0;
+    g.pre_shift = m[4];
+    g.pre_len = m[5];
+    g.post_len = m[6];
+    g.has_head = g.n_in > 0 && (g.o_begin == n_rows || rp_at(st, g, g.o_begin) > g.ts);
+    return g;
+  };
+
+  // Gathers in flight (registers): the tile's connections of this thread and
+  // its halo connections.
+  float pav[kPer];
+  float phv[HMAX];
+  uint8_t phd[HMAX];
+
+  auto issue = [&](uint32_t i) -> bool {
+    const int st = (int)(i % NSTAGE);
+    if (!mbar_wait_bounded(&full[st], (i / NSTAGE) & 1u, a.timeout_ns)) return false;
+    const Geo g = load_geo(i);
+    const unsigned char* sb = stage(st);
+    const uint32_t* s_src = reinterpret_cast<const uint32_t*>(sb);
+    const uint32_t* h_src = reinterpret_cast<const uint32_t*>(sb + L::kOffHalo);
+    const uint32_t* g_src = h_src + 2 * kHaloCap;
+    uint32_t sv[kPer];
+#pragma unroll
+    for (uint32_t j = 0; j < kPer; ++j) {
+      const uint32_t k = ctid + j * NCT;
+      sv[j] = k < g.n_in ? s_src[k] : 0u;
     }
-
-    const uint64_t ts64 = (uint64_t)t * S;
-    const uint32_t ts = (uint32_t)ts64;
-    const uint32_t n_in = (uint32_t)min_u64(S, n_edges > ts64 ? n_edges - ts64 : 0);
-    const uint32_t te = ts + n_in;
-    const uint32_t b0 = t * kBlocksPerTile;
-    const uint32_t b1 = (uint32_t)min_u64((uint64_t)b0 + kBlocksPerTile, nb);
-    const uint32_t o_begin = plan[3 + b0];
-    const uint32_t o_end = plan[3 + b1];
-    const bool has_head =
-        n_in > 0 && (o_begin == a.n_rows || a.row_ptr[o_begin] > ts);
-    const uint32_t n_items = (o_end - o_begin) + (has_head ? 1u : 0u);
-
-    const bool ok = mbar_wait_bounded(&bars[st], (i / NSTAGE) & 1u, a.timeout_ns);
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) record_status(a.status, kStatusTimeout);
-      break;
+    const uint32_t n_halo = FOLD ? g.pre_len + g.post_len : 0u;
+    uint32_t hv[HMAX];
+#pragma unroll
+    for (uint32_t m = 0; m < HMAX; ++m) {
+      const uint32_t j = ctid + m * NCT;
+      hv[m] = j < n_halo ? (j < g.pre_len ? h_src[g.pre_shift + j] : g_src[j - g.pre_len]) : 0u;
     }
-
-    const uint32_t* s_src = stage_src(st);
-    float* s_w = stage_w(st);
-    float* s_e = stage_e(st);
-    const uint8_t* s_dead = stage_dead(st);
-
-    // ---- A: gather source activations ----
-    for (uint32_t k = tid; k < n_in; k += NT) {
-      float v = 0.0f;
-      if (!DEAD || !s_dead[k]) v = gather_act(a, s_src[k]);
-      s_a[k] = v;
+#pragma unroll
+    for (uint32_t j = 0; j < kPer; ++j) pav[j] = gather_act(a, sv[j], bad);
+#pragma unroll
+    for (uint32_t m = 0; m < HMAX; ++m) {
+      const uint32_t j = ctid + m * NCT;
+      phv[m] = j < n_halo ? gather_act(a, hv[m], bad) : 0.0f;
+      phd[m] = 0;
+      if constexpr (DEAD) {
+        if (j < n_halo)
+          phd[m] = __ldg(a.dead + (j < g.pre_len ? g.ts - g.pre_len + j : g.te + j - g.pre_len));
+      }
     }
-    __syncthreads();
+    return true;
+  };
 
-    // ---- B: per-row fold / Apply / broadcast ----
-    auto item_row = [&](uint32_t idx) -> uint32_t {
-      return has_head ? (idx == 0 ? o_begin - 1 : o_begin + idx - 1) : o_begin + idx;
-    };
-    // B1: rows up to PLX_SEQ_ROW_MAX, one thread each.
-    for (uint32_t idx = tid; idx < n_items; idx += NT) {
-      const uint32_t r = item_row(idx);
-      const bool owned = !(has_head && idx == 0);
-      const uint32_t rs = a.row_ptr[r], re = a.row_ptr[r + 1];
-      if (re - rs > PLX_SEQ_ROW_MAX) continue;
+  // Lands the gathers of tile i: act into the FromId slot, products w*act
+  // into s_post, halo products into s_haloP.
+  auto finish = [&](uint32_t i) {
+    const int st = (int)(i % NSTAGE);
+    const Geo g = load_geo(i);
+    unsigned char* sb = stage(st);
+    float* s_a = reinterpret_cast<float*>(sb);
+    const float* s_w = reinterpret_cast<const float*>(sb + L::kOffW);
+    const uint8_t* s_dead = sb + L::kOffDead;
+    const float* h_w = reinterpret_cast<const float*>(sb + L::kOffHalo) + kHaloCap;
+    const float* g_w = h_w + 2 * kHaloCap;
+#pragma unroll
+    for (uint32_t j = 0; j < kPer; ++j) {
+      const uint32_t k = ctid + j * NCT;
+      if (k < g.n_in) {
+        float v = pav[j];
+        float p = __fmul_rn(s_w[k], v);
+        if constexpr (DEAD) {
+          if (s_dead[k]) {
+            v = 0.0f;
+            p = 0.0f;
+          }
+        }
+        s_a[k] = v;
+        s_post[k] = p;
+      }
+    }
+    const uint32_t n_halo = FOLD ? g.pre_len + g.post_len : 0u;
+#pragma unroll
+    for (uint32_t m = 0; m < HMAX; ++m) {
+      const uint32_t j = ctid + m * NCT;
+      if (j < n_halo) {
+        const float w = j < g.pre_len ? h_w[g.pre_shift + j] : g_w[j - g.pre_len];
+        const float p = phd[m] ? 0.0f : __fmul_rn(w, phv[m]);
+        s_haloP[j < g.pre_len ? j : kHaloCap + (j - g.pre_len)] = p;
+      }
+    }
+    if (ctid == 0) *s_wide_n = 0;
+  };
+
+  bool ok = my_tiles == 0 || issue(0);
+  if (named_or(1, NCT, !ok)) {
+    if (ctid == 0) record_status(a.status, kStatusTimeout);
+  } else {
+    if (my_tiles) finish(0);
+    named_sync(1, NCT);
+  }
+  for (uint32_t i = 0; ok && i < my_tiles; ++i) {
+    const int st = (int)(i % NSTAGE);
+    const Geo g = load_geo(i);
+    const uint32_t ts = g.ts, te = g.te, n_in = g.n_in;
+    const bool has_next = i + 1 < my_tiles;
+    const bool ok_next = !has_next || issue(i + 1);
+
+    unsigned char* sb = stage(st);
+    const float* s_a = reinterpret_cast<const float*>(sb);
+    float* s_w = reinterpret_cast<float*>(sb + L::kOffW);
+    float* s_e = reinterpret_cast<float*>(sb + L::kOffE);
+    const uint8_t* s_dead = sb + L::kOffDead;
+    const uint32_t n_items = (g.o_end - g.o_begin) + (g.has_head ? 1u : 0u);
+
+    // ---- B: per-row fold / Apply / broadcast (rows spread over warps) ----
+    for (uint32_t base = 0; base < n_items; base += NCT) {
+      const uint32_t idx = base + lane * L::NCW + cwarp;
+      if (idx >= n_items) continue;
+      const bool head = g.has_head && idx == 0;
+      const uint32_t r = g.has_head ? g.o_begin - 1 + idx : g.o_begin + idx;
+      const uint32_t rs = rp_at(st, g, r), re = rp_at(st, g, r + 1);
+      if (re - rs > kSeqMax) {
+        if constexpr (UPD != kUpdNone) {
+          const uint32_t slot = atomicAdd(s_wide_n, 1u);
+          if (slot < L::kWideCap) s_wide[slot] = r;
+        }
+        continue;
+      }
+      const uint32_t lo = max(rs, ts) - ts, hi = min(re, te) - ts;
       float post;
       if constexpr (FOLD) {
         float acc = 0.0f;
-        uint32_t k = rs;
-        for (; k < re && k < ts; ++k) acc = __fadd_rn(acc, global_term<DEAD>(a, k));
-        const uint32_t mid_end = min(re, te);
-        for (; k < mid_end; ++k) {
-          const uint32_t q = k - ts;
-          float p = __fmul_rn(s_w[q], s_a[q]);
-          if constexpr (DEAD) p = s_dead[q] ? 0.0f : p;
-          acc = __fadd_rn(acc, p);
-        }
-        for (; k < re; ++k) acc = __fadd_rn(acc, global_term<DEAD>(a, k));
-        post = apply_row<APPLY>(acc, r, a, owned);
+        if (head) acc = fold_range(s_haloP, 0, g.pre_len, acc);
+        acc = fold_range(s_post, lo, hi, acc);
+        if (re > te) acc = fold_range(s_haloP + kHaloCap, 0, re - te, acc);
+        post = apply_row<APPLY>(acc, r, a, !head);
       } else {
         post = __ldg(a.post + r);
       }
-      if constexpr (UPD != kUpdNone) {
-        const uint32_t lo = max(rs, ts), hi = min(re, te);
-        for (uint32_t k = lo; k < hi; ++k) s_post[k - ts] = post;
-      }
+      if constexpr (UPD != kUpdNone) fill_range(s_post, lo, hi, post);
     }
-    // B2: longer rows, one warp each.
-    for (uint32_t idx = warp; idx < n_items; idx += NWARPS) {
-      const uint32_t r = item_row(idx);
-      const bool owned = !(has_head && idx == 0);
-      const uint32_t rs = a.row_ptr[r], re = a.row_ptr[r + 1];
-      const uint32_t len = re - rs;
-      if (len <= PLX_SEQ_ROW_MAX) continue;
-      float post = 0.0f;
-      if constexpr (FOLD) {
-        if (len > kLongRow) {
-          post = stored_post<APPLY>(r, a);  // written by k_long_rows
-        } else {
-          float* wide = s_wide + warp * kMaxWideChunks;
-          const uint32_t nch = (len + kWideChunk - 1) / kWideChunk;
-          for (uint32_t c = lane; c < nch; c += 32) {
-            const uint32_t c0 = rs + c * kWideChunk;
-            const uint32_t c1 = min(re, c0 + kWideChunk);
-            float acc = 0.0f;
-            for (uint32_t k = c0; k < c1; ++k) {
-              float p;
-              if (k >= ts && k < te) {
-                const uint32_t q = k - ts;
-                p = __fmul_rn(s_w[q], s_a[q]);
-                if constexpr (DEAD) p = s_dead[q] ? 0.0f : p;
-              } else {
-                p = global_term<DEAD>(a, k);
-              }
-              acc = __fadd_rn(acc, p);
-            }
-            wide[c] = acc;
-          }
-          __syncwarp();
-          if (lane == 0) {
-            float acc = 0.0f;
-            for (uint32_t c = 0; c < nch; ++c) acc = __fadd_rn(acc, wide[c]);
-            post = apply_row<APPLY>(acc, r, a, owned);
-          }
-          post = __shfl_sync(0xffffffffu, post, 0);
-          __syncwarp();
-        }
-      } else {
-        post = __ldg(a.post + r);
-      }
-      if constexpr (UPD != kUpdNone) {
-        const uint32_t lo = max(rs, ts), hi = min(re, te);
-        for (uint32_t k = lo + lane; k < hi; k += 32) s_post[k - ts] = post;
-      }
+    if (named_or(1, NCT, !ok_next)) {
+      if (ctid == 0) record_status(a.status, kStatusTimeout);
+      break;
     }
-    __syncthreads();
 
     if constexpr (UPD != kUpdNone) {
+      // Rows summed by k_wide_rows / k_long_rows: broadcast their stored value.
+      const uint32_t n_wide = min(*s_wide_n, L::kWideCap);
+      for (uint32_t w = cwarp; w < n_wide; w += L::NCW) {
+        const uint32_t r = s_wide[w];
+        const float post = FOLD ? stored_post<APPLY>(r, a) : __ldg(a.post + r);
+        const uint32_t lo = max(rp_at(st, g, r), ts) - ts;
+        const uint32_t hi = min(rp_at(st, g, r + 1), te) - ts;
+        for (uint32_t q = lo + lane; q < hi; q += 32) s_post[q] = post;
+      }
+      if (*s_wide_n > L::kWideCap && ctid == 0) record_status(a.status, kStatusBadPlan);
+      named_sync(1, NCT);
+
       // ---- C: per-connection update in shared memory ----
-      for (uint32_t k = tid; k < n_in; k += NT) {
+#pragma unroll
+      for (uint32_t j = 0; j < kPer; ++j) {
+        const uint32_t k = ctid + j * NCT;
+        if (k >= n_in) break;
         if constexpr (DEAD) {
           if (s_dead[k]) continue;
         }
@@ -446,65 +739,88 @@ __global__ void __launch_bounds__(NT) k_sweep(SweepArgs a) {
           s_w[k] = __fadd_rn(w, __fmul_rn(__fmul_rn(a.rate, post), av));
         }
       }
-      fence_proxy_async_smem();
-      __syncthreads();
+      // The last (n_in % 4) connections are stored here; the producer
+      // bulk-stores the rest.
       const uint32_t n4 = n_in & ~3u;
-      if (tid == 0) {
-        if (n4) {
-          bulk_store(a.w_out + ts, s_w, n4 * 4u);
-          if constexpr (TRACE) bulk_store(a.e_out + ts, s_e, n4 * 4u);
-        }
-        bulk_commit();  // one group per tile, empty or not
-      }
-      for (uint32_t k = n4 + tid; k < n_in; k += NT) {
+      if (ctid < n_in - n4) {
+        const uint32_t k = n4 + ctid;
         a.w_out[ts + k] = s_w[k];
         if constexpr (TRACE) a.e_out[ts + k] = s_e[k];
       }
+      named_sync(1, NCT);
     }
-    __syncthreads();
+    if (has_next) finish(i + 1);
+    // Order this thread's shared-memory writes before the producer's bulk
+    // copies (stores of this tile, loads of a later tile) into the stage.
+    fence_proxy_async_smem();
+    named_sync(1, NCT);
+    if (ctid == 0) mbar_arrive(&done[st]);
   }
-  if constexpr (UPD != kUpdNone) {
-    if (tid == 0) bulk_wait_all<0>();
-  }
+  if (bad) record_status(a.status, kStatusBadIndex);
 }
 
 // ---------------------------------------------------------------------------
 // Host launch helpers
 // ---------------------------------------------------------------------------
-struct TileCfg {
-  static constexpr int S = 2048;
-  static constexpr int NSTAGE = 4;
-  static constexpr int NT = 256;
-};
-
-template <bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
-int launch_sweep(plx_ctx* ctx, const SweepArgs& args, uint32_t n_long) {
-  constexpr int S = TileCfg::S, NSTAGE = TileCfg::NSTAGE, NT = TileCfg::NT;
-  using L = SweepSmem<S, NSTAGE, NT, DEAD, TRACE>;
-  auto kern = k_sweep<S, NSTAGE, NT, FOLD, APPLY, UPD, TRACE, DEAD>;
+template <class L, bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
+int launch_tiles(plx_ctx* ctx, const SweepArgs& args) {
+  auto kern = k_sweep<L, FOLD, APPLY, UPD, TRACE, DEAD>;
   PLX_TRY_CUDA(cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes));
   int per_sm = 0;
-  PLX_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT,
+  PLX_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, L::NT,
                                                              L::kBytes));
   if (per_sm < 1) per_sm = 1;
   const uint64_t nb = plan_blocks(args.n_edges);
-  const uint64_t n_tiles = (nb + S / kPlanG - 1) / (S / kPlanG);
-  const uint64_t grid =
-      std::min<uint64_t>(n_tiles, (uint64_t)ctx->num_sms * per_sm);
-  if (FOLD && n_long) {
-    // Rows longer than kLongRow are summed first.
-    const uint32_t g2 = std::min<uint32_t>(n_long, 4u * ctx->num_sms);
-    k_long_rows<APPLY, DEAD><<<g2, 256, 0, ctx->stream>>>(args);
-    PLX_LAUNCH_CHECK("k_long_rows");
-  }
-  kern<<<(unsigned)grid, NT, L::kBytes, ctx->stream>>>(args);
+  const uint64_t n_tiles = (nb + L::S / kPlanG - 1) / (L::S / kPlanG);
+  const uint64_t grid = std::min<uint64_t>(n_tiles, (uint64_t)ctx->num_sms * per_sm);
+  kern<<<(unsigned)grid, L::NT, L::kBytes, ctx->stream>>>(args);
   PLX_LAUNCH_CHECK("k_sweep");
   return PLX_OK;
 }
 
+// Tile configurations (S, NSTAGE, consumer warps). PLX_SWEEP_CFG selects one
+// for tuning; the default is entry 0.
+static int sweep_cfg() {
+  static int cfg = [] {
+    const char* e = getenv("PLX_SWEEP_CFG");
+    return e ? atoi(e) : 0;
+  }();
+  return cfg;
+}
+
+template <bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
+int launch_sweep(plx_ctx* ctx, const SweepArgs& args, const plx_csr* csr) {
+  constexpr bool U = UPD != kUpdNone;
+  if (FOLD && csr->n_wide) {
+    const uint32_t blocks = std::min<uint32_t>((csr->n_wide + 7) / 8, 16u * ctx->num_sms);
+    k_wide_rows<APPLY, DEAD><<<blocks, 256, 0, ctx->stream>>>(args);
+    PLX_LAUNCH_CHECK("k_wide_rows");
+  }
+  if (FOLD && csr->n_long) {
+    const uint32_t blocks = std::min<uint32_t>(csr->n_long, 4u * ctx->num_sms);
+    k_long_rows<APPLY, DEAD><<<blocks, 256, 0, ctx->stream>>>(args);
+    PLX_LAUNCH_CHECK("k_long_rows");
+  }
+  // A forward-only sweep with no short row is complete after the row kernels.
+  if (!U && csr->n_short == 0) return PLX_OK;
+  switch (sweep_cfg()) {
+    case 1:
+      return launch_tiles<SweepLayout<1024, 4, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+    case 2:
+      return launch_tiles<SweepLayout<2048, 3, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+    case 3:
+      return launch_tiles<SweepLayout<512, 3, 2, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+    case 4:
+      return launch_tiles<SweepLayout<512, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+    default:
+      return launch_tiles<SweepLayout<1024, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+  }
+}
+
 static int validate_csr(const plx_csr* csr) {
   PLX_CHECK_ARG(csr && csr->row_ptr && csr->plan, "csr, row_ptr and plan are required");
+  PLX_CHECK_ARG(aligned16(csr->row_ptr), "row_ptr must be 16-byte aligned");
   PLX_CHECK_ARG(csr->n_edges < 0xFFFF0000ull,
                 "n_edges must be < 2^32 - 2^16 per sweep (split larger layers)");
   return PLX_OK;
@@ -541,40 +857,49 @@ extern "C" int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id,
 
 extern "C" uint64_t plx_csr_plan_words(uint64_t n_edges, uint32_t n_rows) {
   (void)n_rows;
-  return 4 + plan_blocks(n_edges) + n_edges / kLongRow + 1;
+  const uint64_t nb = plan_blocks(n_edges);
+  return plan_wide_off(nb) + plan_max_wide(n_edges) + plan_max_long(n_edges);
 }
 
 extern "C" int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr,
                             uint32_t n_rows, uint64_t n_edges, uint32_t* plan,
-                            uint64_t plan_words, uint32_t* n_long_out) {
+                            uint64_t plan_words, plx_csr* out) {
   PLX_CHECK_ARG(ctx && row_ptr && plan, "ctx, row_ptr and plan are required");
   PLX_CHECK_ARG(n_edges < 0xFFFF0000ull, "n_edges must be < 2^32 - 2^16");
+  PLX_CHECK_ARG(aligned16(row_ptr), "row_ptr must be 16-byte aligned");
   const uint64_t need = plx_csr_plan_words(n_edges, n_rows);
   PLX_CHECK_ARG(plan_words >= need, "plan buffer too small: %llu words, need %llu",
                 (unsigned long long)plan_words, (unsigned long long)need);
   PLX_TRY_CUDA(cudaSetDevice(ctx->device));
   const uint64_t nb = plan_blocks(n_edges);
-  const uint32_t header[3] = {kPlanMagic, (uint32_t)nb, 0u};
+  const uint32_t header[kPlanHdr] = {kPlanMagic, (uint32_t)nb, 0u, 0u, 0u,
+                                     (uint32_t)plan_max_wide(n_edges),
+                                     (uint32_t)plan_max_long(n_edges), 0u};
   PLX_TRY_CUDA(cudaMemcpyAsync(plan, header, sizeof(header),
                                cudaMemcpyHostToDevice, ctx->stream));
   k_plan_blocks<<<(unsigned)((nb + 1 + 255) / 256), 256, 0, ctx->stream>>>(
       row_ptr, n_rows, n_edges, plan);
   PLX_LAUNCH_CHECK("k_plan_blocks");
-  const uint64_t max_long = n_edges / kLongRow + 1;
   k_plan_rows<<<(unsigned)(((uint64_t)n_rows + 256) / 256), 256, 0, ctx->stream>>>(
-      row_ptr, n_rows, n_edges, plan, max_long);
+      row_ptr, n_rows, n_edges, plan);
   PLX_LAUNCH_CHECK("k_plan_rows");
-  // The header copy reads a host stack array: wait for it before returning.
-  uint32_t hdr[3] = {0, 0, 0};
+  uint32_t hdr[kPlanHdr] = {};
   PLX_TRY_CUDA(cudaMemcpyAsync(hdr, plan, sizeof(hdr), cudaMemcpyDeviceToHost,
                                ctx->stream));
   PLX_TRY_CUDA(cudaStreamSynchronize(ctx->stream));
   if (hdr[0] != kPlanMagic)
     return set_error(PLX_ERR_ARG,
                      "row_ptr is not a valid CSR index (must start at 0, be "
-                     "non-decreasing and end at n_edges; at most %llu long rows)",
-                     (unsigned long long)max_long);
-  if (n_long_out) *n_long_out = hdr[2];
+                     "non-decreasing and end at n_edges)");
+  if (out) {
+    out->row_ptr = row_ptr;
+    out->plan = plan;
+    out->n_edges = n_edges;
+    out->n_rows = n_rows;
+    out->n_wide = hdr[2];
+    out->n_long = hdr[3];
+    out->n_short = hdr[4];
+  }
   return PLX_OK;
 }
 
@@ -608,8 +933,8 @@ extern "C" int plx_sweep_forward(plx_ctx* ctx, const plx_csr* csr,
   switch (apply_kind) {
 #define PLX_FWD_CASE(K)                                                       \
   case K:                                                                     \
-    return d ? launch_sweep<true, K, kUpdNone, false, true>(ctx, a, csr->n_long)           \
-             : launch_sweep<true, K, kUpdNone, false, false>(ctx, a, csr->n_long);
+    return d ? launch_sweep<true, K, kUpdNone, false, true>(ctx, a, csr)      \
+             : launch_sweep<true, K, kUpdNone, false, false>(ctx, a, csr);
     PLX_FWD_CASE(PLX_APPLY_IDENTITY)
     PLX_FWD_CASE(PLX_APPLY_SIGMOID)
     PLX_FWD_CASE(PLX_APPLY_TANH)
@@ -631,7 +956,7 @@ extern "C" int plx_sweep_forward_hebbian(
   PLX_CHECK_ARG(csr->n_edges == 0 ||
                     (from_id && act_src && w_in && w_out && trace_in && trace_out),
                 "connection arrays and act_src are required");
-  PLX_CHECK_ARG(w_in != w_out && trace_in != trace_out,
+  PLX_CHECK_ARG(csr->n_edges == 0 || (w_in != w_out && trace_in != trace_out),
                 "the fused sweep needs distinct input and output weight/trace buffers");
   PLX_CHECK_ARG(aligned16(from_id) && aligned16(dead) && aligned16(w_in) &&
                     aligned16(w_out) && aligned16(trace_in) && aligned16(trace_out),
@@ -649,8 +974,8 @@ extern "C" int plx_sweep_forward_hebbian(
   a.decay = decay;
   a.rate = rate;
   a.act_dst = act_dst;
-  return dead ? launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, true>(ctx, a, csr->n_long)
-              : launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, false>(ctx, a, csr->n_long);
+  return dead ? launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, true>(ctx, a, csr)
+              : launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, false>(ctx, a, csr);
 }
 
 extern "C" int plx_sweep_update(plx_ctx* ctx, const plx_csr* csr,
@@ -678,11 +1003,11 @@ extern "C" int plx_sweep_update(plx_ctx* ctx, const plx_csr* csr,
   const bool d = dead != nullptr;
   switch (update_kind) {
     case PLX_UPDATE_GRADIENT:
-      return d ? launch_sweep<false, PLX_APPLY_IDENTITY, kUpdGrad, false, true>(ctx, a, csr->n_long)
-               : launch_sweep<false, PLX_APPLY_IDENTITY, kUpdGrad, false, false>(ctx, a, csr->n_long);
+      return d ? launch_sweep<false, PLX_APPLY_IDENTITY, kUpdGrad, false, true>(ctx, a, csr)
+               : launch_sweep<false, PLX_APPLY_IDENTITY, kUpdGrad, false, false>(ctx, a, csr);
     case PLX_UPDATE_HEBBIAN:
-      return d ? launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebb, false, true>(ctx, a, csr->n_long)
-               : launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebb, false, false>(ctx, a, csr->n_long);
+      return d ? launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebb, false, true>(ctx, a, csr)
+               : launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebb, false, false>(ctx, a, csr);
     default:
       return set_error(PLX_ERR_ARG, "unknown update_kind %d", update_kind);
   }

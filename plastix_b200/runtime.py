@@ -9,7 +9,7 @@ the same bit pattern.
 """
 from __future__ import annotations
 
-from ctypes import byref, c_uint32, c_void_p
+from ctypes import byref, c_void_p
 from typing import Optional
 
 import torch
@@ -89,13 +89,14 @@ class DstCsr:
     def _init_plan(self, ctx: Context, n_edges: int, n_rows: int) -> None:
         words = _abi.lib().plx_csr_plan_words(n_edges, n_rows)
         self.plan = torch.empty(int(words), dtype=torch.int32, device=ctx.device)
-        n_long = c_uint32(0)
+        self.struct = Csr()
         call("plx_csr_plan", ctx.handle, c_void_p(_ptr(self.row_ptr)), n_rows, n_edges,
-             c_void_p(_ptr(self.plan)), words, byref(n_long))
+             c_void_p(_ptr(self.plan)), words, byref(self.struct))
         self.n_edges = n_edges
         self.n_rows = n_rows
-        self.n_long = n_long.value
-        self.struct = Csr(_ptr(self.row_ptr), _ptr(self.plan), n_edges, n_rows, self.n_long)
+        self.n_wide = self.struct.n_wide
+        self.n_long = self.struct.n_long
+        self.n_short = self.struct.n_short
 
 
 def sweep_forward(ctx: Context, csr: DstCsr, from_id: torch.Tensor, weight: torch.Tensor,
