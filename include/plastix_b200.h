@@ -95,6 +95,16 @@ int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
                  uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
                  plx_csr* out);
 
+/* Same as plx_csr_plan without synchronising: out's row counts are set to
+ * PLX_COUNT_UNKNOWN and the sweeps then read them on the device (launching
+ * the wide/long-row kernels unconditionally). An invalid row_ptr is reported
+ * by plx_ctx_sync (PLX_ERR_ARG) after the sweep. For per-step re-planning. */
+int plx_csr_plan_async(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                       uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
+                       plx_csr* out);
+
+#define PLX_COUNT_UNKNOWN 0xFFFFFFFFu
+
 /* ---- forward sweep (Map / Combine / Apply) ----------------------------- */
 
 /* Apply kinds (the unit-side policy run once per destination row). */
@@ -152,6 +162,69 @@ int plx_sweep_update(plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id,
                      const uint8_t* dead, const float* act_src,
                      uint32_t act_src_len, const float* post, int update_kind,
                      float rate, const float* w_in, float* w_out);
+
+/* ---- structural change: compaction, re-sort, regrowth ------------------ */
+
+#define PLX_MAX_FIELDS 16
+
+/* One SoA field to move: element i of src goes to some position of dst. */
+typedef struct plx_field {
+  const void* src;
+  void* dst;            /* must not overlap src                              */
+  uint32_t elem_bytes;  /* 1, 2, 4 or 8                                      */
+  uint32_t flags;       /* PLX_FIELD_*                                       */
+} plx_field;
+
+/* u8 field: the survivor's value is incremented, saturating at 255 (a
+ * connection age counter). plx_compact only. */
+#define PLX_FIELD_INC_SAT_U8 1u
+
+/* Keep predicates of plx_compact. */
+#define PLX_KEEP_FLAGS 0    /* keep_src u8: keep where != 0                     */
+#define PLX_KEEP_NOT_DEAD 1 /* keep_src u8 (the Dead field): keep where == 0    */
+#define PLX_KEEP_ABS_GE 2   /* keep_src f32: prune where |v| < threshold        */
+
+size_t plx_compact_scratch_bytes(uint64_t n);
+
+/* Order-preserving compaction of n connections (single-pass decoupled
+ * lookback). Survivor j of every field lands at dst[j]; *count_out (DEVICE
+ * memory) receives the survivor count; perm_out (optional, device) receives
+ * the surviving ids. Equals the reference's SOAAllocator::Gather
+ * (alloc.hpp:145-156) with the increasing list of ids that
+ * DoPruneConnections (plastix.hpp:280-297) left alive. scratch: device memory
+ * of plx_compact_scratch_bytes(n). */
+int plx_compact(plx_ctx* ctx, uint64_t n, int keep_kind, const void* keep_src,
+                float threshold, const plx_field* fields, uint32_t n_fields,
+                uint32_t* perm_out, uint64_t* count_out, void* scratch,
+                size_t scratch_bytes);
+
+/* dst[i] = src[perm[i]] for i < n and every field: the reference's
+ * SOAAllocator::Gather (alloc.hpp:145-156) on the device. */
+int plx_gather(plx_ctx* ctx, uint64_t n, const uint32_t* perm,
+               const plx_field* fields, uint32_t n_fields);
+
+size_t plx_radix_sort_scratch_bytes(uint64_t n);
+
+/* Stable LSD radix sort of n u32 keys on bits [begin_bit, end_bit): writes the
+ * sorted keys and the sorting permutation (perm_out[i] = original index of
+ * the i-th key). Replaces std::sort by CompactEdge bits (plastix.hpp:411-415)
+ * and the stable counting sort by SrcLevel (plastix.hpp:553-577) for the
+ * re-sort of connections by ToId. n < 2^30. */
+int plx_radix_sort_u32(plx_ctx* ctx, uint64_t n, const uint32_t* keys_in,
+                       uint32_t* keys_out, uint32_t* perm_out,
+                       uint32_t begin_bit, uint32_t end_bit, void* scratch,
+                       size_t scratch_bytes);
+
+/* Regrowth after compaction: connections [*count, n) (count in DEVICE
+ * memory) get FromId/ToId from a seeded counter-based generator, Weight 0
+ * and age 0 (weight/age may be NULL). For the i-th regrown connection:
+ *   h = mix64(mix64(seed) + step_base + i), mix64 = SplitMix64 finaliser;
+ *   FromId = src_base + ((h & 0xffffffff) * n_src >> 32);
+ *   ToId   = dst_base + ((h >> 32) * n_dst >> 32). */
+int plx_regrow(plx_ctx* ctx, uint64_t n, const uint64_t* count,
+               uint32_t* from_id, uint32_t* to_id, float* weight, uint8_t* age,
+               uint32_t src_base, uint32_t n_src, uint32_t dst_base,
+               uint32_t n_dst, uint64_t seed, uint64_t step_base);
 
 #ifdef __cplusplus
 }

@@ -53,6 +53,12 @@ def orc() -> ctypes.CDLL:
         L.oracle_stable_sort_u32.argtypes = [c_void_p, c_uint64, c_void_p]
         L.oracle_sort_unique_u64.argtypes = [c_void_p, c_uint64, c_void_p]
         L.oracle_sort_unique_u64.restype = c_uint64
+        L.oracle_mix64.argtypes = [c_uint64]
+        L.oracle_mix64.restype = c_uint64
+        L.oracle_regrow.argtypes = [c_uint64, c_uint64, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,
+                                    c_uint64, c_uint64]
+        L.oracle_keep_abs_ge.argtypes = [c_void_p, c_uint64, c_float, c_void_p]
         _orc = L
     return _orc
 
@@ -162,3 +168,43 @@ def ref_sweep_run(n_src, n_dst, from_id, to_id, w, trace, act_in, sweeps, decay,
     if rc != 0:
         raise RuntimeError("ref_sweep_run failed")
     return w_out, e_out, a_out
+
+
+# ---------------------------------------------------------------------------
+# Structural plasticity step (prune |w| < thr -> compact, regrow, re-sort by
+# ToId, forward sweep), composed from the restated reference primitives.
+# ---------------------------------------------------------------------------
+def keep_abs_ge(w, thr):
+    w = np.ascontiguousarray(w, np.float32)
+    keep = np.empty(w.size, np.uint8)
+    orc().oracle_keep_abs_ge(_p(w), w.size, thr, _p(keep))
+    return keep
+
+
+def regrow(from_id, to_id, w, age, count, src_base, n_src, dst_base, n_dst, seed,
+           step_base):
+    """In place on copies; returns (from, to, w, age)."""
+    f, t = from_id.copy(), to_id.copy()
+    ww, aa = w.copy(), age.copy()
+    orc().oracle_regrow(f.size, count, _p(f), _p(t), _p(ww), _p(aa), src_base, n_src,
+                        dst_base, n_dst, seed, step_base)
+    return f, t, ww, aa
+
+
+def structural_step(from_id, to_id, w, age, n_src, n_dst, thr, seed, step_base):
+    """One step on the oracle side. Inputs are dst-sorted SoA arrays
+    (from/to u32 absolute ids, w f32, age u8); sources are units [0, n_src),
+    destinations [n_src, n_src + n_dst). Returns the new dst-sorted arrays and
+    the survivor count."""
+    keep = keep_abs_ge(w, thr)
+    perm = survivors(keep)
+    m = perm.size
+    f = np.concatenate([gather(perm, from_id), np.zeros(from_id.size - m, np.uint32)])
+    t = np.concatenate([gather(perm, to_id), np.zeros(to_id.size - m, np.uint32)])
+    ww = np.concatenate([gather(perm, w), np.zeros(w.size - m, np.float32)])
+    a_s = gather(perm, age).astype(np.uint16)
+    aa = np.concatenate([np.minimum(a_s + 1, 255).astype(np.uint8),
+                         np.zeros(age.size - m, np.uint8)])
+    f, t, ww, aa = regrow(f, t, ww, aa, m, 0, n_src, n_src, n_dst, seed, step_base)
+    order = stable_sort_perm_u32(t - np.uint32(n_src))
+    return gather(order, f), gather(order, t), gather(order, ww), gather(order, aa), m

@@ -186,3 +186,35 @@ uint64_t oracle_sort_unique_u64(uint64_t* bits, uint64_t n, uint64_t* out) {
   }
   return m;
 }
+
+/* ---- structural plasticity workload ------------------------------------ */
+
+/* SplitMix64 finaliser (Steele, Lea, Flood 2014), the mixing function of the
+ * seeded regrowth (same definition as the device generator). */
+uint64_t oracle_mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+/* Connections [count, n) get fresh endpoints, weight 0, age 0. */
+void oracle_regrow(uint64_t n, uint64_t count, uint32_t* from, uint32_t* to,
+                   float* w, uint8_t* age, uint32_t src_base, uint32_t n_src,
+                   uint32_t dst_base, uint32_t n_dst, uint64_t seed,
+                   uint64_t step_base) {
+  const uint64_t key = oracle_mix64(seed) + step_base;
+  for (uint64_t i = count; i < n; ++i) {
+    const uint64_t h = oracle_mix64(key + (i - count));
+    from[i] = src_base + (uint32_t)(((h & 0xffffffffull) * n_src) >> 32);
+    to[i] = dst_base + (uint32_t)(((h >> 32) * n_dst) >> 32);
+    if (w) w[i] = 0.0f;
+    if (age) age[i] = 0;
+  }
+}
+
+/* The structural step's prune rule as a PruneConn policy would state it
+ * (ShouldPrune = |w| < threshold, plastix.hpp:290-293): keep = !(|w| < thr). */
+void oracle_keep_abs_ge(const float* w, uint64_t n, float thr, uint8_t* keep) {
+  for (uint64_t c = 0; c < n; ++c) keep[c] = !(fabsf(w[c]) < thr);
+}

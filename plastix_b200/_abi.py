@@ -41,6 +41,18 @@ class Csr(ctypes.Structure):
                 ("n_short", c_uint32)]
 
 
+class Field(ctypes.Structure):
+    _fields_ = [("src", c_void_p), ("dst", c_void_p), ("elem_bytes", c_uint32),
+                ("flags", c_uint32)]
+
+
+KEEP_FLAGS = 0
+KEEP_NOT_DEAD = 1
+KEEP_ABS_GE = 2
+FIELD_INC_SAT_U8 = 1
+COUNT_UNKNOWN = 0xFFFFFFFF
+MAX_FIELDS = 16
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "plx_version": (c_char_p, []),
@@ -55,6 +67,18 @@ _SIGNATURES = {
     "plx_csr_plan_words": (c_uint64, [c_uint64, c_uint32]),
     "plx_csr_plan": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p, c_uint64,
                              c_void_p]),
+    "plx_csr_plan_async": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p,
+                                   c_uint64, c_void_p]),
+    "plx_compact_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
+    "plx_compact": (c_int, [c_void_p, c_uint64, c_int, c_void_p, c_float, c_void_p,
+                            c_uint32, c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_gather": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32]),
+    "plx_radix_sort_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
+    "plx_radix_sort_u32": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p,
+                                   c_uint32, c_uint32, c_void_p, ctypes.c_size_t]),
+    "plx_regrow": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
+                           c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_uint64,
+                           c_uint64]),
     "plx_sweep_forward": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_uint32, c_int, c_void_p, c_void_p, c_void_p]),
     "plx_sweep_forward_hebbian": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p,

@@ -1,0 +1,297 @@
+// K4: stable LSD radix sort (onesweep: one read and one write of the keys and
+// values per 8-bit digit, decoupled lookback across tiles for the per-digit
+// offsets) of u32 keys with a u32 payload, producing the sorted keys and the
+// sorting permutation. plx_gather applies the permutation to the connection
+// fields.
+//
+// Replaces, for connections re-sorted by destination after structural change,
+// the reference's std::sort of CompactEdge bits (include/plastix/plastix.hpp
+// :411-415) and its stable counting sort by SrcLevel + Gather
+// (plastix.hpp:553-577, alloc.hpp:145-156). LSD radix sort is stable, so the
+// output equals a stable sort by key: unique, and checked bit for bit.
+//
+// Per pass and tile (256 threads x 16 keys, element order = item-major):
+//   * per 256-key round, warps rank keys by digit with __match_any_sync and
+//     shared per-warp digit counters, keeping the element order (stable);
+//   * the tile publishes its 256 digit counts, each thread looks back over
+//     the predecessors of its digit (bounded spin) and publishes the prefix;
+//   * keys are re-ordered by digit in shared memory and written out in
+//     digit runs (coalesced).
+#include "common.cuh"
+
+namespace plx {
+
+constexpr int kRT = 256;
+constexpr int kRItems = 16;
+constexpr int kRTile = kRT * kRItems;
+constexpr int kRWarps = kRT / 32;
+constexpr uint32_t kRFlagA = 1u << 30;
+constexpr uint32_t kRFlagP = 2u << 30;
+constexpr uint32_t kRValMask = (1u << 30) - 1;
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Histograms of every pass's digit over all keys (one read of the keys).
+__global__ void __launch_bounds__(256) k_radix_hist(const uint32_t* __restrict__ keys,
+                                                    uint64_t n, uint32_t begin_bit,
+                                                    uint32_t end_bit, uint32_t passes,
+                                                    uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_h[4][256];
+  for (uint32_t i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&s_h[0][0])[i] = 0;
+  __syncthreads();
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t k = __ldg(keys + i);
+    for (uint32_t p = 0; p < passes; ++p) {
+      const uint32_t sh = begin_bit + 8 * p;
+      const uint32_t bits = min(8u, end_bit - sh);
+      atomicAdd(&s_h[p][(k >> sh) & ((1u << bits) - 1u)], 1u);
+    }
+  }
+  __syncthreads();
+  for (uint32_t p = 0; p < passes; ++p)
+    for (uint32_t d = threadIdx.x; d < 256; d += blockDim.x)
+      if (s_h[p][d]) atomicAdd(&hist[p * 256 + d], s_h[p][d]);
+}
+
+// In place: hist[p][d] -> exclusive prefix over digits (global digit starts).
+__global__ void k_radix_scan(uint32_t* hist, uint32_t passes) {
+  __shared__ uint32_t s[256];
+  const uint32_t p = blockIdx.x, d = threadIdx.x;
+  if (p >= passes) return;
+  const uint32_t v = hist[p * 256 + d];
+  s[d] = v;
+  __syncthreads();
+  for (uint32_t o = 1; o < 256; o <<= 1) {
+    const uint32_t t = d >= o ? s[d - o] : 0u;
+    __syncthreads();
+    s[d] += t;
+    __syncthreads();
+  }
+  hist[p * 256 + d] = s[d] - v;
+}
+
+struct RadixPassArgs {
+  const uint32_t* keys_in;
+  const uint32_t* vals_in;  // null on the first pass: values are the indices
+  uint32_t* keys_out;
+  uint32_t* vals_out;
+  uint64_t n;
+  uint32_t shift;
+  uint32_t mask;
+  const uint32_t* digit_start;  // [256] global start of each digit
+  uint32_t* status;             // [tiles][256], zeroed
+  uint32_t* ticket;             // zeroed
+  int32_t* dstatus;
+  uint64_t timeout_ns;
+};
+
+__global__ void __launch_bounds__(kRT) k_radix_pass(RadixPassArgs a) {
+  __shared__ uint32_t s_keys[kRTile];
+  __shared__ uint32_t s_vals[kRTile];
+  __shared__ uint16_t s_cnt[2][kRWarps][256];
+  __shared__ uint32_t s_run[256];
+  __shared__ uint32_t s_local[256];
+  __shared__ uint32_t s_gbase[256];
+  __shared__ uint32_t s_tile;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  if (tid == 0) s_tile = atomicAdd(a.ticket, 1u);
+  for (uint32_t w = 0; w < kRWarps; ++w) s_cnt[0][w][tid] = 0;
+  s_run[tid] = 0;
+  __syncthreads();
+  const uint64_t tile = s_tile;
+  const uint64_t base = tile * kRTile;
+  const uint32_t lt = (1u << lane) - 1u;
+
+  uint32_t key[kRItems], val[kRItems], rank[kRItems];
+#pragma unroll
+  for (int j = 0; j < kRItems; ++j) {
+    const uint64_t e = base + (uint64_t)j * kRT + tid;
+    const bool ok = e < a.n;
+    key[j] = ok ? a.keys_in[e] : 0u;
+    val[j] = ok ? (a.vals_in ? a.vals_in[e] : (uint32_t)e) : 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kRItems; ++j) {
+    const int b = j & 1;
+    const uint64_t e = base + (uint64_t)j * kRT + tid;
+    const bool ok = e < a.n;
+    const uint32_t d = (key[j] >> a.shift) & a.mask;
+    const uint32_t peers = __match_any_sync(0xffffffffu, ok ? d : 0x100u);
+    const uint32_t lrank = __popc(peers & lt);
+    if (ok && lrank == 0) s_cnt[b][warp][d] = (uint16_t)__popc(peers);
+    __syncthreads();
+    {  // digit tid: per-warp counts -> exclusive prefixes; clear the other buffer
+      uint32_t run = s_run[tid];
+#pragma unroll
+      for (int w = 0; w < kRWarps; ++w) {
+        const uint32_t c = s_cnt[b][w][tid];
+        s_cnt[b][w][tid] = (uint16_t)run;
+        run += c;
+        s_cnt[b ^ 1][w][tid] = 0;
+      }
+      s_run[tid] = run;
+    }
+    __syncthreads();
+    rank[j] = ok ? s_cnt[b][warp][d] + lrank : 0u;
+  }
+  // Tile digit counts: s_run. Publish, look back, publish prefix.
+  const uint32_t cnt = s_run[tid];
+  uint32_t* st = a.status + tile * 256;
+  bool ok = true;
+  uint32_t prefix = 0;
+  if (tile == 0) {
+    st_release_u32(&st[tid], kRFlagP | cnt);
+  } else {
+    st_release_u32(&st[tid], kRFlagA | cnt);
+    int64_t p = (int64_t)tile - 1;
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spin = 0;
+    while (p >= 0) {
+      const uint32_t s = ld_acquire_u32(a.status + (uint64_t)p * 256 + tid);
+      if (s & kRFlagP) {
+        prefix += s & kRValMask;
+        break;
+      }
+      if (s & kRFlagA) {
+        prefix += s & kRValMask;
+        --p;
+        continue;
+      }
+      if ((++spin & 255u) == 0 && global_timer_ns() - t0 > a.timeout_ns) {
+        ok = false;
+        break;
+      }
+    }
+    st_release_u32(&st[tid], kRFlagP | (prefix + cnt));
+  }
+  if (!ok) record_status(a.dstatus, kStatusTimeout);
+  s_gbase[tid] = a.digit_start[tid] + prefix;
+  // local exclusive scan of the tile's digit counts
+  s_local[tid] = cnt;
+  __syncthreads();
+  for (uint32_t o = 1; o < 256; o <<= 1) {
+    const uint32_t t = tid >= o ? s_local[tid - o] : 0u;
+    __syncthreads();
+    s_local[tid] += t;
+    __syncthreads();
+  }
+  s_local[tid] -= cnt;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kRItems; ++j) {
+    const uint64_t e = base + (uint64_t)j * kRT + tid;
+    if (e < a.n) {
+      const uint32_t d = (key[j] >> a.shift) & a.mask;
+      const uint32_t pos = s_local[d] + rank[j];
+      s_keys[pos] = key[j];
+      s_vals[pos] = val[j];
+    }
+  }
+  __syncthreads();
+  const uint32_t valid = (uint32_t)min((uint64_t)kRTile, a.n - base);
+  for (uint32_t p = tid; p < valid; p += kRT) {
+    const uint32_t k = s_keys[p];
+    const uint32_t d = (k >> a.shift) & a.mask;
+    const uint64_t out = (uint64_t)s_gbase[d] + (p - s_local[d]);
+    a.keys_out[out] = k;
+    a.vals_out[out] = s_vals[p];
+  }
+}
+
+struct RadixScratch {
+  uint32_t* hist;    // [4][256]
+  uint32_t* ticket;  // [4]
+  uint32_t* status;  // [tiles][256]
+  uint32_t* k_alt;   // [n]
+  uint32_t* v_alt;   // [n]
+};
+
+static RadixScratch carve(void* scratch, uint64_t n) {
+  char* p = static_cast<char*>(scratch);
+  const uint64_t tiles = (n + kRTile - 1) / kRTile + 1;
+  RadixScratch s;
+  s.hist = reinterpret_cast<uint32_t*>(p);
+  s.ticket = reinterpret_cast<uint32_t*>(p + 4096);
+  s.status = reinterpret_cast<uint32_t*>(p + 4096 + 256);
+  char* q = p + 4096 + 256 + ((tiles * 1024 + 255) & ~255ull);
+  s.k_alt = reinterpret_cast<uint32_t*>(q);
+  s.v_alt = reinterpret_cast<uint32_t*>(q + ((n * 4 + 255) & ~255ull));
+  return s;
+}
+
+}  // namespace plx
+
+using namespace plx;
+
+extern "C" size_t plx_radix_sort_scratch_bytes(uint64_t n) {
+  const uint64_t tiles = (n + kRTile - 1) / kRTile + 1;
+  return (size_t)(4096 + 256 + ((tiles * 1024 + 255) & ~255ull) +
+                  2 * ((n * 4 + 255) & ~255ull));
+}
+
+extern "C" int plx_radix_sort_u32(plx_ctx* ctx, uint64_t n, const uint32_t* keys_in,
+                                  uint32_t* keys_out, uint32_t* perm_out,
+                                  uint32_t begin_bit, uint32_t end_bit,
+                                  void* scratch, size_t scratch_bytes) {
+  PLX_CHECK_ARG(ctx, "ctx is required");
+  PLX_CHECK_ARG(n == 0 || (keys_in && keys_out && perm_out),
+                "keys_in, keys_out and perm_out are required");
+  PLX_CHECK_ARG(n < (1ull << 30), "n must be < 2^30 (per-tile digit offsets are 30-bit)");
+  PLX_CHECK_ARG(begin_bit <= end_bit && end_bit <= 32, "bad bit range [%u, %u)",
+                begin_bit, end_bit);
+  PLX_CHECK_ARG(keys_in != keys_out, "keys_out must not alias keys_in");
+  PLX_CHECK_ARG(scratch && scratch_bytes >= plx_radix_sort_scratch_bytes(n),
+                "scratch too small: need %zu bytes", plx_radix_sort_scratch_bytes(n));
+  PLX_TRY_CUDA(cudaSetDevice(ctx->device));
+  if (n == 0) return PLX_OK;
+  const uint32_t passes = (end_bit - begin_bit + 7) / 8;
+  RadixScratch s = carve(scratch, n);
+  const uint64_t tiles = (n + kRTile - 1) / kRTile;
+  PLX_TRY_CUDA(cudaMemsetAsync(s.hist, 0, 4096 + 256, ctx->stream));
+  const uint64_t hb = std::min<uint64_t>((n + 255) / 256, 4ull * ctx->num_sms);
+  if (passes) {
+    k_radix_hist<<<(unsigned)hb, 256, 0, ctx->stream>>>(keys_in, n, begin_bit, end_bit,
+                                                        passes, s.hist);
+    PLX_LAUNCH_CHECK("k_radix_hist");
+    k_radix_scan<<<passes, 256, 0, ctx->stream>>>(s.hist, passes);
+    PLX_LAUNCH_CHECK("k_radix_scan");
+  }
+  // Ping-pong so that the last pass lands in keys_out / perm_out.
+  const uint32_t np = passes ? passes : 1;
+  const uint32_t* kin = keys_in;
+  const uint32_t* vin = nullptr;
+  for (uint32_t p = 0; p < np; ++p) {
+    const bool to_user = ((np - 1 - p) & 1u) == 0;
+    uint32_t* kout = to_user ? keys_out : s.k_alt;
+    uint32_t* vout = to_user ? perm_out : s.v_alt;
+    PLX_TRY_CUDA(cudaMemsetAsync(s.status, 0, tiles * 1024, ctx->stream));
+    PLX_TRY_CUDA(cudaMemsetAsync(s.ticket + p, 0, 4, ctx->stream));
+    RadixPassArgs a{};
+    a.keys_in = kin;
+    a.vals_in = vin;
+    a.keys_out = kout;
+    a.vals_out = vout;
+    a.n = n;
+    a.shift = passes ? begin_bit + 8 * p : 0;
+    const uint32_t bits = passes ? std::min(8u, end_bit - (begin_bit + 8 * p)) : 0;
+    a.mask = (1u << bits) - 1u;
+    a.digit_start = s.hist + (passes ? p * 256 : 0);
+    a.status = s.status;
+    a.ticket = s.ticket + p;
+    a.dstatus = ctx->d_status;
+    a.timeout_ns = ctx->timeout_ns;
+    k_radix_pass<<<(unsigned)tiles, kRT, 0, ctx->stream>>>(a);
+    PLX_LAUNCH_CHECK("k_radix_pass");
+    kin = kout;
+    vin = vout;
+  }
+  return PLX_OK;
+}

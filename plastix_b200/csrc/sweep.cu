@@ -792,13 +792,19 @@ static int sweep_cfg() {
 template <bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
 int launch_sweep(plx_ctx* ctx, const SweepArgs& args, const plx_csr* csr) {
   constexpr bool U = UPD != kUpdNone;
-  if (FOLD && csr->n_wide) {
-    const uint32_t blocks = std::min<uint32_t>((csr->n_wide + 7) / 8, 16u * ctx->num_sms);
+  // Row counts of PLX_COUNT_UNKNOWN (plans built without a host sync): the
+  // row kernels read the counts from the plan on the device.
+  const uint64_t max_wide = std::min<uint64_t>(plan_max_wide(args.n_edges), args.n_rows);
+  const uint64_t max_long = std::min<uint64_t>(plan_max_long(args.n_edges), args.n_rows);
+  const uint64_t n_wide = csr->n_wide == PLX_COUNT_UNKNOWN ? max_wide : csr->n_wide;
+  const uint64_t n_long = csr->n_long == PLX_COUNT_UNKNOWN ? max_long : csr->n_long;
+  if (FOLD && n_wide) {
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n_wide + 7) / 8, 16u * ctx->num_sms);
     k_wide_rows<APPLY, DEAD><<<blocks, 256, 0, ctx->stream>>>(args);
     PLX_LAUNCH_CHECK("k_wide_rows");
   }
-  if (FOLD && csr->n_long) {
-    const uint32_t blocks = std::min<uint32_t>(csr->n_long, 4u * ctx->num_sms);
+  if (FOLD && n_long) {
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>(n_long, 4u * ctx->num_sms);
     k_long_rows<APPLY, DEAD><<<blocks, 256, 0, ctx->stream>>>(args);
     PLX_LAUNCH_CHECK("k_long_rows");
   }
@@ -861,9 +867,40 @@ extern "C" uint64_t plx_csr_plan_words(uint64_t n_edges, uint32_t n_rows) {
   return plan_wide_off(nb) + plan_max_wide(n_edges) + plan_max_long(n_edges);
 }
 
+static int csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                    uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
+                    plx_csr* out, bool sync);
+
 extern "C" int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr,
                             uint32_t n_rows, uint64_t n_edges, uint32_t* plan,
                             uint64_t plan_words, plx_csr* out) {
+  return csr_plan(ctx, row_ptr, n_rows, n_edges, plan, plan_words, out, true);
+}
+
+extern "C" int plx_csr_plan_async(plx_ctx* ctx, const uint32_t* row_ptr,
+                                  uint32_t n_rows, uint64_t n_edges,
+                                  uint32_t* plan, uint64_t plan_words,
+                                  plx_csr* out) {
+  return csr_plan(ctx, row_ptr, n_rows, n_edges, plan, plan_words, out, false);
+}
+
+// Header words are written by a kernel (no host staging) so the async variant
+// needs no synchronisation.
+__global__ void k_plan_header(uint32_t* plan, uint32_t nb, uint32_t max_wide,
+                              uint32_t max_long) {
+  plan[0] = kPlanMagic;
+  plan[1] = nb;
+  plan[2] = 0;
+  plan[3] = 0;
+  plan[4] = 0;
+  plan[5] = max_wide;
+  plan[6] = max_long;
+  plan[7] = 0;
+}
+
+static int csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                    uint64_t n_edges, uint32_t* plan, uint64_t plan_words,
+                    plx_csr* out, bool sync) {
   PLX_CHECK_ARG(ctx && row_ptr && plan, "ctx, row_ptr and plan are required");
   PLX_CHECK_ARG(n_edges < 0xFFFF0000ull, "n_edges must be < 2^32 - 2^16");
   PLX_CHECK_ARG(aligned16(row_ptr), "row_ptr must be 16-byte aligned");
@@ -872,17 +909,28 @@ extern "C" int plx_csr_plan(plx_ctx* ctx, const uint32_t* row_ptr,
                 (unsigned long long)plan_words, (unsigned long long)need);
   PLX_TRY_CUDA(cudaSetDevice(ctx->device));
   const uint64_t nb = plan_blocks(n_edges);
-  const uint32_t header[kPlanHdr] = {kPlanMagic, (uint32_t)nb, 0u, 0u, 0u,
-                                     (uint32_t)plan_max_wide(n_edges),
-                                     (uint32_t)plan_max_long(n_edges), 0u};
-  PLX_TRY_CUDA(cudaMemcpyAsync(plan, header, sizeof(header),
-                               cudaMemcpyHostToDevice, ctx->stream));
+  k_plan_header<<<1, 1, 0, ctx->stream>>>(plan, (uint32_t)nb,
+                                          (uint32_t)plan_max_wide(n_edges),
+                                          (uint32_t)plan_max_long(n_edges));
+  PLX_LAUNCH_CHECK("k_plan_header");
   k_plan_blocks<<<(unsigned)((nb + 1 + 255) / 256), 256, 0, ctx->stream>>>(
       row_ptr, n_rows, n_edges, plan);
   PLX_LAUNCH_CHECK("k_plan_blocks");
   k_plan_rows<<<(unsigned)(((uint64_t)n_rows + 256) / 256), 256, 0, ctx->stream>>>(
       row_ptr, n_rows, n_edges, plan);
   PLX_LAUNCH_CHECK("k_plan_rows");
+  if (!sync) {
+    if (out) {
+      out->row_ptr = row_ptr;
+      out->plan = plan;
+      out->n_edges = n_edges;
+      out->n_rows = n_rows;
+      out->n_wide = PLX_COUNT_UNKNOWN;
+      out->n_long = PLX_COUNT_UNKNOWN;
+      out->n_short = PLX_COUNT_UNKNOWN;
+    }
+    return PLX_OK;
+  }
   uint32_t hdr[kPlanHdr] = {};
   PLX_TRY_CUDA(cudaMemcpyAsync(hdr, plan, sizeof(hdr), cudaMemcpyDeviceToHost,
                                ctx->stream));

@@ -15,7 +15,7 @@ from typing import Optional
 import torch
 
 from . import _abi
-from ._abi import Csr, call
+from ._abi import Csr, Field, call
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -76,6 +76,31 @@ class DstCsr:
         call("plx_csr_row_ptr", ctx.handle, c_void_p(_ptr(to_id) if n_edges else None),
              n_edges, row_base, n_rows, c_void_p(_ptr(self.row_ptr)))
         self._init_plan(ctx, n_edges, n_rows)
+
+    @classmethod
+    def from_sorted_async(cls, ctx: Context, to_id: torch.Tensor, row_base: int,
+                          n_rows: int, row_ptr: Optional[torch.Tensor] = None,
+                          plan: Optional[torch.Tensor] = None) -> "DstCsr":
+        """Builds row_ptr and the plan without a host synchronisation (row
+        counts stay unknown; the sweeps read them on the device). Reuses the
+        given buffers when they are large enough."""
+        self = cls.__new__(cls)
+        n_edges = int(to_id.numel())
+        if row_ptr is None or row_ptr.numel() < n_rows + 1:
+            row_ptr = torch.empty(n_rows + 1, dtype=torch.int32, device=ctx.device)
+        self.row_ptr = row_ptr
+        call("plx_csr_row_ptr", ctx.handle, c_void_p(_ptr(to_id) if n_edges else None),
+             n_edges, row_base, n_rows, c_void_p(_ptr(self.row_ptr)))
+        words = _abi.lib().plx_csr_plan_words(n_edges, n_rows)
+        if plan is None or plan.numel() < words:
+            plan = torch.empty(int(words), dtype=torch.int32, device=ctx.device)
+        self.plan = plan
+        self.struct = Csr()
+        call("plx_csr_plan_async", ctx.handle, c_void_p(_ptr(self.row_ptr)), n_rows, n_edges,
+             c_void_p(_ptr(self.plan)), words, byref(self.struct))
+        self.n_edges, self.n_rows = n_edges, n_rows
+        self.n_wide = self.n_long = self.n_short = _abi.COUNT_UNKNOWN
+        return self
 
     @classmethod
     def from_row_ptr(cls, ctx: Context, row_ptr: torch.Tensor) -> "DstCsr":
@@ -169,4 +194,115 @@ class HebbianSweepLayer:
                               self._w[o], self._e[c], self._e[o], self.act_dst,
                               decay=self.decay, rate=self.rate, dead=self.dead)
         self._cur = o
+        return self.act_dst
+
+
+# ---------------------------------------------------------------------------
+# Structural change: compaction, gather, radix sort, regrowth
+# ---------------------------------------------------------------------------
+def _fields(pairs, flags=None):
+    arr = (Field * max(1, len(pairs)))()
+    for i, (src, dst) in enumerate(pairs):
+        if src.dtype != dst.dtype or src.element_size() != dst.element_size():
+            raise ValueError("field src/dst dtypes differ")
+        arr[i] = Field(_ptr(src), _ptr(dst), src.element_size(),
+                       0 if flags is None else flags[i])
+    return arr
+
+
+class Scratch:
+    """Grow-only device scratch buffer (bytes)."""
+
+    def __init__(self, device):
+        self.device = device
+        self.buf = torch.empty(0, dtype=torch.uint8, device=device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            self.buf = torch.empty(int(nbytes), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def compact(ctx: Context, n: int, keep_kind: int, keep_src: torch.Tensor, pairs,
+            count_out: torch.Tensor, *, threshold: float = 0.0, flags=None,
+            perm_out: Optional[torch.Tensor] = None, scratch: Optional[Scratch] = None):
+    nbytes = _abi.lib().plx_compact_scratch_bytes(n)
+    s = (scratch or Scratch(ctx.device)).get(nbytes)
+    f = _fields(pairs, flags)
+    call("plx_compact", ctx.handle, n, keep_kind, _ptr(keep_src), threshold, f, len(pairs),
+         _ptr(perm_out), _ptr(count_out), _ptr(s), s.numel())
+
+
+def gather(ctx: Context, perm: torch.Tensor, pairs, n: Optional[int] = None):
+    n = int(perm.numel()) if n is None else n
+    f = _fields(pairs)
+    call("plx_gather", ctx.handle, n, _ptr(perm), f, len(pairs))
+
+
+def radix_sort_u32(ctx: Context, keys: torch.Tensor, keys_out: torch.Tensor,
+                   perm_out: torch.Tensor, begin_bit: int = 0, end_bit: int = 32, *,
+                   scratch: Optional[Scratch] = None):
+    n = int(keys.numel())
+    nbytes = _abi.lib().plx_radix_sort_scratch_bytes(n)
+    s = (scratch or Scratch(ctx.device)).get(nbytes)
+    call("plx_radix_sort_u32", ctx.handle, n, _ptr(keys), _ptr(keys_out), _ptr(perm_out),
+         begin_bit, end_bit, _ptr(s), s.numel())
+
+
+def regrow(ctx: Context, count: torch.Tensor, from_id: torch.Tensor, to_id: torch.Tensor,
+           weight: Optional[torch.Tensor], age: Optional[torch.Tensor], *, src_base: int,
+           n_src: int, dst_base: int, n_dst: int, seed: int, step_base: int):
+    call("plx_regrow", ctx.handle, int(from_id.numel()), _ptr(count), _ptr(from_id),
+         _ptr(to_id), _ptr(weight), _ptr(age), src_base, n_src, dst_base, n_dst, seed,
+         step_base)
+
+
+class StructuralLayer:
+    """Sparse layer with structural plasticity, stepped entirely on the device:
+    prune connections with |w| < threshold (order-preserving compaction, ages
+    of survivors +1), regrow the same number with seeded random endpoints
+    (w = 0, age = 0), re-sort all connections by ToId (stable radix sort +
+    Gather), rebuild the row index and run the forward sweep. Sources are
+    units [0, n_src), destinations [n_src, n_src + n_dst)."""
+
+    def __init__(self, ctx: Context, n_src: int, n_dst: int, from_id, to_id, weight, age,
+                 *, threshold: float = 0.02, seed: int = 1):
+        dev = ctx.device
+        self.ctx, self.n_src, self.n_dst = ctx, n_src, n_dst
+        self.threshold, self.seed = threshold, seed
+        n = int(from_id.numel())
+        self.n = n
+        mk = lambda t, dt: t.to(dev, dt).contiguous().clone()  # noqa: E731
+        self.f, self.t = mk(from_id, torch.int32), mk(to_id, torch.int32)
+        self.w, self.age = mk(weight, torch.float32), mk(age, torch.uint8)
+        self.f2, self.t2 = torch.empty_like(self.f), torch.empty_like(self.t)
+        self.w2, self.age2 = torch.empty_like(self.w), torch.empty_like(self.age)
+        self.keys = torch.empty_like(self.t)
+        self.keys_sorted = torch.empty_like(self.t)
+        self.perm = torch.empty_like(self.t)
+        self.count = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.scratch = Scratch(dev)
+        self.act_dst = torch.zeros(n_dst, dtype=torch.float32, device=dev)
+        self.key_bits = max(1, (n_dst - 1).bit_length())
+        self.step_index = 0
+        self.csr = DstCsr.from_sorted_async(ctx, self.t, n_src, n_dst)
+
+    def step(self, act_src: torch.Tensor) -> torch.Tensor:
+        ctx = self.ctx
+        compact(ctx, self.n, _abi.KEEP_ABS_GE, self.w,
+                [(self.f, self.f2), (self.t, self.t2), (self.w, self.w2),
+                 (self.age, self.age2)], self.count, threshold=self.threshold,
+                flags=[0, 0, 0, _abi.FIELD_INC_SAT_U8], scratch=self.scratch)
+        regrow(ctx, self.count, self.f2, self.t2, self.w2, self.age2, src_base=0,
+               n_src=self.n_src, dst_base=self.n_src, n_dst=self.n_dst, seed=self.seed,
+               step_base=self.step_index * self.n)
+        torch.sub(self.t2, self.n_src, out=self.keys)
+        radix_sort_u32(ctx, self.keys, self.keys_sorted, self.perm, 0, self.key_bits,
+                       scratch=self.scratch)
+        gather(ctx, self.perm, [(self.f2, self.f), (self.t2, self.t), (self.w2, self.w),
+                                (self.age2, self.age)])
+        self.csr = DstCsr.from_sorted_async(ctx, self.t, self.n_src, self.n_dst,
+                                            self.csr.row_ptr, self.csr.plan)
+        sweep_forward(ctx, self.csr, self.f, self.w, act_src, self.act_dst)
+        self.step_index += 1
         return self.act_dst
