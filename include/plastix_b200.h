@@ -198,6 +198,26 @@ int plx_compact(plx_ctx* ctx, uint64_t n, int keep_kind, const void* keep_src,
                 uint32_t* perm_out, uint64_t* count_out, void* scratch,
                 size_t scratch_bytes);
 
+/* Same compaction, allocating nothing. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory when they compact
+ * (a step loop with a fixed memory budget, a host framework that owns all
+ * device memory and forbids libraries from calling cudaMalloc). Neither the
+ * caller nor the library allocates: the scratch is a static device array of
+ * 512 KiB + 256 B that every GPU loading this library holds until exit.
+ *   - n <= 2^28 connections (268,435,456); larger n returns PLX_ERR_ARG.
+ *   - Runs on `stream` (a cudaStream_t) of the current device; no context.
+ *   - The first call on a device looks up the array's device address; make
+ *     that first call before any stream capture on the device.
+ *   - Every call on a device shares the array. Calls whose kernels overlap
+ *     on the GPU (different streams, no ordering between them) race and give
+ *     wrong results: order them on one stream or with events.
+ *   - If a bounded device-side wait expires, *count_out is set to UINT64_MAX.
+ * Output and arguments are otherwise those of plx_compact. */
+int plx_compact_noalloc(void* stream, uint64_t n, int keep_kind,
+                        const void* keep_src, float threshold,
+                        const plx_field* fields, uint32_t n_fields,
+                        uint32_t* perm_out, uint64_t* count_out);
+
 /* dst[i] = src[perm[i]] for i < n and every field: the reference's
  * SOAAllocator::Gather (alloc.hpp:145-156) on the device. */
 int plx_gather(plx_ctx* ctx, uint64_t n, const uint32_t* perm,

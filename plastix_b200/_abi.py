@@ -72,6 +72,8 @@ _SIGNATURES = {
     "plx_compact_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_compact": (c_int, [c_void_p, c_uint64, c_int, c_void_p, c_float, c_void_p,
                             c_uint32, c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_compact_noalloc": (c_int, [c_void_p, c_uint64, c_int, c_void_p, c_float, c_void_p,
+                                    c_uint32, c_void_p, c_void_p]),
     "plx_gather": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32]),
     "plx_radix_sort_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_radix_sort_u32": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p,

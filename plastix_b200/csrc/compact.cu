@@ -330,3 +330,87 @@ extern "C" int plx_regrow(plx_ctx* ctx, uint64_t n, const uint64_t* count,
   PLX_LAUNCH_CHECK("k_regrow");
   return PLX_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Compaction that allocates nothing.
+//
+// For callers that cannot allocate device memory at the point where they
+// compact: code running inside a region where an allocation would break the
+// caller's guarantees (a real-time step loop with a fixed memory budget, a
+// host framework that owns every device allocation through its own pool and
+// forbids libraries from calling cudaMalloc). The scratch lives in the static
+// array below, which every GPU that loads this library holds until exit.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace plx {
+
+constexpr uint64_t kNoAllocMaxN = 1ull << 28;             // 268,435,456 connections
+constexpr uint64_t kNoAllocTiles = kNoAllocMaxN / kCTile;  // 65,536 tiles
+constexpr size_t kNoAllocBytes = 256 + kNoAllocTiles * 8;  // 512 KiB + 256 B
+constexpr int kNoAllocMaxDevices = 64;
+
+// [0, 4): tile ticket; [4, 8): device status word; [256, ...): tile status.
+static __device__ __align__(256) unsigned char g_compact_scratch[kNoAllocBytes];
+
+struct NoAllocSlot {
+  std::once_flag once;
+  unsigned char* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+static NoAllocSlot g_noalloc_slots[kNoAllocMaxDevices];
+
+// A bounded wait that expired leaves the count at UINT64_MAX.
+__global__ void k_compact_noalloc_finish(const int32_t* status, uint64_t* count_out) {
+  if (*status != kStatusOk) *count_out = ~0ull;
+}
+
+}  // namespace plx
+
+extern "C" int plx_compact_noalloc(void* stream, uint64_t n, int keep_kind,
+                                   const void* keep_src, float threshold,
+                                   const plx_field* fields, uint32_t n_fields,
+                                   uint32_t* perm_out, uint64_t* count_out) {
+  PLX_CHECK_ARG(count_out, "count_out is required");
+  PLX_CHECK_ARG(keep_kind == PLX_KEEP_FLAGS || keep_kind == PLX_KEEP_NOT_DEAD ||
+                    keep_kind == PLX_KEEP_ABS_GE,
+                "unknown keep_kind %d", keep_kind);
+  PLX_CHECK_ARG(n == 0 || keep_src, "keep_src is required");
+  PLX_CHECK_ARG(n <= kNoAllocMaxN,
+                "n = %llu exceeds the no-allocation limit of %llu connections; "
+                "use plx_compact with caller-provided scratch",
+                (unsigned long long)n, (unsigned long long)kNoAllocMaxN);
+  int dev = 0;
+  PLX_TRY_CUDA(cudaGetDevice(&dev));
+  PLX_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "device %d out of range", dev);
+  NoAllocSlot& slot = g_noalloc_slots[dev];
+  // Once per device, with that device current: the device address of the
+  // static scratch (its host-side name is only a stand-in for the symbol).
+  std::call_once(slot.once, [&slot] {
+    slot.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&slot.ptr), g_compact_scratch);
+  });
+  if (slot.err != cudaSuccess) return check_cuda(slot.err, "cudaGetSymbolAddress");
+  CompactArgs a{};
+  if (int rc = fill_fields(a.f, fields, n_fields, n)) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t tiles = (n + kCTile - 1) / kCTile;
+  a.n = n;
+  a.keep_kind = keep_kind;
+  a.keep_src = keep_src;
+  a.threshold = threshold;
+  a.n_fields = n_fields;
+  a.perm_out = perm_out;
+  a.count_out = count_out;
+  a.ticket = reinterpret_cast<uint32_t*>(slot.ptr);
+  a.dstatus = reinterpret_cast<int32_t*>(slot.ptr + 4);
+  a.status = reinterpret_cast<uint64_t*>(slot.ptr + 256);
+  a.timeout_ns = 2000000000ull;
+  // The array keeps the previous call's contents: clear ticket, status word
+  // and the tile words this call uses.
+  PLX_TRY_CUDA(cudaMemsetAsync(slot.ptr, 0, 256 + tiles * 8, s));
+  k_compact<<<(unsigned)(tiles ? tiles : 1), kCT, 0, s>>>(a);
+  PLX_LAUNCH_CHECK("k_compact");
+  k_compact_noalloc_finish<<<1, 1, 0, s>>>(a.dstatus, count_out);
+  PLX_LAUNCH_CHECK("k_compact_noalloc_finish");
+  return PLX_OK;
+}
