@@ -77,12 +77,20 @@ int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id, uint64_t n_edges,
 typedef struct plx_csr {
   const uint32_t* row_ptr; /* n_rows + 1 entries, row_ptr[0] == 0          */
   const uint32_t* plan;    /* from plx_csr_plan                             */
+  const uint32_t* to_id;   /* optional ToId field (see below), or NULL      */
   uint64_t n_edges;        /* == row_ptr[n_rows], < 2^32 - 2^16             */
   uint32_t n_rows;
+  uint32_t row_base;       /* unit id of row 0 (ToId of its connections)    */
   uint32_t n_wide;         /* rows with PLX_SEQ_ROW_MAX < length <= 2048    */
   uint32_t n_long;         /* rows longer than 2048                         */
   uint32_t n_short;        /* rows of at most PLX_SEQ_ROW_MAX (incl. empty) */
+  uint32_t max_row;        /* connections in the longest row                */
 } plx_csr;
+/* plx_csr_plan fills every member except to_id (set to NULL) and row_base
+ * (set to 0). When the caller sets to_id (the dst-sorted ToId field, 16-byte
+ * aligned, consistent with row_ptr) and row_base, sweeps over CSRs whose rows
+ * all have at most PLX_SEQ_ROW_MAX connections run the register-resident
+ * warp kernel; otherwise the tile kernel. Results are identical. */
 
 /* Size (in u32 words) of the sweep plan for n_edges connections. */
 uint64_t plx_csr_plan_words(uint64_t n_edges, uint32_t n_rows);

@@ -36,9 +36,10 @@ class PlxError(RuntimeError):
 
 
 class Csr(ctypes.Structure):
-    _fields_ = [("row_ptr", c_void_p), ("plan", c_void_p), ("n_edges", c_uint64),
-                ("n_rows", c_uint32), ("n_wide", c_uint32), ("n_long", c_uint32),
-                ("n_short", c_uint32)]
+    _fields_ = [("row_ptr", c_void_p), ("plan", c_void_p), ("to_id", c_void_p),
+                ("n_edges", c_uint64), ("n_rows", c_uint32), ("row_base", c_uint32),
+                ("n_wide", c_uint32), ("n_long", c_uint32), ("n_short", c_uint32),
+                ("max_row", c_uint32)]
 
 
 class Field(ctypes.Structure):

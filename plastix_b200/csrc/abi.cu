@@ -48,8 +48,9 @@ extern "C" int plx_ctx_create(int device, void* stream, plx_ctx** out) {
   c->device = device;
   c->stream = static_cast<cudaStream_t>(stream);
   c->num_sms = prop.multiProcessorCount;
-  cudaError_t e = cudaMalloc(&c->d_status, sizeof(int32_t));
-  if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, sizeof(int32_t));
+  cudaError_t e = cudaMalloc(&c->d_status, 64);
+  if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, 64);
+  c->d_queue = reinterpret_cast<uint32_t*>(c->d_status + 4);
   if (e != cudaSuccess) {
     cudaFree(c->d_status);
     delete c;

@@ -166,5 +166,6 @@ struct plx_ctx {
   cudaStream_t stream = nullptr;
   int num_sms = 0;
   int32_t* d_status = nullptr;  // device word written by bounded waits
+  uint32_t* d_queue = nullptr;  // work counter of the warp sweeps (same allocation)
   uint64_t timeout_ns = 2000000000ull;
 };

@@ -44,6 +44,7 @@ constexpr uint32_t kPlanHdr = 8;
 // Plan layout (u32 words):
 //   [0] magic (0 when row_ptr failed validation)  [1] n_blocks
 //   [2] n_wide  [3] n_long  [4] n_short  [5] max_wide  [6] max_long
+//   [7] longest row (connections)
 //   [8 + 3b + 0]  first row f whose start >= b*kPlanG (b = n_blocks: n_rows)
 //   [8 + 3b + 1]  row_ptr[f-1]: start of the last row starting before b*kPlanG
 //   [8 + 3b + 2]  row_ptr[f]:   its end (0 and 0 when f == 0)
@@ -87,6 +88,10 @@ struct SweepArgs {
   float rate;
   int32_t* status;
   uint64_t timeout_ns;
+  const uint32_t* to_id;  // ToId field (warp fast path)
+  uint32_t row_base;      // unit id of row 0
+  uint32_t* queue;        // stripe work counter (warp fast path), zeroed
+  uint32_t only_long;     // warp fast path: run only if the longest row > 128
 };
 
 enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3 };
@@ -174,6 +179,9 @@ __global__ void k_plan_rows(const uint32_t* __restrict__ row_ptr,
   }
   const uint32_t m = __ballot_sync(0xffffffffu, is_short);
   if ((threadIdx.x & 31) == 0 && m) atomicAdd(&plan[4], (uint32_t)__popc(m));
+  uint32_t len = r < n_rows ? row_ptr[r + 1] - row_ptr[r] : 0u;
+  len = __reduce_max_sync(0xffffffffu, len);
+  if ((threadIdx.x & 31) == 0 && len) atomicMax(&plan[7], len);
 }
 
 // ---------------------------------------------------------------------------
@@ -402,6 +410,9 @@ __global__ void __launch_bounds__(L::NT) k_sweep(SweepArgs a) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_status(a.status, kStatusBadPlan);
     return;
   }
+  // Launched next to k_sweep_warp for a plan whose row counts the host does
+  // not know: the warp kernel does the work when there is no wide/long row.
+  if (a.to_id && plan[2] == 0 && plan[3] == 0) return;
   const uint64_t nb = plan[1];
   const uint64_t n_edges = a.n_edges;
   const uint32_t n_rows = a.n_rows;
@@ -760,6 +771,308 @@ __global__ void __launch_bounds__(L::NT) k_sweep(SweepArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Fast path for CSRs whose rows all have at most PLX_SEQ_ROW_MAX connections
+// (the plan lists no wide or long row): warp-autonomous and register
+// resident, no shared memory and no CTA barrier.
+//
+// Warps take row-aligned stripes (the rows starting in 16 plan blocks, ~4096
+// connections) from an atomic work queue and walk them in windows of 256
+// connections, 8 consecutive connections per lane loaded with 128-bit loads
+// (ToId, FromId, Weight, [Trace], [Dead]). Each row is folded strictly left
+// to right: lanes fold their own connections, and the running sum of a row
+// that spans lanes is chained from lane to lane with shuffles (one hop per
+// round, as many rounds as the longest chain in the window), so the sums are
+// bit-exact with the reference loop. The row that continues into the next
+// window carries its running sum across; its connections' update waits in
+// registers until the next window completes the row.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kStripeBlocks = 16;
+constexpr uint32_t kWin = 256;
+constexpr uint32_t kNone = 0xFFFFFFFFu;
+constexpr uint32_t kCont = 0xFFFFFFFEu;
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* base, uint32_t k0, uint64_t n, T (&v)[8]) {
+  static_assert(sizeof(T) == 4, "4-byte fields");
+  if ((uint64_t)k0 + 8 <= n) {
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(base + k0));
+    const uint4 y = __ldg(reinterpret_cast<const uint4*>(base + k0 + 4));
+    const uint32_t u[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const T*>(&u[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (uint64_t)k0 + j < n ? base[k0 + j] : T();
+  }
+}
+
+__device__ __forceinline__ void load8_u8(const uint8_t* base, uint32_t k0, uint64_t n,
+                                         uint8_t (&v)[8]) {
+  if ((uint64_t)k0 + 8 <= n && (k0 & 7u) == 0) {
+    const uint2 x = __ldg(reinterpret_cast<const uint2*>(base + k0));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j] = (uint8_t)(x.x >> (8 * j));
+      v[j + 4] = (uint8_t)(x.y >> (8 * j));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (uint64_t)k0 + j < n ? base[k0 + j] : (uint8_t)0;
+  }
+}
+
+// Stores the elements of `mask` (8 consecutive connections from k0).
+__device__ __forceinline__ void store8(float* base, uint32_t k0, uint32_t mask,
+                                       const float (&v)[8]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t m = (mask >> (4 * h)) & 0xFu;
+    if (m == 0xFu) {
+      *reinterpret_cast<float4*>(base + k0 + 4 * h) =
+          make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+    } else if (m) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if ((m >> c) & 1u) base[k0 + 4 * h + c] = v[4 * h + c];
+    }
+  }
+}
+
+// Folds s[q0, q1) (shared memory) into acc strictly left to right: scalar
+// head to the 16-byte boundary, float4 body loaded 16 vectors at a time,
+// scalar tail.
+__device__ __forceinline__ float fold_seg(const float* s, uint32_t q0, uint32_t q1,
+                                          float acc) {
+  uint32_t q = q0;
+  for (; q < q1 && (q & 3u); ++q) acc = __fadd_rn(acc, s[q]);
+  for (; q + 64 <= q1; q += 64) {
+    float4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = *reinterpret_cast<const float4*>(s + q + 4 * u);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      acc = __fadd_rn(acc, v[u].x);
+      acc = __fadd_rn(acc, v[u].y);
+      acc = __fadd_rn(acc, v[u].z);
+      acc = __fadd_rn(acc, v[u].w);
+    }
+  }
+  for (; q + 4 <= q1; q += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(s + q);
+    acc = __fadd_rn(acc, v.x);
+    acc = __fadd_rn(acc, v.y);
+    acc = __fadd_rn(acc, v.z);
+    acc = __fadd_rn(acc, v.w);
+  }
+  for (; q < q1; ++q) acc = __fadd_rn(acc, s[q]);
+  return acc;
+}
+
+template <int EPL, typename T>
+__device__ __forceinline__ void loadv(const T* base, uint32_t k0, uint64_t n, T (&v)[EPL]) {
+  if constexpr (EPL == 8) {
+    load8(base, k0, n, v);
+  } else {
+    static_assert(EPL == 4 && sizeof(T) == 4, "4 or 8 elements per lane");
+    if ((uint64_t)k0 + 4 <= n) {
+      const uint4 x = __ldg(reinterpret_cast<const uint4*>(base + k0));
+      const uint32_t u[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const T*>(&u[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (uint64_t)k0 + j < n ? base[k0 + j] : T();
+    }
+  }
+}
+
+template <int EPL>
+__device__ __forceinline__ void loadv_u8(const uint8_t* base, uint32_t k0, uint64_t n,
+                                         uint8_t (&v)[EPL]) {
+  if constexpr (EPL == 8) {
+    load8_u8(base, k0, n, v);
+  } else {
+    if ((uint64_t)k0 + 4 <= n && (k0 & 3u) == 0) {
+      const uint32_t x = __ldg(reinterpret_cast<const uint32_t*>(base + k0));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (uint8_t)(x >> (8 * j));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (uint64_t)k0 + j < n ? base[k0 + j] : (uint8_t)0;
+    }
+  }
+}
+
+template <int EPL>
+__device__ __forceinline__ void storev(float* base, uint32_t k0, uint32_t mask,
+                                       const float (&v)[EPL]) {
+  if constexpr (EPL == 8) {
+    store8(base, k0, mask, v);
+  } else {
+    if ((mask & 0xFu) == 0xFu) {
+      *reinterpret_cast<float4*>(base + k0) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if (mask) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if ((mask >> c) & 1u) base[k0 + c] = v[c];
+    }
+  }
+}
+
+// Warp-tile sweep. Each warp takes a row-aligned tile (the rows that start in
+// kTileBlocks consecutive plan blocks, at most kTileCap connections because
+// every row has at most PLX_SEQ_ROW_MAX) from an atomic queue and runs three
+// phases on it with only __syncwarp between them:
+//   1  coalesced 128-bit loads of FromId/Weight (4 consecutive connections per
+//      lane per step), gathers of act[FromId], products w*act and activations
+//      staged in the warp's shared memory;
+//   2  one lane per row folds the row's products strictly left to right
+//      (bit-exact with the reference), runs Apply, writes the row output and
+//      writes the row value over the row's products;
+//   3  (update) coalesced reloads of Weight/Trace, trace/weight update from
+//      the staged activation and row value, coalesced stores.
+template <uint32_t TB, int KB, int NW>
+struct WTileCfg {
+  static constexpr uint32_t kTileBlocks = TB;                        // plan blocks per tile
+  static constexpr uint32_t kTileCap = TB * kPlanG + kSeqMax + 8;    // connections
+  static constexpr uint32_t kTileVec = (kTileCap + 127) / 128;       // 4-wide steps
+  static constexpr int kB = KB;            // 4-wide steps in flight per lane (phase 1)
+  static constexpr int kWarpsPerCta = NW;
+  static constexpr size_t smem(bool upd) {
+    return (upd ? 2 : 1) * (size_t)NW * kTileVec * 128 * sizeof(float);
+  }
+};
+
+template <class C, int APPLY, bool UPD, bool DEAD>
+__global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs a) {
+  constexpr uint32_t kTileBlocks = C::kTileBlocks;
+  constexpr uint32_t kTileVec = C::kTileVec;
+  constexpr int kWarpsPerCta = C::kWarpsPerCta;
+  // per warp: products, then row values; (update) staged activations
+  extern __shared__ __align__(16) float s_tile[];
+  constexpr uint32_t kStride = kTileVec * 128;
+  const uint32_t* __restrict__ plan = a.plan;
+  // Only for plans whose rows are all short (the tile kernel handles others).
+  if (plan[0] != kPlanMagic || plan[2] != 0 || plan[3] != 0) return;
+  const uint64_t nb = plan[1];
+  const uint32_t n_tiles = (uint32_t)((nb + kTileBlocks - 1) / kTileBlocks);
+  const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+  float* sp = s_tile + wid * kStride;
+  float* sa = s_tile + (kWarpsPerCta + wid) * kStride;  // used only by update sweeps
+  const uint64_t n = a.n_edges;
+  const uint32_t len1 = a.act_src_len - 1u;
+  bool bad = false;
+  for (;;) {
+    uint32_t t = 0;
+    if (lane == 0) t = atomicAdd(a.queue, 1u);
+    t = __shfl_sync(kFull, t, 0);
+    if (t >= n_tiles) break;
+    const uint32_t b0 = t * kTileBlocks;
+    const uint32_t b1 = (uint32_t)min_u64((uint64_t)b0 + kTileBlocks, nb);
+    const uint32_t* P0 = plan + kPlanHdr + 3 * b0;
+    const uint32_t* P1 = plan + kPlanHdr + 3 * b1;
+    const uint32_t f0 = P0[0], f1 = P1[0];
+    const uint32_t lo = P0[2], hi = P1[2];  // row_ptr[f0], row_ptr[f1]
+    const uint32_t base = lo & ~3u;
+    const uint32_t nv = (hi - base + 127) / 128;  // 4-wide steps of the warp
+
+    // ---- 1: stream, gather, stage (kB 4-wide steps in flight per lane) ----
+    constexpr int kB = C::kB;
+    for (uint32_t v0 = 0; v0 < nv; v0 += kB) {
+      uint32_t sid[kB][4];
+      float w[kB][4];
+      uint8_t dd[kB][4];
+#pragma unroll
+      for (int h = 0; h < kB; ++h) {
+        const uint32_t k = base + 128 * (v0 + h) + 4 * lane;
+        if (v0 + h < nv) {
+          loadv<4>(a.src, k, n, sid[h]);
+          loadv<4>(a.w_in, k, n, w[h]);
+          if constexpr (DEAD) loadv_u8<4>(a.dead, k, n, dd[h]);
+        }
+      }
+      float av[kB][4];
+      uint32_t smax = 0;
+#pragma unroll
+      for (int h = 0; h < kB; ++h) {
+        const uint32_t k = base + 128 * (v0 + h) + 4 * lane;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const bool in = v0 + h < nv && k + c >= lo && k + c < hi;
+          const uint32_t sj = in ? sid[h][c] : 0u;
+          smax = max(smax, sj);
+          av[h][c] = __ldg(a.act_src + min(sj, len1));
+        }
+      }
+      bad |= smax > len1;
+#pragma unroll
+      for (int h = 0; h < kB; ++h) {
+        if (v0 + h >= nv) continue;
+        const uint32_t k = base + 128 * (v0 + h) + 4 * lane;
+        float pv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          bool live = k + c >= lo && k + c < hi;
+          if constexpr (DEAD) live = live && !dd[h][c];
+          pv[c] = live ? __fmul_rn(w[h][c], av[h][c]) : 0.0f;
+        }
+        const uint32_t q = 128 * (v0 + h) + 4 * lane;
+        *reinterpret_cast<float4*>(sp + q) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+        if constexpr (UPD)
+          *reinterpret_cast<float4*>(sa + q) =
+              make_float4(av[h][0], av[h][1], av[h][2], av[h][3]);
+      }
+    }
+    __syncwarp();
+
+    // ---- 2: one lane per row ----
+    for (uint32_t r = f0 + lane; r < f1; r += 32) {
+      const uint32_t rs = a.row_ptr[r], re = a.row_ptr[r + 1];
+      const float acc = fold_seg(sp, rs - base, re - base, 0.0f);
+      const float post = apply_row<APPLY>(acc, r, a, true);
+      if constexpr (UPD) fill_range(sp, rs - base, re - base, post);
+    }
+
+    if constexpr (UPD) {
+      __syncwarp();
+      // ---- 3: per-connection update ----
+#pragma unroll 4
+      for (uint32_t v = 0; v < nv; ++v) {
+        const uint32_t k = base + 128 * v + 4 * lane;
+        const uint32_t q = 128 * v + 4 * lane;
+        float w[4], e[4];
+        uint8_t dd[4];
+        loadv<4>(a.w_in, k, n, w);
+        loadv<4>(a.e_in, k, n, e);
+        if constexpr (DEAD) loadv_u8<4>(a.dead, k, n, dd);
+        const float4 av = *reinterpret_cast<const float4*>(sa + q);
+        const float4 ps = *reinterpret_cast<const float4*>(sp + q);
+        const float avv[4] = {av.x, av.y, av.z, av.w};
+        const float pst[4] = {ps.x, ps.y, ps.z, ps.w};
+        uint32_t m = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const bool in = k + c >= lo && k + c < hi;
+          m |= (uint32_t)in << c;
+          bool live = in;
+          if constexpr (DEAD) live = live && !dd[c];
+          if (live) {
+            const float ne = __fadd_rn(__fmul_rn(a.decay, e[c]), __fmul_rn(avv[c], pst[c]));
+            e[c] = ne;
+            w[c] = __fadd_rn(w[c], __fmul_rn(a.rate, ne));
+          }
+        }
+        storev<4>(a.w_out, k, m, w);
+        storev<4>(a.e_out, k, m, e);
+      }
+    }
+    __syncwarp();  // the next tile overwrites the staged values
+  }
+  if (bad) record_status(a.status, kStatusBadIndex);
+}
+
+// ---------------------------------------------------------------------------
 // Host launch helpers
 // ---------------------------------------------------------------------------
 template <class L, bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
@@ -789,6 +1102,42 @@ static int sweep_cfg() {
   return cfg;
 }
 
+template <class C, int APPLY, bool UPD, bool DEAD>
+int launch_wtile(plx_ctx* ctx, const SweepArgs& args) {
+  auto kern = k_sweep_wtile<C, APPLY, UPD, DEAD>;
+  const size_t smem = C::smem(UPD);
+  PLX_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem));
+  int per_sm = 0;
+  PLX_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern,
+                                                             C::kWarpsPerCta * 32, smem));
+  if (per_sm < 1) per_sm = 1;
+  const uint64_t nb = plan_blocks(args.n_edges);
+  const uint64_t tiles = (nb + C::kTileBlocks - 1) / C::kTileBlocks;
+  const uint64_t grid = std::min<uint64_t>((tiles + C::kWarpsPerCta - 1) / C::kWarpsPerCta,
+                                           (uint64_t)ctx->num_sms * per_sm);
+  PLX_TRY_CUDA(cudaMemsetAsync(ctx->d_queue, 0, sizeof(uint32_t), ctx->stream));
+  SweepArgs wa = args;
+  wa.queue = ctx->d_queue;
+  kern<<<(unsigned)std::max<uint64_t>(grid, 1), C::kWarpsPerCta * 32, smem, ctx->stream>>>(wa);
+  PLX_LAUNCH_CHECK("k_sweep_wtile");
+  return PLX_OK;
+}
+
+static int sweep_cfg();
+
+template <int APPLY, bool UPD, bool DEAD>
+int launch_warp(plx_ctx* ctx, const SweepArgs& args, uint32_t max_row) {
+  (void)max_row;
+  switch (sweep_cfg()) {
+    case 1: return launch_wtile<WTileCfg<4, 6, 8>, APPLY, UPD, DEAD>(ctx, args);
+    case 2: return launch_wtile<WTileCfg<4, 8, 8>, APPLY, UPD, DEAD>(ctx, args);
+    case 3: return launch_wtile<WTileCfg<4, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
+    case 4: return launch_wtile<WTileCfg<8, 4, 8>, APPLY, UPD, DEAD>(ctx, args);
+    default: return launch_wtile<WTileCfg<4, 4, 8>, APPLY, UPD, DEAD>(ctx, args);
+  }
+}
+
 template <bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
 int launch_sweep(plx_ctx* ctx, const SweepArgs& args, const plx_csr* csr) {
   constexpr bool U = UPD != kUpdNone;
@@ -810,23 +1159,35 @@ int launch_sweep(plx_ctx* ctx, const SweepArgs& args, const plx_csr* csr) {
   }
   // A forward-only sweep with no short row is complete after the row kernels.
   if (!U && csr->n_short == 0) return PLX_OK;
+  const bool unknown = csr->n_wide == PLX_COUNT_UNKNOWN || csr->n_long == PLX_COUNT_UNKNOWN;
+  const bool all_short = !unknown && csr->n_wide == 0 && csr->n_long == 0;
+  if (args.to_id && (all_short || unknown) &&
+      (UPD == kUpdNone || UPD == kUpdHebbTrace)) {
+    if (int rc = launch_warp<APPLY, UPD == kUpdHebbTrace, DEAD>(ctx, args, csr->max_row))
+      return rc;
+    if (all_short) return PLX_OK;
+    // unknown counts: the tile kernel below runs only if the plan has wide rows
+  }
+  SweepArgs targs = args;
+  if (!(args.to_id && unknown && (UPD == kUpdNone || UPD == kUpdHebbTrace))) targs.to_id = nullptr;
   switch (sweep_cfg()) {
     case 1:
-      return launch_tiles<SweepLayout<1024, 4, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+      return launch_tiles<SweepLayout<1024, 4, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
     case 2:
-      return launch_tiles<SweepLayout<2048, 3, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+      return launch_tiles<SweepLayout<2048, 3, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
     case 3:
-      return launch_tiles<SweepLayout<512, 3, 2, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+      return launch_tiles<SweepLayout<512, 3, 2, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
     case 4:
-      return launch_tiles<SweepLayout<512, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+      return launch_tiles<SweepLayout<512, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
     default:
-      return launch_tiles<SweepLayout<1024, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, args);
+      return launch_tiles<SweepLayout<1024, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
   }
 }
 
 static int validate_csr(const plx_csr* csr) {
   PLX_CHECK_ARG(csr && csr->row_ptr && csr->plan, "csr, row_ptr and plan are required");
   PLX_CHECK_ARG(aligned16(csr->row_ptr), "row_ptr must be 16-byte aligned");
+  PLX_CHECK_ARG(aligned16(csr->to_id), "to_id must be 16-byte aligned");
   PLX_CHECK_ARG(csr->n_edges < 0xFFFF0000ull,
                 "n_edges must be < 2^32 - 2^16 per sweep (split larger layers)");
   return PLX_OK;
@@ -840,6 +1201,8 @@ static SweepArgs base_args(plx_ctx* ctx, const plx_csr* csr) {
   a.n_rows = csr->n_rows;
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
+  a.to_id = csr->to_id;
+  a.row_base = csr->row_base;
   return a;
 }
 
@@ -928,6 +1291,9 @@ static int csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
       out->n_wide = PLX_COUNT_UNKNOWN;
       out->n_long = PLX_COUNT_UNKNOWN;
       out->n_short = PLX_COUNT_UNKNOWN;
+      out->to_id = nullptr;
+      out->row_base = 0;
+      out->max_row = PLX_COUNT_UNKNOWN;
     }
     return PLX_OK;
   }
@@ -947,6 +1313,9 @@ static int csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
     out->n_wide = hdr[2];
     out->n_long = hdr[3];
     out->n_short = hdr[4];
+    out->to_id = nullptr;
+    out->row_base = 0;
+    out->max_row = hdr[7];
   }
   return PLX_OK;
 }

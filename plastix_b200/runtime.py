@@ -70,12 +70,20 @@ class DstCsr:
     """CSR index over connections sorted by ToId: rows are the destination
     units [row_base, row_base + n_rows)."""
 
-    def __init__(self, ctx: Context, to_id: torch.Tensor, row_base: int, n_rows: int):
+    def __init__(self, ctx: Context, to_id: torch.Tensor, row_base: int, n_rows: int,
+                 *, use_to_id: bool = True):
         n_edges = int(to_id.numel())
         self.row_ptr = torch.empty(n_rows + 1, dtype=torch.int32, device=ctx.device)
         call("plx_csr_row_ptr", ctx.handle, c_void_p(_ptr(to_id) if n_edges else None),
              n_edges, row_base, n_rows, c_void_p(_ptr(self.row_ptr)))
         self._init_plan(ctx, n_edges, n_rows)
+        self.set_to_id(to_id if use_to_id else None, row_base)
+
+    def set_to_id(self, to_id: Optional[torch.Tensor], row_base: int) -> None:
+        """Enables the warp fast path (needs the dst-sorted ToId field)."""
+        self.to_id = to_id
+        self.struct.to_id = _ptr(to_id) if to_id is not None and to_id.numel() else None
+        self.struct.row_base = row_base
 
     @classmethod
     def from_sorted_async(cls, ctx: Context, to_id: torch.Tensor, row_base: int,
@@ -100,6 +108,7 @@ class DstCsr:
              c_void_p(_ptr(self.plan)), words, byref(self.struct))
         self.n_edges, self.n_rows = n_edges, n_rows
         self.n_wide = self.n_long = self.n_short = _abi.COUNT_UNKNOWN
+        self.set_to_id(to_id, row_base)
         return self
 
     @classmethod
@@ -109,6 +118,7 @@ class DstCsr:
         n_rows = int(self.row_ptr.numel()) - 1
         n_edges = int(self.row_ptr[-1].item())
         self._init_plan(ctx, n_edges, n_rows)
+        self.set_to_id(None, 0)
         return self
 
     def _init_plan(self, ctx: Context, n_edges: int, n_rows: int) -> None:
@@ -162,7 +172,8 @@ class HebbianSweepLayer:
     def __init__(self, ctx: Context, n_src: int, n_dst: int, from_id: torch.Tensor,
                  to_id: torch.Tensor, weight: torch.Tensor,
                  trace: Optional[torch.Tensor] = None, *, decay: float = 0.9,
-                 rate: float = 1e-3, dead: Optional[torch.Tensor] = None):
+                 rate: float = 1e-3, dead: Optional[torch.Tensor] = None,
+                 fast: bool = True):
         dev = ctx.device
         self.ctx = ctx
         self.n_src, self.n_dst = n_src, n_dst
@@ -177,7 +188,7 @@ class HebbianSweepLayer:
             trace.to(dev, torch.float32).contiguous().clone()
         self._e = [tr, torch.empty(n, dtype=torch.float32, device=dev)]
         self._cur = 0
-        self.csr = DstCsr(ctx, self.to_id, n_src, n_dst)
+        self.csr = DstCsr(ctx, self.to_id, n_src, n_dst, use_to_id=fast)
         self.act_dst = torch.zeros(n_dst, dtype=torch.float32, device=dev)
 
     @property

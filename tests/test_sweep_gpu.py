@@ -42,10 +42,10 @@ def assert_rows(got, want, row_len, exact_ok=True):
     np.testing.assert_allclose(got[~short], want[~short], rtol=RTOL, atol=ATOL)
 
 
-def run_hebbian(ctx, L, sweeps, decay=0.9, rate=1e-3, dead=None):
+def run_hebbian(ctx, L, sweeps, decay=0.9, rate=1e-3, dead=None, fast=True):
     layer = HebbianSweepLayer(ctx, L.n_src, L.n_dst, ids(L.from_id), ids(L.to_id),
                               dev(L.weight), dev(L.trace), decay=decay, rate=rate,
-                              dead=None if dead is None else dev(dead))
+                              dead=None if dead is None else dev(dead), fast=fast)
     act = dev(L.act_in)
     for _ in range(sweeps):
         out = layer.step(act)
@@ -67,9 +67,10 @@ def oracle_hebbian(orc, L, sweeps, decay=0.9, rate=1e-3, dead=None):
     (8, 3, 7, 4),                 # fewer edges than one bulk vector
     (1 << 14, 1 << 10, 1 << 16, 5),
 ])
-def test_fused_hebbian_bit_exact(ctx, orc, n_src, n_dst, n_edges, seed):
+@pytest.mark.parametrize("fast", [True, False])
+def test_fused_hebbian_bit_exact(ctx, orc, n_src, n_dst, n_edges, seed, fast):
     L = workloads.sparse_layer(n_src, n_dst, n_edges, seed=seed)
-    got = run_hebbian(ctx, L, sweeps=4)
+    got = run_hebbian(ctx, L, sweeps=4, fast=fast)
     want = oracle_hebbian(orc, L, sweeps=4)
     for g, w in zip(got, want):
         np.testing.assert_array_equal(g, w)
@@ -86,16 +87,20 @@ def test_fused_hebbian_golden_fixture(ctx):
     np.testing.assert_array_equal(a, fx["act"])
 
 
-def test_fused_hebbian_dead_connections(ctx, orc):
+@pytest.mark.parametrize("fast", [True, False])
+def test_fused_hebbian_dead_connections(ctx, orc, fast):
     L = workloads.sparse_layer(3000, 500, 40000, seed=11)
     dead = (np.random.default_rng(3).random(L.from_id.size) < 0.2).astype(np.uint8)
-    got = run_hebbian(ctx, L, 3, dead=dead)
+    got = run_hebbian(ctx, L, 3, dead=dead, fast=fast)
     want = oracle_hebbian(orc, L, 3, dead=dead)
     for g, w in zip(got, want):
         np.testing.assert_array_equal(g, w)
 
 
 @pytest.mark.parametrize("lens", [
+    [256] * 30 + [1, 255, 0, 254, 3] * 20,            # rows at the short-row limit
+    [0] * 50 + [7] * 3000 + [0] * 50,                 # empty rows at both stripe ends
+    [64, 0, 0, 128, 1] * 4000,                        # many stripes, mixed lengths
     [0, 0, 5, 0, 3000, 0, 1, 2047, 2048, 2049, 0],   # wide + long rows, empty rows
     [257] * 40 + [256] * 40,                          # warp rows vs thread rows
     [10000],                                          # one long row (many tiles)
@@ -117,8 +122,9 @@ def test_row_shapes(ctx, orc, lens):
 @pytest.mark.parametrize("apply", [_abi.APPLY_IDENTITY, _abi.APPLY_SIGMOID,
                                    _abi.APPLY_TANH, _abi.APPLY_IPC_ERROR])
 @pytest.mark.parametrize("with_dead", [False, True])
-def test_forward_apply_kinds(ctx, orc, apply, with_dead):
-    L = workloads.sparse_layer_rows(5000, list(np.random.default_rng(9).integers(0, 300, 900)),
+@pytest.mark.parametrize("max_len", [300, 257])
+def test_forward_apply_kinds(ctx, orc, apply, with_dead, max_len):
+    L = workloads.sparse_layer_rows(5000, list(np.random.default_rng(9).integers(0, max_len, 900)),
                                     seed=21)
     dead = (np.random.default_rng(4).random(L.from_id.size) < 0.1).astype(np.uint8) \
         if with_dead else None
