@@ -254,6 +254,47 @@ int plx_regrow(plx_ctx* ctx, uint64_t n, const uint64_t* count,
                uint32_t src_base, uint32_t n_src, uint32_t dst_base,
                uint32_t n_dst, uint64_t seed, uint64_t step_base);
 
+/* ---- SwiftTD (examples/swifttd/swifttd.cpp) ------------------------------ */
+
+/* Number of per-feature SoA fields, in the reference's ExtraConnFields order
+ * (swifttd.cpp:199-209): W, Z, ZDelta, DeltaW, H, HOld, HTemp, ZBar, P, Beta. */
+#define PLX_TD_NUM_FIELDS 10
+
+/* The network's globals (swifttd.cpp:47-62), in DEVICE memory: the six
+ * hyperparameters (the caller sets them; the reference fixes them as member
+ * initialisers) and the seven running values (start at zero). */
+typedef struct plx_td_globals {
+  float gamma, lambda, eta, eta_min, decay, meta;
+  float v, v_old, delta, v_delta_prev, v_delta, tau, b;
+} plx_td_globals;
+
+/* Scratch for plx_swifttd_step with up to max_active active features. */
+uint64_t plx_swifttd_scratch_bytes(uint64_t n_features, uint32_t max_active);
+
+/* One Network::DoStep of the SwiftTD network (plastix.hpp:439-455 with the
+ * swifttd.cpp policies): DoForwardPass (V = sum W*F, swifttd.cpp:74-85), Loss
+ * (:90-100), the UpdateIncoming sweep (phase 1, :106-150), the UpdateOutgoing
+ * sweep (phase 2, :152-186), ResetGlobal (:189-191).
+ *   fields:     host array of PLX_TD_NUM_FIELDS device pointers, n_features
+ *               floats each, 16-byte aligned; updated in place.
+ *   active_idx: the features with F != 0, strictly increasing, < n_features
+ *               (an unsorted or out-of-range list is reported by
+ *               plx_ctx_sync as PLX_ERR_ARG); active_val their values, or
+ *               NULL for binary features (all 1.0). Inactive features have
+ *               F = 0 and still take the full update, as in the reference.
+ *   reward:     DEVICE pointer to this step's reward (Targets[0]).
+ *   v_out:      optional DEVICE pointer receiving V (GetOutput()[0]).
+ *   scratch:    plx_swifttd_scratch_bytes(n_features, >= n_active) bytes,
+ *               zero-filled before the first step; each step leaves it ready
+ *               for the next.
+ * V, Tau, B and VDelta are summed in double precision in a fixed order
+ * (deterministic); the reference sums them sequentially in float. */
+int plx_swifttd_step(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+                     const uint32_t* active_idx, const float* active_val,
+                     uint32_t n_active, const float* reward,
+                     plx_td_globals* globals, float* v_out, void* scratch,
+                     uint64_t scratch_bytes);
+
 #ifdef __cplusplus
 }
 #endif

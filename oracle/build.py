@@ -6,7 +6,8 @@
   ``-std=c++20 -O2`` build.
 * ``oracle/_ref/libplx_ref.so`` — the reference itself: its headers
   compiled from the reference tree (``/root/reference/include``) together with
-  ``oracle/ref_harness.cpp``. Only when the reference tree is present (it is
+  ``oracle/ref_harness.cpp`` (which also compiles the reference's
+  ``examples/swifttd/swifttd.cpp`` unchanged, its ``main`` renamed). Only when the reference tree is present (it is
   not on the GPU machines, which use the prebuilt file). The one change to the
   reference sources: the fixed capacities ``UnitAlloc(4096), ConnAlloc(4096 *
   4)`` of ``include/plastix/plastix.hpp`` become calls into the harness, so
@@ -54,7 +55,8 @@ def build_reference() -> Path | None:
     if not hpp.exists():
         return REF_SO if REF_SO.exists() else None
     harness = HERE / "ref_harness.cpp"
-    deps = [harness, Path(__file__)] + sorted((REF_ROOT / "include" / "plastix").glob("*.hpp"))
+    deps = ([harness, Path(__file__), REF_ROOT / "examples" / "swifttd" / "swifttd.cpp"]
+            + sorted((REF_ROOT / "include" / "plastix").glob("*.hpp")))
     if not _stale(REF_SO, deps):
         return REF_SO
     REF_DIR.mkdir(exist_ok=True)
@@ -72,7 +74,8 @@ def build_reference() -> Path | None:
                            "std::size_t plx_ref_unit_capacity();\n"
                            "std::size_t plx_ref_conn_capacity();\n")
         cmd = ["g++", "-std=c++20", "-O2", "-fPIC", "-shared", "-pthread",
-               "-include", str(prelude), f"-I{inc}", str(harness),
+               "-include", str(prelude), f"-I{inc}", f"-I{REF_ROOT / 'examples' / 'swifttd'}",
+               str(harness),
                str(REF_ROOT / "src" / "plastix.cpp"), "-o", str(REF_SO)]
         subprocess.run(cmd, check=True)
     return REF_SO

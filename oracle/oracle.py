@@ -59,6 +59,9 @@ def orc() -> ctypes.CDLL:
                                     c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,
                                     c_uint64, c_uint64]
         L.oracle_keep_abs_ge.argtypes = [c_void_p, c_uint64, c_float, c_void_p]
+        L.oracle_swifttd_step.argtypes = [c_uint64, c_void_p, c_void_p, c_float, c_void_p,
+                                          c_int]
+        L.oracle_swifttd_step.restype = c_float
         _orc = L
     return _orc
 
@@ -77,6 +80,8 @@ def ref() -> Optional[ctypes.CDLL]:
         L.ref_sweep_shards_create.restype = c_void_p
         L.ref_sweep_shards_step.argtypes = [c_void_p, c_void_p]
         L.ref_sweep_shards_destroy.argtypes = [c_void_p]
+        L.ref_swifttd_example_run.argtypes = [c_uint64, c_void_p, c_void_p, c_int, c_float,
+                                              c_void_p, c_void_p]
         _ref = L
     return _ref
 
@@ -208,3 +213,59 @@ def structural_step(from_id, to_id, w, age, n_src, n_dst, thr, seed, step_base):
     f, t, ww, aa = regrow(f, t, ww, aa, m, 0, n_src, n_src, n_dst, seed, step_base)
     order = stable_sort_perm_u32(t - np.uint32(n_src))
     return gather(order, f), gather(order, t), gather(order, ww), gather(order, aa), m
+
+
+# ---------------------------------------------------------------------------
+# SwiftTD (examples/swifttd/swifttd.cpp)
+# ---------------------------------------------------------------------------
+TD_FIELDS = ("w", "z", "z_delta", "delta_w", "h", "h_old", "h_temp", "z_bar", "p", "beta")
+TD_GLOBALS = ("gamma", "lambda", "eta", "eta_min", "decay", "meta",
+              "v", "v_old", "delta", "v_delta_prev", "v_delta", "tau", "b")
+
+
+def td_globals(gamma=0.99, lambda_=0.9, eta=0.05, eta_min=1e-7, decay=0.999, meta=1e-3):
+    """A 13-float globals record: hyperparameters, then V, VOld, Delta,
+    VDeltaPrev, VDelta, Tau, B (all zero)."""
+    g = np.zeros(len(TD_GLOBALS), np.float32)
+    g[:6] = (gamma, lambda_, eta, eta_min, decay, meta)
+    return g
+
+
+def td_fields(n, alpha_init=0.05):
+    """Initial connection fields as SwiftTDConnInit leaves them: all zero but
+    Beta = log(alpha_init) (computed in single precision like std::log on a
+    float)."""
+    f = np.zeros((len(TD_FIELDS), n), np.float32)
+    f[9] = np.float32(np.log(np.float64(np.float32(alpha_init))))
+    return f
+
+
+def swifttd_step(fields, features, reward, globals_, acc_f64=False):
+    """One DoStep of the SwiftTD network, in place on fields (10 x n float32,
+    C order) and globals_ (13 float32). Returns V."""
+    assert fields.dtype == np.float32 and fields.flags["C_CONTIGUOUS"]
+    assert globals_.dtype == np.float32 and globals_.size == len(TD_GLOBALS)
+    n = fields.shape[1]
+    rows = (c_void_p * 10)(*[fields[i].ctypes.data for i in range(10)])
+    f = np.ascontiguousarray(features, np.float32)
+    assert f.size == n
+    return orc().oracle_swifttd_step(n, ctypes.cast(rows, c_void_p), _p(f), float(reward),
+                                     _p(globals_), int(acc_f64))
+
+
+def ref_swifttd_example_run(features, rewards, alpha_init=0.05):
+    """The reference's own SwiftTD example network (Gamma 1.0 as that file
+    fixes it) stepped over features (steps x n) and rewards. Returns
+    (fields 10 x n, V per step)."""
+    L = ref()
+    if L is None:
+        raise FileNotFoundError(f"{REF_SO} was not built")
+    feats = np.ascontiguousarray(features, np.float32)
+    steps, n = feats.shape
+    rw = np.ascontiguousarray(rewards, np.float32)
+    fields = np.empty((len(TD_FIELDS), n), np.float32)
+    v = np.empty(steps, np.float32)
+    if L.ref_swifttd_example_run(n, _p(feats), _p(rw), steps, alpha_init, _p(fields),
+                                 _p(v)) != 0:
+        raise RuntimeError("ref_swifttd_example_run failed")
+    return fields, v

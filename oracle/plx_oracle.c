@@ -10,7 +10,7 @@
  * rounding: built with -O2 -ffp-contract=off on x86-64 (SSE, no FMA), as the
  * reference is. Parity of this restatement with the reference itself is pinned
  * by tests/test_oracle_pins.py against oracle/_ref (the reference headers
- * compiled by oracle/build_ref.py) and the committed fixtures in tests/golden/.
+ * compiled by oracle/build.py) and the committed fixtures in tests/golden/.
  */
 #include <math.h>
 #include <stdint.h>
@@ -217,4 +217,102 @@ void oracle_regrow(uint64_t n, uint64_t count, uint32_t* from, uint32_t* to,
  * (ShouldPrune = |w| < threshold, plastix.hpp:290-293): keep = !(|w| < thr). */
 void oracle_keep_abs_ge(const float* w, uint64_t n, float thr, uint8_t* keep) {
   for (uint64_t c = 0; c < n; ++c) keep[c] = !(fabsf(w[c]) < thr);
+}
+
+/* ---- SwiftTD (examples/swifttd/swifttd.cpp:47-191) ---------------------- */
+
+/* Globals of the SwiftTD network (swifttd.cpp:47-62): six hyperparameters,
+ * then the seven running values. The device code uses the same layout. */
+typedef struct {
+  float gamma, lambda, eta, eta_min, decay, meta;
+  float v, v_old, delta, v_delta_prev, v_delta, tau, b;
+} oracle_td_globals;
+
+/* One Network::DoStep of the SwiftTD network: N features (units 0..N-1) feed
+ * one value unit over connections 0..N-1. fld[10] = W, Z, ZDelta, DeltaW, H,
+ * HOld, HTemp, ZBar, P, Beta (swifttd.cpp:199-209 field order). The step is
+ * DoForwardPass (V = W.F folded in connection order, Apply stores V,
+ * swifttd.cpp:74-85), Loss (:90-100), the UpdateIncoming sweep over all
+ * connections (phase 1, :106-150), the UpdateOutgoing sweep (phase 2,
+ * :152-186) and ResetGlobal (:189-191); plastix.hpp:232-256 runs the two
+ * sweeps in connection order.
+ *
+ * acc_f64 = 0 folds V, Tau, B and VDelta in fp32 in connection order, exactly
+ * as the reference. acc_f64 = 1 folds the same fp32 terms in double and rounds
+ * once: the parallel device reductions are compared against this form, since
+ * a sequential fp32 sum over ~2e4 terms carries its own rounding error of
+ * order 1e-5. Returns V. */
+float oracle_swifttd_step(uint64_t n, float** fld, const float* f, float reward,
+                          oracle_td_globals* g, int acc_f64) {
+  float *W = fld[0], *Z = fld[1], *Zd = fld[2], *Dw = fld[3], *H = fld[4];
+  float *HOld = fld[5], *HTemp = fld[6], *ZBar = fld[7], *P = fld[8], *Beta = fld[9];
+  float acc = 0.0f;
+  double acc_d = 0.0;
+  for (uint64_t i = 0; i < n; ++i) {
+    const float t = W[i] * f[i];
+    acc = acc + t;
+    acc_d += (double)t;
+  }
+  g->v = acc_f64 ? (float)acc_d : acc;
+  g->delta = reward + g->gamma * g->v - g->v_old;
+  g->v_delta_prev = g->v_delta;
+  g->v_delta = 0.0f;
+  g->tau = 0.0f;
+  g->b = 0.0f;
+  double tau_d = 0.0, b_d = 0.0, vd_d = 0.0;
+  for (uint64_t i = 0; i < n; ++i) {
+    const float F = f[i];
+    Dw[i] = g->delta * Z[i] - Zd[i] * g->v_delta_prev;
+    W[i] += Dw[i];
+    Beta[i] += g->meta / expf(Beta[i]) * (g->delta - g->v_delta_prev) * P[i];
+    float eb = expf(Beta[i]);
+    if (eb > g->eta || isinf(eb)) {
+      Beta[i] = logf(g->eta);
+      eb = g->eta;
+    }
+    if (eb < g->eta_min) {
+      Beta[i] = logf(g->eta_min);
+      eb = g->eta_min;
+    }
+    HOld[i] = H[i];
+    H[i] = HTemp[i] + g->delta * ZBar[i] - Zd[i] * g->v_delta_prev;
+    HTemp[i] = H[i];
+    Zd[i] = 0.0f;
+    const float td = g->gamma * g->lambda;
+    Z[i] *= td;
+    P[i] *= td;
+    ZBar[i] *= td;
+    const float t_tau = eb * F * F, t_b = Z[i] * F;
+    g->tau += t_tau;
+    g->b += t_b;
+    tau_d += (double)t_tau;
+    b_d += (double)t_b;
+  }
+  if (acc_f64) {
+    g->tau = (float)tau_d;
+    g->b = (float)b_d;
+  }
+  for (uint64_t i = 0; i < n; ++i) {
+    const float F = f[i];
+    const float t_vd = Dw[i] * F;
+    g->v_delta += t_vd;
+    vd_d += (double)t_vd;
+    float mult = 1.0f;
+    if (g->tau > 0.0f && g->eta / g->tau < 1.0f) mult = g->eta / g->tau;
+    Zd[i] = mult * expf(Beta[i]) * F;
+    Z[i] += Zd[i] * (1.0f - g->b);
+    P[i] += HOld[i] * F;
+    ZBar[i] += Zd[i] * (1.0f - g->b - ZBar[i] * F);
+    HTemp[i] = H[i] - HOld[i] * F * (Z[i] - Zd[i]) - H[i] * Zd[i] * F;
+    if (g->tau > g->eta) {
+      HTemp[i] = 0.0f;
+      H[i] = 0.0f;
+      HOld[i] = 0.0f;
+      ZBar[i] = 0.0f;
+      Beta[i] += logf(g->decay) * F * F;
+    }
+  }
+  if (acc_f64) g->v_delta = (float)vd_d;
+  g->v_old = g->v;
+  return g->v;
 }

@@ -1,5 +1,5 @@
 // ref_harness.cpp — drives the REFERENCE implementation (its own headers,
-// compiled from the reference tree by oracle/build_ref.py) on arrays handed
+// compiled from the reference tree by oracle/build.py) on arrays handed
 // over from Python, so the oracle restatement and the CPU baseline can be
 // checked against the reference itself.
 //
@@ -91,6 +91,7 @@ struct SweepShard {
 
 }  // namespace
 
+
 extern "C" {
 
 const char *ref_version() { return plastix::version(); }
@@ -169,3 +170,46 @@ void ref_sweep_shards_destroy(void *handle) {
 }
 
 }  // extern "C"
+
+// ---- The reference's SwiftTD example (examples/swifttd/swifttd.cpp), -----
+// compiled unchanged in this translation unit with its main() renamed, so its
+// own traits (SwiftTDTraits, Gamma = 1.0 as that file sets it) drive the
+// reference Network here.
+#define main plx_ref_swifttd_example_main
+#include "swifttd.cpp"
+#undef main
+
+// Runs `steps` DoStep calls of the example's network (n features -> 1 value
+// unit, FullyConnected with SwiftTDConnInit{alpha_init}). features: steps x n
+// row-major; rewards: steps. Outputs: the ten connection fields (10 x n, in
+// the example's ExtraConnFields order) and V after every step.
+extern "C" int ref_swifttd_example_run(uint64_t n, const float *features,
+                                       const float *rewards, int steps,
+                                       float alpha_init, float *fields_out,
+                                       float *v_out) {
+  g_unit_cap = n + 2;
+  g_conn_cap = n + 1;
+  using FC = plastix::FullyConnected<SwiftTDConnInit>;
+  ImprintingLearner Net(n, FC{1, SwiftTDConnInit{alpha_init}});
+  for (int S = 0; S < steps; ++S) {
+    const float R[1] = {rewards[S]};
+    Net.DoStep(std::span<const float>(features + (uint64_t)S * n, n),
+               std::span<const float>(R, 1));
+    v_out[S] = Net.GetOutput()[0];
+  }
+  auto &CA = Net.GetConnAlloc();
+  if (CA.Size() != n) return -1;
+  for (uint64_t I = 0; I < n; ++I) {
+    fields_out[0 * n + I] = plastix::GetWeight(CA, I);
+    fields_out[1 * n + I] = plastix::GetField<ZTag>(CA, I);
+    fields_out[2 * n + I] = plastix::GetField<ZDeltaTag>(CA, I);
+    fields_out[3 * n + I] = plastix::GetField<DeltaWTag>(CA, I);
+    fields_out[4 * n + I] = plastix::GetField<HTag>(CA, I);
+    fields_out[5 * n + I] = plastix::GetField<HOldTag>(CA, I);
+    fields_out[6 * n + I] = plastix::GetField<HTempTag>(CA, I);
+    fields_out[7 * n + I] = plastix::GetField<ZBarTag>(CA, I);
+    fields_out[8 * n + I] = plastix::GetField<PTag>(CA, I);
+    fields_out[9 * n + I] = plastix::GetField<BetaTag>(CA, I);
+  }
+  return 0;
+}

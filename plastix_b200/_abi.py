@@ -79,6 +79,9 @@ _SIGNATURES = {
     "plx_radix_sort_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_radix_sort_u32": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p,
                                    c_uint32, c_uint32, c_void_p, ctypes.c_size_t]),
+    "plx_swifttd_scratch_bytes": (c_uint64, [c_uint64, c_uint32]),
+    "plx_swifttd_step": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
+                                 c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),
     "plx_regrow": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_uint64,
                            c_uint64]),

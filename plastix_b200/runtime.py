@@ -317,3 +317,67 @@ class StructuralLayer:
         sweep_forward(ctx, self.csr, self.f, self.w, act_src, self.act_dst)
         self.step_index += 1
         return self.act_dst
+
+
+# ---------------------------------------------------------------------------
+# SwiftTD (examples/swifttd/swifttd.cpp): N features -> one value unit
+# ---------------------------------------------------------------------------
+TD_FIELDS = ("w", "z", "z_delta", "delta_w", "h", "h_old", "h_temp", "z_bar", "p", "beta")
+TD_GLOBALS = ("gamma", "lambda", "eta", "eta_min", "decay", "meta",
+              "v", "v_old", "delta", "v_delta_prev", "v_delta", "tau", "b")
+
+
+class SwiftTDLearner:
+    """The SwiftTD network of the reference example on the device.
+
+    State is the reference's ten connection fields (swifttd.cpp:199-209) as
+    rows of one [10, n] float32 tensor (row stride padded to 16 bytes), plus
+    the 13-float globals record (swifttd.cpp:47-62) in device memory.
+    ``step(active_idx, reward)`` is one Network::DoStep with the given active
+    features (sorted, unique, int32 device tensor) and a device reward scalar;
+    it returns V (a 1-element device tensor). ``alpha_init`` sets Beta =
+    log(alpha_init) as SwiftTDConnInit does (swifttd.cpp:66-72).
+    """
+
+    def __init__(self, ctx: Context, n_features: int, *, gamma=0.99, lambda_=0.9, eta=0.05,
+                 eta_min=1e-7, decay=0.999, meta=1e-3, alpha_init=0.05,
+                 max_active: Optional[int] = None):
+        import math
+        import struct
+
+        self.ctx = ctx
+        self.n = int(n_features)
+        dev = ctx.device
+        self.stride = (self.n + 3) // 4 * 4
+        self.state = torch.zeros((len(TD_FIELDS), self.stride), dtype=torch.float32, device=dev)
+        # std::log on a float argument, rounded to float (SwiftTDConnInit).
+        a32 = struct.unpack("f", struct.pack("f", alpha_init))[0]
+        self.state[9].fill_(struct.unpack("f", struct.pack("f", math.log(a32)))[0])
+        self.globals = torch.zeros(len(TD_GLOBALS), dtype=torch.float32, device=dev)
+        self.globals[:6] = torch.tensor([gamma, lambda_, eta, eta_min, decay, meta],
+                                        dtype=torch.float32)
+        self.v = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.max_active = int(max_active if max_active is not None else max(1, self.n // 100))
+        nbytes = _abi.lib().plx_swifttd_scratch_bytes(self.n, self.max_active)
+        self.scratch = torch.zeros(int(nbytes), dtype=torch.uint8, device=dev)
+        self._ptrs = (c_void_p * len(TD_FIELDS))(
+            *[self.state[i].data_ptr() for i in range(len(TD_FIELDS))])
+
+    def field(self, name: str) -> torch.Tensor:
+        return self.state[TD_FIELDS.index(name), :self.n]
+
+    def fields(self) -> torch.Tensor:
+        return self.state[:, :self.n]
+
+    def step(self, active_idx: torch.Tensor, reward: torch.Tensor,
+             active_val: Optional[torch.Tensor] = None) -> torch.Tensor:
+        k = int(active_idx.numel())
+        if k > self.max_active:
+            nbytes = _abi.lib().plx_swifttd_scratch_bytes(self.n, k)
+            self.scratch = torch.zeros(int(nbytes), dtype=torch.uint8,
+                                       device=self.scratch.device)
+            self.max_active = k
+        call("plx_swifttd_step", self.ctx.handle, self.n, self._ptrs,
+             _ptr(active_idx) if k else None, _ptr(active_val), k, _ptr(reward),
+             _ptr(self.globals), _ptr(self.v), _ptr(self.scratch), self.scratch.numel())
+        return self.v

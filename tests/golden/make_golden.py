@@ -27,9 +27,31 @@ def sweep_hebbian_small():
                         w=w, trace=e, act=a)
 
 
+def swifttd_features(n, steps, seed):
+    """Seeded feature rows for the SwiftTD fixtures: 0, 1, 2 or 5 active
+    features per step (one active feature keeps Tau <= Eta, so both branches
+    of swifttd.cpp:169-185 occur), value 1.0; rewards N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    feats = np.zeros((steps, n), np.float32)
+    for s in range(steps):
+        # the last steps have one active feature, so the final H/ZBar are live
+        k = 1 if s >= steps - 6 else rng.choice([0, 1, 1, 1, 2, 5])
+        feats[s, rng.choice(n, k, replace=False)] = 1.0
+    return feats, rng.normal(size=steps).astype(np.float32)
+
+
+def swifttd_small():
+    n, steps, seed = 64, 200, 5
+    feats, rewards = swifttd_features(n, steps, seed)
+    fields, v = oracle.ref_swifttd_example_run(feats, rewards, alpha_init=0.05)
+    np.savez_compressed(HERE / "swifttd_small.npz", n=n, steps=steps, seed=seed,
+                        features=feats, rewards=rewards, fields=fields, v=v)
+
+
 if __name__ == "__main__":
     ob.build()
     if oracle.ref() is None:
         sys.exit("reference build missing: the reference tree is needed to make fixtures")
     sweep_hebbian_small()
+    swifttd_small()
     print("fixtures written to", HERE)

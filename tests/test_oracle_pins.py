@@ -105,3 +105,46 @@ def test_oracle_matches_reference_build(orc, seed, n_src, n_dst, n_edges):
     np.testing.assert_array_equal(w, w_r)
     np.testing.assert_array_equal(e, e_r)
     np.testing.assert_array_equal(a[n_src:], a_r)
+
+
+def _swifttd_oracle_run(orc, feats, rewards, gamma, acc_f64=False):
+    fields = orc.td_fields(feats.shape[1])
+    g = orc.td_globals(gamma=gamma)
+    v = [orc.swifttd_step(fields, feats[s], rewards[s], g, acc_f64) for s in range(len(feats))]
+    return fields, np.array(v, np.float32), g
+
+
+def test_swifttd_oracle_matches_reference_fixture(orc):
+    """The SwiftTD restatement against the fixture made by the reference's own
+    examples/swifttd/swifttd.cpp network (Gamma 1.0 as that file sets it):
+    bit for bit, V after every step and all ten fields at the end."""
+    z = np.load(GOLDEN / "swifttd_small.npz")
+    fields, v, _ = _swifttd_oracle_run(orc, z["features"], z["rewards"], 1.0)
+    np.testing.assert_array_equal(v.view(np.uint32), z["v"].view(np.uint32))
+    np.testing.assert_array_equal(fields.view(np.uint32), z["fields"].view(np.uint32))
+    assert np.count_nonzero(z["fields"][4]) > 0  # H live: the no-reset branch ran last
+
+
+def test_swifttd_oracle_matches_reference_build(orc):
+    if orc.ref() is None:
+        pytest.skip("reference not built here")
+    rng = np.random.default_rng(21)
+    n, steps = 3000, 25
+    feats = np.zeros((steps, n), np.float32)
+    for s in range(steps):
+        feats[s, rng.choice(n, 30, replace=False)] = 1.0
+    rewards = rng.normal(size=steps).astype(np.float32)
+    want_f, want_v = orc.ref_swifttd_example_run(feats, rewards)
+    fields, v, _ = _swifttd_oracle_run(orc, feats, rewards, 1.0)
+    np.testing.assert_array_equal(v.view(np.uint32), want_v.view(np.uint32))
+    np.testing.assert_array_equal(fields.view(np.uint32), want_f.view(np.uint32))
+
+
+def test_swifttd_f64_sums_stay_close_to_sequential_f32(orc):
+    """The double-precision-sum form of the oracle (what the device reductions
+    are compared with) tracks the reference's sequential float sums."""
+    z = np.load(GOLDEN / "swifttd_small.npz")
+    f32, v32, _ = _swifttd_oracle_run(orc, z["features"], z["rewards"], 1.0)
+    f64, v64, _ = _swifttd_oracle_run(orc, z["features"], z["rewards"], 1.0, acc_f64=True)
+    np.testing.assert_allclose(v64, v32, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(f64, f32, rtol=1e-5, atol=1e-6)
