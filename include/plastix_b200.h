@@ -120,6 +120,11 @@ int plx_csr_plan_async(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
 #define PLX_APPLY_SIGMOID 1   /* act = 1/(1+exp(-acc))  mlp_xor.cpp:24-26  */
 #define PLX_APPLY_TANH 2      /* act = tanh(acc)      manual_fcc Apply      */
 #define PLX_APPLY_IPC_ERROR 3 /* err = x - acc        ipc_multilayer.cpp:147-150 */
+/* Backward-pass applies (the sweep run over a source-major connection order,
+ * see plx_transpose): value[r] is the row unit's activation or value node. */
+#define PLX_APPLY_SIGMOID_GRAD 4 /* out = acc * a * (1 - a)   mlp_xor.cpp:43-46 */
+#define PLX_APPLY_TANH_GRAD 5    /* out = (1 - tanh(x)^2) * acc
+                                    ipc_multilayer.cpp:128-131,170-175        */
 
 /* One forward sweep with the default Map/Combine (w * act[src], +), then
  * Apply per row. Replaces Network::DoForwardPass, Pipeline branch
@@ -160,7 +165,12 @@ int plx_sweep_forward_hebbian(plx_ctx* ctx, const plx_csr* csr,
 #define PLX_UPDATE_GRADIENT 1 /* w -= rate * post[dst] * act[src]
                                  (mlp_xor.cpp:51-56, linear_regression.cpp:31-36) */
 #define PLX_UPDATE_HEBBIAN 2  /* w += rate * post[dst] * act[src]
-                                 (ipc_multilayer.cpp:183-190)                 */
+                                 (ipc_multilayer.cpp:182-190)                 */
+#define PLX_UPDATE_HEBBIAN_T 3 /* the same rule on a source-major copy, where
+                                  the row value is act[src] and the gathered
+                                  value post[dst]: w += (rate * post) * act,
+                                  rounded in the same order as kind 2, so a
+                                  source-major copy stays bit-identical */
 
 /* Per-connection weight update over dst-sorted connections; replaces the
  * UpdateIncomingConnection sweep of DoUpdateConnectionState
@@ -253,6 +263,37 @@ int plx_regrow(plx_ctx* ctx, uint64_t n, const uint64_t* count,
                uint32_t* from_id, uint32_t* to_id, float* weight, uint8_t* age,
                uint32_t src_base, uint32_t n_src, uint32_t dst_base,
                uint32_t n_dst, uint64_t seed, uint64_t step_base);
+
+/* ---- backward order and per-unit steps ----------------------------------- */
+
+size_t plx_transpose_scratch_bytes(uint64_t n);
+
+/* Source-major order of n connections for the backward sweep: a stable sort
+ * by FromId (sources src_base .. src_base + n_src - 1; connections from other
+ * units sort after them and belong to no row), each source's run in
+ * DESCENDING connection index order when `reverse` is set -- the Pipeline
+ * backward order, plastix.hpp:193-203 -- or ascending (the Topological level
+ * sweep, plastix.hpp:172-181). Outputs: keys_out[j] = FromId - src_base of
+ * position j (n_src for excluded connections), perm_out[j] = its connection
+ * index (apply with plx_gather to ToId, Weight, ...), row_ptr_out[0..n_src].
+ * A sweep over (row_ptr_out, gathered ToId as the gathered index, gathered
+ * Weight) with a PLX_APPLY_*_GRAD apply is the reference's DoBackwardPass.
+ * n < 2^30. */
+int plx_transpose(plx_ctx* ctx, uint64_t n, const uint32_t* from_id,
+                  uint32_t src_base, uint32_t n_src, int reverse,
+                  uint32_t* keys_out, uint32_t* perm_out, uint32_t* row_ptr_out,
+                  void* scratch, size_t scratch_bytes);
+
+/* iPC value nodes of n hidden units (ipc_multilayer.cpp:239-245 then the
+ * pre-step of the next step, :220-228): mode 1: x += gamma * (-eps + bu);
+ * bu = 0; act = tanh(x). mode 0: act = tanh(x) only. */
+int plx_ipc_value_update(plx_ctx* ctx, uint64_t n, float* x, const float* eps,
+                         float* bu, float gamma, float* act, int mode);
+
+/* MSELoss (traits.hpp:185-193) and the sigmoid backward Apply of the output
+ * units (mlp_xor.cpp:43-46): grad = ((a - target) * a) * (1 - a). */
+int plx_mse_sigmoid_grad(plx_ctx* ctx, uint64_t n, const float* act,
+                         const float* target, float* grad);
 
 /* ---- SwiftTD (examples/swifttd/swifttd.cpp) ------------------------------ */
 

@@ -6,8 +6,10 @@
   ``-std=c++20 -O2`` build.
 * ``oracle/_ref/libplx_ref.so`` — the reference itself: its headers
   compiled from the reference tree (``/root/reference/include``) together with
-  ``oracle/ref_harness.cpp`` (which also compiles the reference's
-  ``examples/swifttd/swifttd.cpp`` unchanged, its ``main`` renamed). Only when the reference tree is present (it is
+  ``oracle/ref_harness.cpp``, ``oracle/ref_mlp.cpp`` and ``oracle/ref_ipc.cpp``,
+  which compile the reference's ``examples/swifttd/swifttd.cpp``,
+  ``examples/mlp-xor/mlp_xor.cpp`` and ``examples/ipc-multilayer/ipc_multilayer.cpp``
+  unchanged (each ``main`` renamed) to drive their own policies. Only when the reference tree is present (it is
   not on the GPU machines, which use the prebuilt file). The one change to the
   reference sources: the fixed capacities ``UnitAlloc(4096), ConnAlloc(4096 *
   4)`` of ``include/plastix/plastix.hpp`` become calls into the harness, so
@@ -55,7 +57,9 @@ def build_reference() -> Path | None:
     if not hpp.exists():
         return REF_SO if REF_SO.exists() else None
     harness = HERE / "ref_harness.cpp"
-    deps = ([harness, Path(__file__), REF_ROOT / "examples" / "swifttd" / "swifttd.cpp"]
+    units = [harness, HERE / "ref_mlp.cpp", HERE / "ref_ipc.cpp"]
+    examples = [REF_ROOT / "examples" / d for d in ("swifttd", "mlp-xor", "ipc-multilayer")]
+    deps = (units + [Path(__file__)] + [e / f"{e.name.replace('-', '_')}.cpp" for e in examples]
             + sorted((REF_ROOT / "include" / "plastix").glob("*.hpp")))
     if not _stale(REF_SO, deps):
         return REF_SO
@@ -73,10 +77,10 @@ def build_reference() -> Path | None:
         prelude.write_text("#include <cstddef>\n"
                            "std::size_t plx_ref_unit_capacity();\n"
                            "std::size_t plx_ref_conn_capacity();\n")
-        cmd = ["g++", "-std=c++20", "-O2", "-fPIC", "-shared", "-pthread",
-               "-include", str(prelude), f"-I{inc}", f"-I{REF_ROOT / 'examples' / 'swifttd'}",
-               str(harness),
-               str(REF_ROOT / "src" / "plastix.cpp"), "-o", str(REF_SO)]
+        cmd = (["g++", "-std=c++20", "-O2", "-fPIC", "-shared", "-pthread",
+                "-include", str(prelude), f"-I{inc}"] + [f"-I{e}" for e in examples]
+               + [str(u) for u in units] + [
+               str(REF_ROOT / "src" / "plastix.cpp"), "-o", str(REF_SO)])
         subprocess.run(cmd, check=True)
     return REF_SO
 

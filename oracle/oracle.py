@@ -59,6 +59,12 @@ def orc() -> ctypes.CDLL:
                                     c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,
                                     c_uint64, c_uint64]
         L.oracle_keep_abs_ge.argtypes = [c_void_p, c_uint64, c_float, c_void_p]
+        L.oracle_backward.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_int, c_uint64, c_uint64, c_uint64, c_int,
+                                      c_void_p, c_void_p, c_void_p]
+        L.oracle_ipc_value_update.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p, c_float,
+                                              c_void_p, c_int]
+        L.oracle_mse_sigmoid_grad.argtypes = [c_uint64, c_void_p, c_void_p, c_void_p]
         L.oracle_swifttd_step.argtypes = [c_uint64, c_void_p, c_void_p, c_float, c_void_p,
                                           c_int]
         L.oracle_swifttd_step.restype = c_float
@@ -80,6 +86,12 @@ def ref() -> Optional[ctypes.CDLL]:
         L.ref_sweep_shards_create.restype = c_void_p
         L.ref_sweep_shards_step.argtypes = [c_void_p, c_void_p]
         L.ref_sweep_shards_destroy.argtypes = [c_void_p]
+        L.ref_mlp_run.argtypes = [c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]
+        L.ref_mlp_run.restype = ctypes.c_int64
+        L.ref_ipc_run.argtypes = [c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_uint64]
+        L.ref_ipc_run.restype = ctypes.c_int64
         L.ref_swifttd_example_run.argtypes = [c_uint64, c_void_p, c_void_p, c_int, c_float,
                                               c_void_p, c_void_p]
         _ref = L
@@ -269,3 +281,170 @@ def ref_swifttd_example_run(features, rewards, alpha_init=0.05):
                                  _p(v)) != 0:
         raise RuntimeError("ref_swifttd_example_run failed")
     return fields, v
+
+
+# ---------------------------------------------------------------------------
+# Backward pass and the example networks (mlp-xor: Topological; iPC: Pipeline)
+# ---------------------------------------------------------------------------
+def backward(from_id, to_id, w, dval, n_units, lo, hi, apply=0, value=None, out=None,
+             descending=True, dead=None):
+    """DoBackwardPass over the given connections (Pipeline order when
+    descending, else one Topological level range). Returns out (n_units
+    float32; entries [lo, hi) written)."""
+    out = np.zeros(n_units, np.float32) if out is None else out
+    acc = np.zeros(n_units, np.float32)
+    value = None if value is None else np.ascontiguousarray(value, np.float32)
+    orc().oracle_backward(from_id.size, _p(from_id), _p(to_id), _p(dead), _p(w),
+                          _p(np.ascontiguousarray(dval, np.float32)), int(descending),
+                          n_units, lo, hi, apply, _p(value), _p(out), _p(acc))
+    return out
+
+
+def ipc_value_update(x, eps, bu, gamma, act, mode=1):
+    """In place on float32 arrays of equal length."""
+    orc().oracle_ipc_value_update(x.size, _p(x), _p(eps), _p(bu), gamma, _p(act), mode)
+
+
+def mse_sigmoid_grad(act, target):
+    act = np.ascontiguousarray(act, np.float32)
+    g = np.empty_like(act)
+    orc().oracle_mse_sigmoid_grad(act.size, _p(act), _p(np.ascontiguousarray(target, np.float32)),
+                                  _p(g))
+    return g
+
+
+class MlpTopo:
+    """A layered sigmoid MLP in the reference's Topological mode with the
+    mlp_xor.cpp policies: FullyConnected layers (dst-major), levels 0..L.
+    layers = unit counts per level; w = weights in connection order."""
+
+    def __init__(self, layers, w, lr=0.5):
+        self.layers = list(layers)
+        self.begin = np.cumsum([0] + self.layers)
+        self.n_units = int(self.begin[-1])
+        frm, to, self.level_conn = [], [], [0]
+        for L in range(1, len(self.layers)):
+            for u in range(self.begin[L], self.begin[L + 1]):
+                for s_ in range(self.begin[L - 1], self.begin[L]):
+                    frm.append(s_)
+                    to.append(u)
+            self.level_conn.append(len(frm))
+        self.from_id = np.array(frm, np.uint32)
+        self.to_id = np.array(to, np.uint32)
+        self.w = np.array(w, np.float32, copy=True)
+        self.lr = lr
+        self.act = np.zeros(self.n_units, np.float32)
+        self.grad = np.zeros(self.n_units, np.float32)
+
+    def _conns(self, L):  # connections with SrcLevel == L
+        return slice(self.level_conn[L], self.level_conn[L + 1])
+
+    def forward(self, x):
+        self.act[:self.layers[0]] = x
+        acc = np.zeros(self.n_units, np.float32)
+        for L in range(1, len(self.layers)):
+            c = self._conns(L - 1)
+            f, t = np.ascontiguousarray(self.from_id[c]), np.ascontiguousarray(self.to_id[c])
+            ww = np.ascontiguousarray(self.w[c])
+            orc().oracle_forward_pipeline(f.size, _p(f), _p(t), None, _p(ww), _p(self.act),
+                                          int(self.begin[L + 1]), int(self.begin[L]), 1, None,
+                                          None, _p(acc))
+        return self.act[self.begin[-2]:].copy()
+
+    def step(self, x, target):
+        """DoStep: forward, MSELoss, backward (levels L..1), gradient update."""
+        self.forward(x)
+        top = len(self.layers) - 1
+        o = slice(self.begin[top], self.begin[top + 1])
+        self.grad[o] = mse_sigmoid_grad(self.act[o], np.atleast_1d(target))
+        for L in range(top - 1, 0, -1):
+            c = self._conns(L)
+            self.grad = backward(np.ascontiguousarray(self.from_id[c]),
+                                 np.ascontiguousarray(self.to_id[c]),
+                                 np.ascontiguousarray(self.w[c]), self.grad, self.n_units,
+                                 int(self.begin[L]), int(self.begin[L + 1]), apply=4,
+                                 value=self.act, out=self.grad, descending=False)
+        self.w = update_post(self.from_id, self.to_id, self.act, self.grad, self.w, 1, self.lr)
+
+
+def ipc_prestep(x, inputs, hidden):
+    """Activation = f(ValueNode): inputs as given (DoForwardPass clamps them),
+    tanh for hidden units, identity for the rest (ipc_multilayer.cpp:220-228)."""
+    lo, hi = hidden
+    act = np.array(x, np.float32, copy=True)
+    act[:inputs.size] = inputs
+    ipc_value_update(x[lo:hi].copy(), np.zeros(hi - lo, np.float32),
+                     np.zeros(hi - lo, np.float32), 0.0, act[lo:hi], mode=0)
+    return act
+
+
+def ipc_forward(from_id, to_id, w, act, x, n_in):
+    """DoForwardPass, Pipeline, iPC Apply: eps = x - mu for units >= n_in."""
+    n = x.size
+    err = np.zeros(n, np.float32)
+    acc = np.zeros(n, np.float32)
+    act = np.array(act, np.float32, copy=True)
+    orc().oracle_forward_pipeline(from_id.size, _p(from_id), _p(to_id), None, _p(w), _p(act),
+                                  n, n_in, 3, _p(x), _p(err), _p(acc))
+    return err
+
+
+def ipc_backward(from_id, to_id, w, err, x, hidden):
+    """DoBackwardPass, Pipeline: BottomUp of the hidden units."""
+    lo, hi = hidden
+    return backward(from_id, to_id, w, err, x.size, lo, hi, apply=5, value=x,
+                    descending=True)
+
+
+def ipc_hidden_update(x, err, bu, act, gamma, hidden):
+    """Value-node update of the hidden units and the next pre-step, in place
+    on x and act (ipc_multilayer.cpp:239-245)."""
+    lo, hi = hidden
+    xh, eh, bh, ah = x[lo:hi].copy(), err[lo:hi].copy(), bu[lo:hi].copy(), act[lo:hi].copy()
+    ipc_value_update(xh, eh, bh, gamma, ah, mode=1)
+    x[lo:hi] = xh
+    act[lo:hi] = ah
+
+
+def ipc_step(from_id, to_id, w, x, inputs, hidden, gamma, alpha):
+    """The iPC example's iPCStep (ipc_multilayer.cpp:214-246) on a Pipeline
+    network: units [0, n_in) inputs, `hidden` = (lo, hi) tanh units, the rest
+    identity outputs. In place on w and x; returns (err, act)."""
+    act = ipc_prestep(x, inputs, hidden)
+    err = ipc_forward(from_id, to_id, w, act, x, inputs.size)
+    bu = ipc_backward(from_id, to_id, w, err, x, hidden)
+    w[:] = update_post(from_id, to_id, act, err, w, 2, alpha)
+    ipc_hidden_update(x, err, bu, act, gamma, hidden)
+    return err, act
+
+
+def ref_mlp_run(n_in, n_hidden, seed, epochs, inputs, targets):
+    L = ref()
+    if L is None:
+        raise FileNotFoundError(f"{REF_SO} was not built")
+    inputs = np.ascontiguousarray(inputs, np.float32)
+    targets = np.ascontiguousarray(targets, np.float32)
+    maxc = n_in * n_hidden + n_hidden + 16
+    w0, w1 = np.zeros(maxc, np.float32), np.zeros(maxc, np.float32)
+    preds = np.zeros(targets.size, np.float32)
+    m = L.ref_mlp_run(n_in, n_hidden, seed, epochs, targets.size, _p(inputs), _p(targets),
+                      _p(w0), _p(w1), _p(preds), maxc)
+    if m < 0:
+        raise RuntimeError("ref_mlp_run failed")
+    return w0[:m], w1[:m], preds
+
+
+def ref_ipc_run(inputs, targets, w, x):
+    """The example's own iPCStep for len(targets) steps (3 -> 16 -> 1)."""
+    L = ref()
+    if L is None:
+        raise FileNotFoundError(f"{REF_SO} was not built")
+    w = np.array(w, np.float32, copy=True)
+    x = np.array(x, np.float32, copy=True)
+    err = np.zeros_like(x)
+    inputs = np.ascontiguousarray(inputs, np.float32)
+    targets = np.ascontiguousarray(targets, np.float32)
+    m = L.ref_ipc_run(targets.size, _p(inputs), _p(targets), _p(w), _p(x), _p(err), w.size)
+    if m != w.size:
+        raise RuntimeError("ref_ipc_run failed")
+    return w, x, err

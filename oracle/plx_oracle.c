@@ -316,3 +316,62 @@ float oracle_swifttd_step(uint64_t n, float** fld, const float* f, float reward,
   g->v_old = g->v;
   return g->v;
 }
+
+/* ---- backward pass and per-unit steps of the example networks ----------- */
+
+/* Backward Apply (kinds as the device: 0 store, 4 sigmoid gradient
+ * mlp_xor.cpp:43-46, 5 iPC bottom-up ipc_multilayer.cpp:128-131,170-175). */
+static float backward_apply(int kind, float acc, float value) {
+  if (kind == 4) return acc * value * (1.0f - value);
+  if (kind == 5) {
+    const float t = tanhf(value);
+    return (1.0f - t * t) * acc;
+  }
+  return acc;
+}
+
+/*
+ * Network::DoBackwardPass over connections [0, n_conn) of the given arrays:
+ * Pipeline order (descending = 1, plastix.hpp:193-203) or one Topological
+ * level range (descending = 0, plastix.hpp:172-181). Map = W[C] * dval[To[C]]
+ * (mlp_xor.cpp:38-41, ipc_multilayer.cpp:163-166), Combine = +. Then
+ * out[I] = Apply(acc[I], value[I]) for I in [lo, hi) and acc is cleared for
+ * all n_units units. bwd_acc holds n_units zeros on entry and on return.
+ */
+void oracle_backward(uint64_t n_conn, const uint32_t* from, const uint32_t* to,
+                     const uint8_t* dead, const float* w, const float* dval,
+                     int descending, uint64_t n_units, uint64_t lo, uint64_t hi,
+                     int apply_kind, const float* value, float* out,
+                     float* bwd_acc) {
+  for (uint64_t j = 0; j < n_conn; ++j) {
+    const uint64_t c = descending ? n_conn - 1 - j : j;
+    if (dead && dead[c]) continue;
+    bwd_acc[from[c]] = bwd_acc[from[c]] + w[c] * dval[to[c]];
+  }
+  for (uint64_t i = lo; i < hi; ++i)
+    out[i] = backward_apply(apply_kind, bwd_acc[i], value ? value[i] : 0.0f);
+  for (uint64_t i = 0; i < n_units; ++i) bwd_acc[i] = 0.0f;
+}
+
+/* iPC value-node update and pre-step (ipc_multilayer.cpp:239-245, :220-228),
+ * as plx_ipc_value_update. */
+void oracle_ipc_value_update(uint64_t n, float* x, const float* eps, float* bu,
+                             float gamma, float* act, int mode) {
+  for (uint64_t i = 0; i < n; ++i) {
+    if (mode) {
+      x[i] += gamma * (-eps[i] + bu[i]);
+      bu[i] = 0.0f;
+    }
+    act[i] = tanhf(x[i]);
+  }
+}
+
+/* MSELoss + sigmoid backward Apply of the outputs (traits.hpp:185-193,
+ * mlp_xor.cpp:43-46). */
+void oracle_mse_sigmoid_grad(uint64_t n, const float* act, const float* target,
+                             float* grad) {
+  for (uint64_t i = 0; i < n; ++i) {
+    const float acc = act[i] - target[i];
+    grad[i] = acc * act[i] * (1.0f - act[i]);
+  }
+}

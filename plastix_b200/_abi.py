@@ -22,9 +22,12 @@ APPLY_IDENTITY = 0
 APPLY_SIGMOID = 1
 APPLY_TANH = 2
 APPLY_IPC_ERROR = 3
+APPLY_SIGMOID_GRAD = 4
+APPLY_TANH_GRAD = 5
 
 UPDATE_GRADIENT = 1
 UPDATE_HEBBIAN = 2
+UPDATE_HEBBIAN_T = 3
 
 SEQ_ROW_MAX = 256
 
@@ -79,6 +82,12 @@ _SIGNATURES = {
     "plx_radix_sort_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_radix_sort_u32": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p,
                                    c_uint32, c_uint32, c_void_p, ctypes.c_size_t]),
+    "plx_transpose_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
+    "plx_transpose": (c_int, [c_void_p, c_uint64, c_void_p, c_uint32, c_uint32, c_int, c_void_p,
+                              c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_ipc_value_update": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_float,
+                                     c_void_p, c_int]),
+    "plx_mse_sigmoid_grad": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p]),
     "plx_swifttd_scratch_bytes": (c_uint64, [c_uint64, c_uint32]),
     "plx_swifttd_step": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),

@@ -8,7 +8,7 @@
 // Design (B200):
 // * Rows (destination units) are classified once per connectivity by
 //   plx_csr_plan: short rows (<= PLX_SEQ_ROW_MAX connections), wide rows
-//   (<= 2048) and long rows.
+//   (<= 8192) and long rows.
 // * Short rows are swept by k_sweep, a persistent warp-specialised kernel
 //   over fixed edge tiles of S connections. A producer warp streams each
 //   tile's SoA slices (FromId, Weight, [Trace], [Dead]) and the tile's slice
@@ -36,7 +36,7 @@ namespace plx {
 
 constexpr uint32_t kPlanG = 256;                // plan granularity (edges)
 constexpr uint32_t kSeqMax = PLX_SEQ_ROW_MAX;   // short-row limit
-constexpr uint32_t kLongRow = 2048;             // wide-row limit
+constexpr uint32_t kLongRow = 8192;             // wide-row limit
 constexpr uint32_t kHalo = kSeqMax;             // max out-of-tile piece of a short row
 constexpr uint32_t kPlanMagic = 0x504C4E32u;    // "PLN2"
 constexpr uint32_t kPlanHdr = 8;
@@ -94,7 +94,7 @@ struct SweepArgs {
   uint32_t only_long;     // warp fast path: run only if the longest row > 128
 };
 
-enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3 };
+enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3, kUpdHebbT = 4 };
 
 // ---------------------------------------------------------------------------
 // Plan construction
@@ -194,9 +194,19 @@ __device__ __forceinline__ float apply_row(float acc, uint32_t r,
   if constexpr (APPLY == PLX_APPLY_IDENTITY) {
     post = acc;
   } else if constexpr (APPLY == PLX_APPLY_SIGMOID) {
-    post = 1.0f / __fadd_rn(1.0f, expf(-acc));
+    // exp in double precision, rounded once to float: the correctly rounded
+    // single-precision exponential (up to rare near-halfway cases), which is
+    // also what the host's expf returns to within its half-ulp accuracy, so
+    // long training runs do not drift from the reference.
+    post = 1.0f / __fadd_rn(1.0f, (float)exp(-(double)acc));
   } else if constexpr (APPLY == PLX_APPLY_TANH) {
     post = tanhf(acc);
+  } else if constexpr (APPLY == PLX_APPLY_SIGMOID_GRAD) {
+    const float v = __ldg(a.value + r);
+    post = __fmul_rn(__fmul_rn(acc, v), __fsub_rn(1.0f, v));
+  } else if constexpr (APPLY == PLX_APPLY_TANH_GRAD) {
+    const float t = tanhf(__ldg(a.value + r));
+    post = __fmul_rn(__fsub_rn(1.0f, __fmul_rn(t, t)), acc);
   } else {
     post = __fsub_rn(__ldg(a.value + r), acc);
   }
@@ -746,6 +756,8 @@ __global__ void __launch_bounds__(L::NT) k_sweep(SweepArgs a) {
           s_w[k] = __fadd_rn(w, __fmul_rn(a.rate, e));
         } else if constexpr (UPD == kUpdGrad) {
           s_w[k] = __fsub_rn(w, __fmul_rn(__fmul_rn(a.rate, post), av));
+        } else if constexpr (UPD == kUpdHebbT) {
+          s_w[k] = __fadd_rn(w, __fmul_rn(__fmul_rn(a.rate, av), post));
         } else {
           s_w[k] = __fadd_rn(w, __fmul_rn(__fmul_rn(a.rate, post), av));
         }
@@ -1336,6 +1348,8 @@ extern "C" int plx_sweep_forward(plx_ctx* ctx, const plx_csr* csr,
     PLX_CHECK_ARG(value && err_out, "IPC_ERROR needs value and err_out");
   else
     PLX_CHECK_ARG(act_dst, "act_dst is required");
+  if (apply_kind == PLX_APPLY_SIGMOID_GRAD || apply_kind == PLX_APPLY_TANH_GRAD)
+    PLX_CHECK_ARG(value, "the gradient applies need value");
   PLX_TRY_CUDA(cudaSetDevice(ctx->device));
   SweepArgs a = base_args(ctx, csr);
   a.src = from_id;
@@ -1356,6 +1370,8 @@ extern "C" int plx_sweep_forward(plx_ctx* ctx, const plx_csr* csr,
     PLX_FWD_CASE(PLX_APPLY_SIGMOID)
     PLX_FWD_CASE(PLX_APPLY_TANH)
     PLX_FWD_CASE(PLX_APPLY_IPC_ERROR)
+    PLX_FWD_CASE(PLX_APPLY_SIGMOID_GRAD)
+    PLX_FWD_CASE(PLX_APPLY_TANH_GRAD)
 #undef PLX_FWD_CASE
     default:
       return set_error(PLX_ERR_ARG, "unknown apply_kind %d", apply_kind);
@@ -1425,6 +1441,9 @@ extern "C" int plx_sweep_update(plx_ctx* ctx, const plx_csr* csr,
     case PLX_UPDATE_HEBBIAN:
       return d ? launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebb, false, true>(ctx, a, csr)
                : launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebb, false, false>(ctx, a, csr);
+    case PLX_UPDATE_HEBBIAN_T:
+      return d ? launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebbT, false, true>(ctx, a, csr)
+               : launch_sweep<false, PLX_APPLY_IDENTITY, kUpdHebbT, false, false>(ctx, a, csr);
     default:
       return set_error(PLX_ERR_ARG, "unknown update_kind %d", update_kind);
   }

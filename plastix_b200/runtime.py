@@ -381,3 +381,220 @@ class SwiftTDLearner:
              _ptr(active_idx) if k else None, _ptr(active_val), k, _ptr(reward),
              _ptr(self.globals), _ptr(self.v), _ptr(self.scratch), self.scratch.numel())
         return self.v
+
+
+# ---------------------------------------------------------------------------
+# Backward sweep (K2): a source-major copy of a connection range
+# ---------------------------------------------------------------------------
+class SrcMajor:
+    """Source-major order of connections whose sources are units
+    [src_base, src_base + n_src): the permutation from plx_transpose, a CSR
+    over the sources, and the gathered ToId (the index the backward sweep
+    gathers through) and Weight. ``reverse`` gives each source's
+    connections in descending index order (Pipeline backward,
+    plastix.hpp:193-203); otherwise ascending (Topological,
+    plastix.hpp:172-181). Connections from other units are left out."""
+
+    def __init__(self, ctx: Context, from_id: torch.Tensor, to_id: torch.Tensor,
+                 weight: torch.Tensor, src_base: int, n_src: int, reverse: bool):
+        n = int(from_id.numel())
+        dev = ctx.device
+        self.ctx = ctx
+        keys = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        self.perm = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        row_ptr = torch.empty(n_src + 1, dtype=torch.int32, device=dev)
+        nbytes = _abi.lib().plx_transpose_scratch_bytes(n)
+        scratch = torch.empty(int(nbytes), dtype=torch.uint8, device=dev)
+        call("plx_transpose", ctx.handle, n, _ptr(from_id) if n else None, src_base, n_src,
+             int(reverse), _ptr(keys), _ptr(self.perm), _ptr(row_ptr), _ptr(scratch),
+             scratch.numel())
+        del scratch, keys
+        self.csr = DstCsr.from_row_ptr(ctx, row_ptr)
+        self.m = self.csr.n_edges
+        self.src_base, self.n_src = src_base, n_src
+        self.to_id = torch.empty(max(self.m, 1), dtype=torch.int32, device=dev)
+        self.weight = torch.empty(max(self.m, 1), dtype=torch.float32, device=dev)
+        if self.m:
+            gather(ctx, self.perm, [(to_id, self.to_id), (weight, self.weight)], n=self.m)
+
+    def refresh_weight(self, weight: torch.Tensor) -> None:
+        """Re-gathers Weight (after an update of the destination-major copy)."""
+        if self.m:
+            gather(self.ctx, self.perm, [(weight, self.weight)], n=self.m)
+
+    def backward(self, dval: torch.Tensor, out_rows: torch.Tensor, value_rows: torch.Tensor,
+                 apply: int) -> None:
+        """out_rows[s] = Apply(fold over source s of Weight * dval[ToId])."""
+        sweep_forward(self.ctx, self.csr, self.to_id, self.weight, dval, out_rows,
+                      apply=apply, value=value_rows)
+
+
+class MlpTopoNet:
+    """The mlp_xor.cpp network on the device: FullyConnected sigmoid layers
+    in the reference's Topological mode (levels processed in order), MSELoss,
+    the sigmoid backward pass and the gradient-descent connection update --
+    one Network::DoStep per ``step``. Connections are stored per level
+    (SrcLevel), destination-major as FullyConnected creates them."""
+
+    def __init__(self, ctx: Context, layers, weights, lr: float = 0.5):
+        import numpy as np
+
+        self.ctx = ctx
+        self.layers = [int(x) for x in layers]
+        self.begin = [0]
+        for n in self.layers:
+            self.begin.append(self.begin[-1] + n)
+        self.n_units = self.begin[-1]
+        self.lr = float(lr)
+        dev = ctx.device
+        w_all = np.asarray(weights, np.float32)
+        self.from_id, self.to_id, self.w, self.csr, self.bwd = [], [], [], [], {}
+        off = 0
+        for L in range(1, len(self.layers)):
+            frm = np.repeat(np.arange(self.begin[L - 1], self.begin[L], dtype=np.int32)[None, :],
+                            self.layers[L], axis=0).reshape(-1)
+            to = np.repeat(np.arange(self.begin[L], self.begin[L + 1], dtype=np.int32),
+                           self.layers[L - 1])
+            m = frm.size
+            f_d = torch.from_numpy(frm).to(dev)
+            t_d = torch.from_numpy(to).to(dev)
+            w_d = torch.from_numpy(w_all[off:off + m].copy()).to(dev)
+            off += m
+            self.from_id.append(f_d)
+            self.to_id.append(t_d)
+            self.w.append(w_d)
+            self.csr.append(DstCsr(ctx, t_d, self.begin[L], self.layers[L], use_to_id=False))
+        for L in range(1, len(self.layers) - 1):  # backward levels (SrcLevel == L)
+            self.bwd[L] = SrcMajor(ctx, self.from_id[L], self.to_id[L], self.w[L],
+                                   self.begin[L], self.layers[L], reverse=False)
+        self.act = torch.zeros(self.n_units, dtype=torch.float32, device=dev)
+        self.grad = torch.zeros(self.n_units, dtype=torch.float32, device=dev)
+
+    def weights(self) -> torch.Tensor:
+        return torch.cat(self.w)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """DoForwardPass (Topological: level by level, sigmoid Apply)."""
+        self.act[:self.layers[0]].copy_(x)
+        for L in range(1, len(self.layers)):
+            b0, b1 = self.begin[L], self.begin[L + 1]
+            sweep_forward(self.ctx, self.csr[L - 1], self.from_id[L - 1], self.w[L - 1],
+                          self.act, self.act[b0:b1], apply=_abi.APPLY_SIGMOID)
+        return self.act[self.begin[-2]:]
+
+    def step(self, x: torch.Tensor, target: torch.Tensor) -> None:
+        self.forward(x)
+        top = len(self.layers) - 1
+        o0, o1 = self.begin[top], self.begin[top + 1]
+        call("plx_mse_sigmoid_grad", self.ctx.handle, o1 - o0, _ptr(self.act[o0:o1]),
+             _ptr(target), _ptr(self.grad[o0:o1]))
+        for L in range(top - 1, 0, -1):
+            b0, b1 = self.begin[L], self.begin[L + 1]
+            sm = self.bwd[L]
+            sm.refresh_weight(self.w[L])
+            sm.backward(self.grad, self.grad[b0:b1], self.act[b0:b1], _abi.APPLY_SIGMOID_GRAD)
+        for L in range(1, len(self.layers)):
+            b0, b1 = self.begin[L], self.begin[L + 1]
+            sweep_update(self.ctx, self.csr[L - 1], self.from_id[L - 1], self.act,
+                         self.grad[b0:b1], self.w[L - 1], self.w[L - 1],
+                         kind=_abi.UPDATE_GRADIENT, rate=self.lr)
+
+
+class PredictiveCodingNet:
+    """Streaming iPC (examples/ipc-multilayer/ipc_multilayer.cpp) on a stack
+    of sparse layers: layer 0 takes the input, the last layer is the output,
+    the ones between are tanh hidden layers with persistent value nodes.
+    Block l holds the connections into layer l + 1 (destination-major, the
+    reference's connection order); blocks whose sources are hidden also keep
+    a source-major copy (descending per source: the Pipeline backward order)
+    with its own weights, updated with the same rule and rounding so both
+    copies stay identical.
+
+    ``iteration()`` is one inference step of iPCStep (pre-step done by the
+    previous value update, DoForwardPass with eps = x - mu, DoBackwardPass
+    with the bottom-up Apply, value-node update). ``update()`` is
+    DoUpdateConnectionState (theta += alpha * eps * f(x_src)).
+    ``example_step()`` is the example's own order: forward, backward, update,
+    value update."""
+
+    def __init__(self, ctx: Context, sizes, blocks, *, gamma: float = 0.1,
+                 alpha: float = 0.005):
+        """blocks[l] = (from_id, to_id, weight) device tensors of the
+        connections into layer l + 1 (absolute unit ids, destination-major).
+        to_id is only used here to build the index."""
+        self.ctx = ctx
+        self.sizes = [int(s) for s in sizes]
+        self.begin = [0]
+        for s in self.sizes:
+            self.begin.append(self.begin[-1] + s)
+        self.n_units = self.begin[-1]
+        self.gamma, self.alpha = float(gamma), float(alpha)
+        dev = ctx.device
+        self.from_id, self.w, self.csr, self.sm = [], [], [], {}
+        for l, (f, t, w) in enumerate(blocks):
+            self.from_id.append(f)
+            self.w.append(w)
+            self.csr.append(DstCsr(ctx, t, self.begin[l + 1], self.sizes[l + 1],
+                                   use_to_id=False))
+            if l >= 1:
+                self.sm[l] = SrcMajor(ctx, f, t, w, self.begin[l], self.sizes[l], reverse=True)
+        self.x = torch.zeros(self.n_units, dtype=torch.float32, device=dev)
+        self.act = torch.zeros_like(self.x)
+        self.err = torch.zeros_like(self.x)
+        self.bu = torch.zeros_like(self.x)
+
+    @property
+    def hidden(self):
+        return self.begin[1], self.begin[-2]
+
+    def clamp(self, inputs: torch.Tensor, targets: torch.Tensor) -> None:
+        """Clamps the input and output value nodes (ipc_multilayer.cpp:299-304)
+        and runs the pre-step (Activation = f(x): inputs identity, hidden
+        tanh)."""
+        n_in = self.sizes[0]
+        self.x[:n_in].copy_(inputs)
+        self.act[:n_in].copy_(inputs)
+        self.x[self.begin[-2]:].copy_(targets)
+        lo, hi = self.hidden
+        call("plx_ipc_value_update", self.ctx.handle, hi - lo, _ptr(self.x[lo:hi]), None, None,
+             0.0, _ptr(self.act[lo:hi]), 0)
+
+    def forward(self) -> None:
+        for l in range(len(self.csr)):
+            b0, b1 = self.begin[l + 1], self.begin[l + 2]
+            sweep_forward(self.ctx, self.csr[l], self.from_id[l], self.w[l], self.act,
+                          apply=_abi.APPLY_IPC_ERROR, value=self.x[b0:b1],
+                          err_out=self.err[b0:b1])
+
+    def backward(self) -> None:
+        for l, sm in self.sm.items():
+            b0, b1 = self.begin[l], self.begin[l + 1]
+            sm.backward(self.err, self.bu[b0:b1], self.x[b0:b1], _abi.APPLY_TANH_GRAD)
+
+    def value_update(self) -> None:
+        lo, hi = self.hidden
+        call("plx_ipc_value_update", self.ctx.handle, hi - lo, _ptr(self.x[lo:hi]),
+             _ptr(self.err[lo:hi]), _ptr(self.bu[lo:hi]), self.gamma, _ptr(self.act[lo:hi]), 1)
+
+    def update(self) -> None:
+        for l in range(len(self.csr)):
+            b0, b1 = self.begin[l + 1], self.begin[l + 2]
+            sweep_update(self.ctx, self.csr[l], self.from_id[l], self.act, self.err[b0:b1],
+                         self.w[l], self.w[l], kind=_abi.UPDATE_HEBBIAN, rate=self.alpha)
+            if l in self.sm:
+                sm = self.sm[l]
+                s0, s1 = self.begin[l], self.begin[l + 1]
+                sweep_update(self.ctx, sm.csr, sm.to_id, self.err, self.act[s0:s1],
+                             sm.weight, sm.weight, kind=_abi.UPDATE_HEBBIAN_T,
+                             rate=self.alpha)
+
+    def iteration(self) -> None:
+        self.forward()
+        self.backward()
+        self.value_update()
+
+    def example_step(self) -> None:
+        self.forward()
+        self.backward()
+        self.update()
+        self.value_update()

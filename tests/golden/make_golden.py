@@ -48,10 +48,41 @@ def swifttd_small():
                         features=feats, rewards=rewards, fields=fields, v=v)
 
 
+XOR_INPUTS = np.array([[0, 0], [0, 1], [1, 0], [1, 1]], np.float32)
+XOR_TARGETS = np.array([0, 1, 1, 0], np.float32)
+
+
+def mlp_xor_small():
+    """The XOR MLP (2 -> 8 -> 1, RandomUniformWeight seed 1234) trained by the
+    reference with mlp_xor.cpp's policies: initial and final weights and the
+    final predictions after 200 and after 5000 epochs."""
+    w0, w200, p200 = oracle.ref_mlp_run(2, 8, 1234, 200, XOR_INPUTS, XOR_TARGETS)
+    _, w5000, p5000 = oracle.ref_mlp_run(2, 8, 1234, 5000, XOR_INPUTS, XOR_TARGETS)
+    np.savez_compressed(HERE / "mlp_xor_small.npz", inputs=XOR_INPUTS, targets=XOR_TARGETS,
+                        seed=1234, w_init=w0, w_200=w200, preds_200=p200, w_5000=w5000,
+                        preds_5000=p5000)
+
+
+def ipc_small():
+    """30 steps of the iPC example's own iPCStep (3 -> 16 -> 1) from seeded
+    weights and value nodes."""
+    rng = np.random.default_rng(3)
+    n_conn, n_units, steps = 3 * 16 + 16, 20, 30
+    w = rng.uniform(-0.5, 0.5, n_conn).astype(np.float32)
+    x = rng.uniform(-1, 1, n_units).astype(np.float32)
+    inputs = rng.uniform(-1, 1, (steps, 3)).astype(np.float32)
+    targets = rng.normal(size=steps).astype(np.float32)
+    rw, rx, rerr = oracle.ref_ipc_run(inputs, targets, w, x)
+    np.savez_compressed(HERE / "ipc_small.npz", w0=w, x0=x, inputs=inputs, targets=targets,
+                        w=rw, x=rx, err=rerr)
+
+
 if __name__ == "__main__":
     ob.build()
     if oracle.ref() is None:
         sys.exit("reference build missing: the reference tree is needed to make fixtures")
     sweep_hebbian_small()
     swifttd_small()
+    mlp_xor_small()
+    ipc_small()
     print("fixtures written to", HERE)

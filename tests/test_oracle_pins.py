@@ -148,3 +148,51 @@ def test_swifttd_f64_sums_stay_close_to_sequential_f32(orc):
     f64, v64, _ = _swifttd_oracle_run(orc, z["features"], z["rewards"], 1.0, acc_f64=True)
     np.testing.assert_allclose(v64, v32, rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(f64, f32, rtol=1e-5, atol=1e-6)
+
+
+def test_mlp_xor_oracle_matches_reference_fixture(orc):
+    """The Topological MLP restatement (forward per level, MSELoss, backward
+    per level, gradient update) against the reference's own mlp_xor.cpp
+    policies: bit for bit after 200 epochs of 4 DoSteps."""
+    z = np.load(GOLDEN / "mlp_xor_small.npz")
+    net = orc.MlpTopo([2, 8, 1], z["w_init"])
+    for _ in range(200):
+        for s in range(4):
+            net.step(z["inputs"][s], z["targets"][s])
+    np.testing.assert_array_equal(net.w.view(np.uint32), z["w_200"].view(np.uint32))
+    preds = np.array([net.forward(z["inputs"][s])[0] for s in range(4)], np.float32)
+    np.testing.assert_array_equal(preds.view(np.uint32), z["preds_200"].view(np.uint32))
+
+
+def test_mlp_xor_learns_xor_in_reference_fixture():
+    z = np.load(GOLDEN / "mlp_xor_small.npz")
+    assert np.array_equal(z["preds_5000"] > 0.5, z["targets"] > 0.5)
+
+
+def test_ipc_oracle_matches_reference_fixture(orc):
+    """The iPC restatement (pre-step, forward with eps = x - mu, Pipeline
+    backward in descending connection order, Hebbian update, value-node
+    update) against 30 steps of the example's own iPCStep, bit for bit."""
+    z = np.load(GOLDEN / "ipc_small.npz")
+    f, t, _ = fc_edges([3, 16, 1])
+    w, x = z["w0"].copy(), z["x0"].copy()
+    for s in range(z["targets"].size):
+        x[:3] = z["inputs"][s]
+        x[-1] = z["targets"][s]
+        err, _ = orc.ipc_step(f, t, w, x, z["inputs"][s], (3, 19), 0.1, 0.005)
+    np.testing.assert_array_equal(w.view(np.uint32), z["w"].view(np.uint32))
+    np.testing.assert_array_equal(x.view(np.uint32), z["x"].view(np.uint32))
+    np.testing.assert_array_equal(err.view(np.uint32), z["err"].view(np.uint32))
+
+
+def test_backward_descending_order_known_answer(orc):
+    # The shape of reference tests/test_plastix.cpp:202-226 (BackwardPassBasic:
+    # 2 inputs -> 1 output; BackwardAcc of each source collects Weight times
+    # the destination's value, and is cleared after Apply). With weights 2 and
+    # 3 and destination value 1 the sources' Apply sees 2 and 3.
+    f, t, n = fc_edges([2, 1])
+    w = np.array([2.0, 3.0], np.float32)
+    dval = np.zeros(n, np.float32)
+    dval[2] = 1.0
+    out = orc.backward(f, t, w, dval, n, 0, 2)
+    assert list(out[:2]) == [2.0, 3.0]
