@@ -40,8 +40,8 @@ WORKLOAD = "single sparse layer sweep, fwd + fused Hebbian trace update"
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--n-src", type=int, default=1 << 20)
     p.add_argument("--n-dst", type=int, default=1 << 20)
@@ -50,6 +50,11 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["sweep", "swifttd", "ipc", "structural"],
+                   default="sweep",
+                   help="sweep: the single-layer fwd+Hebbian sweep (default, the headline); "
+                        "swifttd: 4M-feature SwiftTD learner; ipc: 5-layer predictive-coding "
+                        "net; structural: prune/regrow/re-sort/forward step")
     return p.parse_args()
 
 
@@ -71,49 +76,58 @@ def traffic_per_launch(workload_key: str):
 
 
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples the SM clock and the clock-event reasons of one GPU while the
+    timed region runs: NVML (read-only queries) from a thread every 2 ms, so
+    even a timed region of a few milliseconds gets samples. Returns None when
+    NVML is unavailable. Nothing is changed on the GPU."""
 
-    def __init__(self, gpu_index: int):
-        self.path = tempfile.mktemp(prefix="plx_clocks_", suffix=".csv")
-        self.proc = None
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4),
+               ("hw_power_brake_slowdown", 0x80))
+
+    def __init__(self, device_index: int):
+        import threading
+
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.fh, stderr=subprocess.DEVNULL)
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((float(mhz), int(rs)))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.002)
+
+            self._thread = threading.Thread(target=poll, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
 
     def stop(self):
-        if self.proc is None:
+        if self._thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.fh.close()
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
+        self._stop.set()
+        self._thread.join(timeout=2)
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for name, v in zip(names, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        reasons = sorted({name for _, bits in self.samples for name, m in self.REASONS
+                          if bits & m})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
@@ -343,9 +357,272 @@ def run_ours(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# The other configurations (single GPU): SwiftTD, iPC, structural plasticity.
+# Each prints one JSON line of the same shape as the headline.
+# ---------------------------------------------------------------------------
+def _events(n):
+    import torch
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def _timed_loop(stream, fn, steps, warmup, sampler_device=0):
+    """W untimed calls, then K timed ones bracketed by synchronize; returns
+    (total ms, clocks)."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(sampler_device)
+    t0, t1 = _events(2)
+    t0.record(stream)
+    for i in range(steps):
+        fn(warmup + i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1), sampler.stop()
+
+
+def _cpu_time(step, budget_s, min_steps=2):
+    step()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        step()
+        n += 1
+        if time.perf_counter() - t0 >= budget_s and n >= min_steps:
+            break
+    return (time.perf_counter() - t0) / n
+
+
+def _line(args, workload, value, unit, ms_per_step, config, roofline, cpu, e2e, clocks,
+          launches, dtype="f32", extra=None):
+    line = {"metric": METRIC if workload == "sweep" else f"{unit} ({workload})",
+            "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded generators)", "config": config,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": launches}
+    if args.impl == "reference":
+        line = {"impl": "reference", "metric": line["metric"], "value": cpu["value"],
+                "unit": cpu["unit"], "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "dtype": dtype,
+                "data": line["data"], "config": config, "cpu_baseline": cpu,
+                "e2e": {"value": cpu["value"], "unit": cpu["unit"], "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+    if extra:
+        line.update(extra)
+    print(json.dumps(line), flush=True)
+
+
+def _roof(bytes_per_launch, launch_ms, traffic_key):
+    peak, kind = measured_peak_gbs()
+    achieved = bytes_per_launch / (launch_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": f"{kind} (MEASURED_PEAKS hbm_gbs)",
+            "traffic": traffic_per_launch(traffic_key), "kernel_ms": launch_ms,
+            "algorithmic_bytes_per_launch": bytes_per_launch}
+
+
+def bench_swifttd(args):
+    """C4: 4,194,304 binary features, 20,971 active per step (seeded random
+    sets), gamma 0.99, lambda 0.9, meta step size 1e-3, rewards N(0,1)."""
+    import numpy as np
+    import torch
+
+    from plastix_b200.runtime import Context, SwiftTDLearner
+
+    n, k, n_sets = 1 << 22, 20_971, 64
+    torch.cuda.set_device(0)
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    sets = [torch.sort(torch.randperm(n, generator=g, device="cuda")[:k])[0].to(torch.int32)
+            for _ in range(n_sets)]
+    rewards = torch.randn(max(args.steps + args.warmup, 1), generator=g, device="cuda")
+    td = SwiftTDLearner(ctx, n, gamma=0.99, lambda_=0.9, meta=1e-3, max_active=k)
+    cpu = None
+    if args.impl == "reference" or not args.no_cpu_baseline:
+        cpu = _swifttd_cpu(args, n, k)
+        if args.impl == "reference":
+            return _line(args, "swifttd", None, "feature-updates/s", None,
+                         {"workload": "SwiftTD", "n_features": n, "active": k}, None, cpu,
+                         None, None, 0)
+    ms, clocks = _timed_loop(ctx.stream, lambda i: td.step(sets[i % n_sets], rewards[i:i + 1]),
+                             args.steps, args.warmup)
+    # the dense pass alone (events between the two halves of the step)
+    e = _events(2 * 20)
+    for i in range(20):
+        td.step_parts(sets[i % n_sets], rewards[i:i + 1], between=lambda j=i: e[2 * j].record())
+        e[2 * i + 1].record()
+    torch.cuda.synchronize()
+    dense_ms = statistics.mean(e[2 * i].elapsed_time(e[2 * i + 1]) for i in range(20))
+    # end to end: the active list and reward from pinned host memory, V back
+    h_sets = [s.cpu().pin_memory() for s in sets[:8]]
+    h_rw = rewards[:8].cpu().pin_memory()
+    d_idx = torch.empty(k, dtype=torch.int32, device="cuda")
+    d_rw = torch.empty(1, device="cuda")
+    h_v = torch.empty(1, pin_memory=True)
+
+    def e2e(i):
+        d_idx.copy_(h_sets[i % 8], non_blocking=True)
+        d_rw.copy_(h_rw[i % 8:i % 8 + 1], non_blocking=True)
+        v = td.step(d_idx, d_rw)
+        h_v.copy_(v, non_blocking=True)
+    ems, _ = _timed_loop(ctx.stream, e2e, args.steps, args.warmup)
+    ctx.sync()
+    value = n * args.steps / (ms / 1e3)
+    algo = 72 * n  # dense pass: 8 fields read, 10 written, 4 B each
+    _line(args, "swifttd", value, "feature-updates/s", ms / args.steps,
+          {"workload": "SwiftTD linear TD learner", "n_features": n, "active_per_step": k,
+           "gamma": 0.99, "lambda": 0.9, "meta": 1e-3,
+           "l2": "inputs larger than L2: 168 MB of per-feature state per step"},
+          _roof(algo, dense_ms, "swifttd_dense_4M"), cpu,
+          {"value": n * args.steps / (ems / 1e3), "unit": "feature-updates/s",
+           "h2d_bytes_per_step": 4 * k + 4, "d2h_bytes_per_step": 4},
+          clocks, 3 * args.steps,
+          extra={"dense_pass_ms": dense_ms, "step_overhead_ms": ms / args.steps - dense_ms})
+
+
+def _swifttd_cpu(args, n, k):
+    import numpy as np
+
+    from oracle import oracle
+    rng = np.random.default_rng(args.seed)
+    f = np.zeros(n, np.float32)
+    f[rng.choice(n, k, replace=False)] = 1.0
+    R = oracle.ref()
+    if R is not None:
+        feats = f[None, :]
+        rw = np.zeros(1, np.float32)
+        out = np.empty((10, n), np.float32)
+        v = np.empty(1, np.float32)
+
+        def step():  # network construction excluded below: time DoStep only
+            R.ref_swifttd_example_run(n, oracle._p(feats), oracle._p(rw), 1, 0.05,
+                                      oracle._p(out), oracle._p(v))
+        t_one = _cpu_time(step, args.cpu_seconds / 2, 1)
+        feats3 = np.repeat(f[None, :], 3, axis=0)
+        rw3 = np.zeros(3, np.float32)
+
+        def step3():
+            R.ref_swifttd_example_run(n, oracle._p(feats3), oracle._p(rw3), 3, 0.05,
+                                      oracle._p(out), oracle._p(v))
+        t_three = _cpu_time(step3, args.cpu_seconds / 2, 1)
+        per_step = max((t_three - t_one) / 2, 1e-9)
+        return {"value": n / per_step, "unit": "feature-updates/s", "cores": 1,
+                "kind": "reference",
+                "sample": f"reference SwiftTD example network ({n} features, {k} active; its "
+                          "fixed gamma 1.0, same work per step), DoStep time from runs of 1 and 3 "
+                          "steps (construction cancels out)"}
+    fields = oracle.td_fields(n)
+    g = oracle.td_globals()
+    per_step = _cpu_time(lambda: oracle.swifttd_step(fields, f, 0.5, g), args.cpu_seconds, 2)
+    return {"value": n / per_step, "unit": "feature-updates/s", "cores": 1, "kind": "port",
+            "sample": f"oracle SwiftTD step, {n} features, {k} active"}
+
+
+def bench_ipc(args):
+    """C5: 5 layers of 262,144 units, 2,048 random sources per destination
+    (2^31 connections), weights N(0, 1/2048), inputs U(0,1); a sample = 20
+    inference iterations (forward, Pipeline backward, value update) + one
+    weight update. One timed step = one sample."""
+    import math
+
+    import torch
+
+    from plastix_b200.runtime import Context, PredictiveCodingNet
+
+    S, F, iters = 1 << 18, 2048, 20
+    torch.cuda.set_device(0)
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    begin = [i * S for i in range(6)]
+    blocks = []
+    for l in range(4):
+        f = torch.randint(begin[l], begin[l] + S, (S * F,), generator=g, device="cuda",
+                          dtype=torch.int32)
+        t = (torch.arange(S, device="cuda", dtype=torch.int32) + begin[l + 1]).repeat_interleave(F)
+        w = torch.randn(S * F, generator=g, device="cuda") * (1.0 / math.sqrt(F))
+        blocks.append((f, t, w))
+    net = PredictiveCodingNet(ctx, [S] * 5, blocks, gamma=0.1, alpha=0.005)
+    blocks = None
+    inputs = torch.rand(S, generator=g, device="cuda")
+    targets = torch.rand(S, generator=g, device="cuda") * 2 - 1
+    E, Eb = 4 * S * F, 3 * S * F
+
+    def sample(i):
+        net.clamp(inputs, targets)
+        for _ in range(iters):
+            net.iteration()
+        net.update()
+    steps = max(1, min(args.steps, 5))
+    ms, clocks = _timed_loop(ctx.stream, sample, steps, min(args.warmup, 3))
+    # per-launch view of the dominant sweep (forward, all four blocks)
+    e = _events(2)
+    e[0].record()
+    for _ in range(5):
+        net.forward()
+    e[1].record()
+    torch.cuda.synchronize()
+    fwd_ms = e[0].elapsed_time(e[1]) / 5
+    ctx.sync()
+    visits = iters * (E + Eb) + (E + Eb)
+    per_sample = ms / steps
+    _line(args, "ipc", visits / (per_sample / 1e3), "connection-visits/s", per_sample,
+          {"workload": "multilayer sparse predictive coding (iPC)", "layers": 5,
+           "units_per_layer": S, "fan_in": F, "connections": E, "iterations_per_sample": iters,
+           "counting": "per sample: 20 x (forward over all connections + backward over the "
+                       "hidden-source ones) + one update of both copies",
+           "l2": "inputs larger than L2: 16 GiB of destination-major connections"},
+          _roof(8 * E, fwd_ms, "ipc_forward_2G"), None,
+          None, clocks, None, extra={"forward_ms": fwd_ms, "samples": steps})
+
+
+def bench_structural(args):
+    """C3: 2^23 sources, 2^23 destinations, 2^24 connections dst-sorted,
+    w N(0, 0.1^2), u8 age; prune |w| < 0.02 by compaction, regrow the same
+    number, radix-sort by destination, forward sweep."""
+    import torch
+
+    from plastix_b200.runtime import Context, StructuralLayer
+
+    n_src = n_dst = 1 << 23
+    n = 1 << 24
+    torch.cuda.set_device(0)
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    src = torch.randint(0, n_src, (n,), generator=g, device="cuda")
+    dst = torch.randint(0, n_dst, (n,), generator=g, device="cuda")
+    dst, order = torch.sort(dst, stable=True)
+    f = src[order].to(torch.int32)
+    t = (dst + n_src).to(torch.int32)
+    w = torch.randn(n, generator=g, device="cuda") * 0.1
+    age = torch.randint(0, 256, (n,), generator=g, device="cuda").to(torch.uint8)
+    act = torch.rand(n_src, generator=g, device="cuda")
+    del src, dst, order
+    layer = StructuralLayer(ctx, n_src, n_dst, f, t, w, age, threshold=0.02, seed=11)
+    steps = max(1, min(args.steps, 50))
+    ms, clocks = _timed_loop(ctx.stream, lambda i: layer.step(act), steps, args.warmup)
+    ctx.sync()
+    _line(args, "structural", n * steps / (ms / 1e3), "connections/s", ms / steps,
+          {"workload": "structural plasticity step", "n_src": n_src, "n_dst": n_dst,
+           "connections": n, "prune": "|w| < 0.02", "steps": steps},
+          None, None, None, clocks, None)
+
+
+def run_other(args):
+    if args.gpus != 1:
+        raise SystemExit(f"--workload {args.workload} runs on one GPU")
+    return {"swifttd": bench_swifttd, "ipc": bench_ipc,
+            "structural": bench_structural}[args.workload](args) or 0
+
+
 def main():
     args = parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
+    if args.workload != "sweep":
+        return run_other(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

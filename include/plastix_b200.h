@@ -336,6 +336,22 @@ int plx_swifttd_step(plx_ctx* ctx, uint64_t n_features, float* const* fields,
                      plx_td_globals* globals, float* v_out, void* scratch,
                      uint64_t scratch_bytes);
 
+/* The two halves of plx_swifttd_step, for callers that time or schedule
+ * them apart: plx_swifttd_reduce is DoForwardPass + Loss and the global sums
+ * of phase 1 over the active features (V, Delta, VDeltaPrev, Tau, B,
+ * VDelta into *globals); plx_swifttd_apply is the dense pass over all
+ * features (phases 1 and 2, ResetGlobal). Same arguments and rules as
+ * plx_swifttd_step; apply must follow reduce with the same active list. */
+int plx_swifttd_reduce(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+                       const uint32_t* active_idx, const float* active_val,
+                       uint32_t n_active, const float* reward,
+                       plx_td_globals* globals, float* v_out, void* scratch,
+                       uint64_t scratch_bytes);
+int plx_swifttd_apply(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+                      const uint32_t* active_idx, const float* active_val,
+                      uint32_t n_active, plx_td_globals* globals, void* scratch,
+                      uint64_t scratch_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,6 +91,10 @@ _SIGNATURES = {
     "plx_swifttd_scratch_bytes": (c_uint64, [c_uint64, c_uint32]),
     "plx_swifttd_step": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),
+    "plx_swifttd_reduce": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
+                                   c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),
+    "plx_swifttd_apply": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
+                                  c_void_p, c_void_p, c_uint64]),
     "plx_regrow": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_uint64,
                            c_uint64]),

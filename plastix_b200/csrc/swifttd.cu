@@ -528,11 +528,15 @@ extern "C" uint64_t plx_swifttd_scratch_bytes(uint64_t n_features, uint32_t max_
   return td_scratch_layout(n_features, &op, &os);
 }
 
-extern "C" int plx_swifttd_step(plx_ctx* ctx, uint64_t n_features,
-                                float* const* fields, const uint32_t* active_idx,
-                                const float* active_val, uint32_t n_active,
-                                const float* reward, plx_td_globals* globals,
-                                float* v_out, void* scratch, uint64_t scratch_bytes) {
+namespace {
+
+constexpr int kTdRunReduce = 1;  // k_td_value + k_td_terms
+constexpr int kTdRunApply = 2;   // k_td_dense
+
+int td_launch(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+              const uint32_t* active_idx, const float* active_val, uint32_t n_active,
+              const float* reward, plx_td_globals* globals, float* v_out, void* scratch,
+              uint64_t scratch_bytes, int parts) {
   PLX_CHECK_ARG(ctx && fields && reward && globals && scratch,
                 "ctx, fields, reward, globals and scratch are required");
   PLX_CHECK_ARG(n_features > 0 && n_features <= 0xFFFFFFFFull,
@@ -580,18 +584,51 @@ extern "C" int plx_swifttd_step(plx_ctx* ctx, uint64_t n_features,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(td_active_blocks(n_active));
-  cfg.blockDim = dim3(kTdAThreads);
-  cfg.dynamicSmemBytes = 0;
   cfg.stream = ctx->stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  PLX_TRY_CUDA(cudaLaunchKernelEx(&cfg, k_td_value, a, fl));
-  PLX_TRY_CUDA(cudaLaunchKernelEx(&cfg, k_td_terms, a, fl));
-
-  cfg.gridDim = dim3((unsigned)std::min<uint64_t>(a.n_tiles, 2ull * (uint64_t)ctx->num_sms));
-  cfg.blockDim = dim3(kTdThreads);
-  cfg.dynamicSmemBytes = smem;
-  PLX_TRY_CUDA(cudaLaunchKernelEx(&cfg, k_td_dense, a, fl, (uint64_t)ctx->timeout_ns));
+  if (parts & kTdRunReduce) {
+    cfg.gridDim = dim3(td_active_blocks(n_active));
+    cfg.blockDim = dim3(kTdAThreads);
+    cfg.dynamicSmemBytes = 0;
+    PLX_TRY_CUDA(cudaLaunchKernelEx(&cfg, k_td_value, a, fl));
+    PLX_TRY_CUDA(cudaLaunchKernelEx(&cfg, k_td_terms, a, fl));
+  }
+  if (parts & kTdRunApply) {
+    cfg.gridDim =
+        dim3((unsigned)std::min<uint64_t>(a.n_tiles, 2ull * (uint64_t)ctx->num_sms));
+    cfg.blockDim = dim3(kTdThreads);
+    cfg.dynamicSmemBytes = smem;
+    PLX_TRY_CUDA(cudaLaunchKernelEx(&cfg, k_td_dense, a, fl, (uint64_t)ctx->timeout_ns));
+  }
   return PLX_OK;
+}
+
+}  // namespace
+
+extern "C" int plx_swifttd_step(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+                                const uint32_t* active_idx, const float* active_val,
+                                uint32_t n_active, const float* reward,
+                                plx_td_globals* globals, float* v_out, void* scratch,
+                                uint64_t scratch_bytes) {
+  return td_launch(ctx, n_features, fields, active_idx, active_val, n_active, reward, globals,
+                   v_out, scratch, scratch_bytes, kTdRunReduce | kTdRunApply);
+}
+
+extern "C" int plx_swifttd_reduce(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+                                  const uint32_t* active_idx, const float* active_val,
+                                  uint32_t n_active, const float* reward,
+                                  plx_td_globals* globals, float* v_out, void* scratch,
+                                  uint64_t scratch_bytes) {
+  return td_launch(ctx, n_features, fields, active_idx, active_val, n_active, reward, globals,
+                   v_out, scratch, scratch_bytes, kTdRunReduce);
+}
+
+extern "C" int plx_swifttd_apply(plx_ctx* ctx, uint64_t n_features, float* const* fields,
+                                 const uint32_t* active_idx, const float* active_val,
+                                 uint32_t n_active, plx_td_globals* globals, void* scratch,
+                                 uint64_t scratch_bytes) {
+  static const float kNoReward = 0.0f;  // not read by the dense pass
+  return td_launch(ctx, n_features, fields, active_idx, active_val, n_active, &kNoReward,
+                   globals, nullptr, scratch, scratch_bytes, kTdRunApply);
 }

@@ -382,6 +382,23 @@ class SwiftTDLearner:
              _ptr(self.globals), _ptr(self.v), _ptr(self.scratch), self.scratch.numel())
         return self.v
 
+    def step_parts(self, active_idx: torch.Tensor, reward: torch.Tensor,
+                   active_val: Optional[torch.Tensor] = None, between=None) -> torch.Tensor:
+        """``step`` as its two halves (active-set reductions, then the dense
+        pass), calling ``between()`` in between (e.g. to record an event)."""
+        k = int(active_idx.numel())
+        if k > self.max_active:
+            raise ValueError("more active features than max_active")
+        idx = _ptr(active_idx) if k else None
+        call("plx_swifttd_reduce", self.ctx.handle, self.n, self._ptrs, idx, _ptr(active_val),
+             k, _ptr(reward), _ptr(self.globals), _ptr(self.v), _ptr(self.scratch),
+             self.scratch.numel())
+        if between is not None:
+            between()
+        call("plx_swifttd_apply", self.ctx.handle, self.n, self._ptrs, idx, _ptr(active_val), k,
+             _ptr(self.globals), _ptr(self.scratch), self.scratch.numel())
+        return self.v
+
 
 # ---------------------------------------------------------------------------
 # Backward sweep (K2): a source-major copy of a connection range

@@ -118,3 +118,22 @@ def test_swifttd_full_size(ctx, orc):
     sets = active_sets(n, k, steps, seed=17)
     rewards = np.random.default_rng(18).normal(size=steps).astype(np.float32)
     check(*run_both(ctx, orc, n, sets, rewards))
+
+
+def test_swifttd_step_parts_equal_step(ctx):
+    """plx_swifttd_reduce + plx_swifttd_apply give the same bits as
+    plx_swifttd_step."""
+    n, k, steps = 50_000, 400, 6
+    sets = active_sets(n, k, steps, seed=30)
+    rw = torch.from_numpy(np.random.default_rng(31).normal(size=steps).astype(np.float32)).cuda()
+    a = SwiftTDLearner(ctx, n, max_active=k)
+    b = SwiftTDLearner(ctx, n, max_active=k)
+    for s, idx in enumerate(sets):
+        idx_d = torch.from_numpy(idx.view(np.int32)).cuda()
+        a.step(idx_d, rw[s:s + 1])
+        b.step_parts(idx_d, rw[s:s + 1])
+    ctx.sync()
+    np.testing.assert_array_equal(a.fields().cpu().numpy().view(np.uint32),
+                                  b.fields().cpu().numpy().view(np.uint32))
+    np.testing.assert_array_equal(a.globals.cpu().numpy().view(np.uint32),
+                                  b.globals.cpu().numpy().view(np.uint32))
