@@ -439,7 +439,8 @@ def bench_swifttd(args):
     g = torch.Generator(device="cuda").manual_seed(args.seed)
     sets = [torch.sort(torch.randperm(n, generator=g, device="cuda")[:k])[0].to(torch.int32)
             for _ in range(n_sets)]
-    rewards = torch.randn(max(args.steps + args.warmup, 1), generator=g, device="cuda")
+    n_rw = max(args.steps + args.warmup, 64)
+    rewards = torch.randn(n_rw, generator=g, device="cuda")
     td = SwiftTDLearner(ctx, n, gamma=0.99, lambda_=0.9, meta=1e-3, max_active=k)
     cpu = None
     if args.impl == "reference" or not args.no_cpu_baseline:
@@ -453,7 +454,8 @@ def bench_swifttd(args):
     # the dense pass alone (events between the two halves of the step)
     e = _events(2 * 20)
     for i in range(20):
-        td.step_parts(sets[i % n_sets], rewards[i:i + 1], between=lambda j=i: e[2 * j].record())
+        td.step_parts(sets[i % n_sets], rewards[i % n_rw:i % n_rw + 1],
+                      between=lambda j=i: e[2 * j].record())
         e[2 * i + 1].record()
     torch.cuda.synchronize()
     dense_ms = statistics.mean(e[2 * i].elapsed_time(e[2 * i + 1]) for i in range(20))
@@ -545,7 +547,7 @@ def bench_ipc(args):
         t = (torch.arange(S, device="cuda", dtype=torch.int32) + begin[l + 1]).repeat_interleave(F)
         w = torch.randn(S * F, generator=g, device="cuda") * (1.0 / math.sqrt(F))
         blocks.append((f, t, w))
-    net = PredictiveCodingNet(ctx, [S] * 5, blocks, gamma=0.1, alpha=0.005)
+    net = PredictiveCodingNet(ctx, [S] * 5, blocks, gamma=0.1, alpha=0.005, layout="chunked")
     blocks = None
     inputs = torch.rand(S, generator=g, device="cuda")
     targets = torch.rand(S, generator=g, device="cuda") * 2 - 1
@@ -574,8 +576,11 @@ def bench_ipc(args):
            "units_per_layer": S, "fan_in": F, "connections": E, "iterations_per_sample": iters,
            "counting": "per sample: 20 x (forward over all connections + backward over the "
                        "hidden-source ones) + one update of both copies",
-           "l2": "inputs larger than L2: 16 GiB of destination-major connections"},
-          _roof(8 * E, fwd_ms, "ipc_forward_2G"), None,
+           "layout": "chunked-source (16-bit source offsets, 16384-source chunks in shared "
+                     "memory)",
+           "roofline_bytes": "forward: 6 B per connection (16-bit offset + weight)",
+           "l2": "inputs larger than L2: 12 GiB of destination-major connections"},
+          _roof(6 * E, fwd_ms, "ipc_forward_2G"), None,
           None, clocks, None, extra={"forward_ms": fwd_ms, "samples": steps})
 
 

@@ -40,7 +40,7 @@ extern "C" {
 /* Rows (destination units) with at most this many connections are summed
  * strictly left to right, exactly like the reference loop. Longer rows use a
  * fixed deterministic order: 32 lane-strided partial sums (every 32nd
- * connection) folded in lane order; rows over 2048 connections use 256
+ * connection) folded in lane order; rows over 8192 connections use 256
  * thread-strided partial sums. */
 #define PLX_SEQ_ROW_MAX 256
 
@@ -81,8 +81,8 @@ typedef struct plx_csr {
   uint64_t n_edges;        /* == row_ptr[n_rows], < 2^32 - 2^16             */
   uint32_t n_rows;
   uint32_t row_base;       /* unit id of row 0 (ToId of its connections)    */
-  uint32_t n_wide;         /* rows with PLX_SEQ_ROW_MAX < length <= 2048    */
-  uint32_t n_long;         /* rows longer than 2048                         */
+  uint32_t n_wide;         /* rows with PLX_SEQ_ROW_MAX < length <= 8192    */
+  uint32_t n_long;         /* rows longer than 8192                         */
   uint32_t n_short;        /* rows of at most PLX_SEQ_ROW_MAX (incl. empty) */
   uint32_t max_row;        /* connections in the longest row                */
 } plx_csr;
@@ -294,6 +294,64 @@ int plx_ipc_value_update(plx_ctx* ctx, uint64_t n, float* x, const float* eps,
  * units (mlp_xor.cpp:43-46): grad = ((a - target) * a) * (1 - a). */
 int plx_mse_sigmoid_grad(plx_ctx* ctx, uint64_t n, const float* act,
                          const float* target, float* grad);
+
+/* ---- chunked-source layout for long rows --------------------------------- */
+
+/* Sources per chunk: a chunk of gathered values (64 KB) sits in one CTA's
+ * shared memory while it folds the chunk's share of many rows. */
+#define PLX_CHUNK_SOURCES 16384
+
+/* Connections of a row set stored by (chunk of the gathered side, row), each
+ * (chunk, row) segment padded to a multiple of 4 connections; src holds the
+ * 16-bit offset within the chunk (PLX_CHUNK_SOURCES marks padding, which
+ * reads 0), perm the original connection index (0xFFFFFFFF for padding).
+ * n_chunks = ceil(n_src / PLX_CHUNK_SOURCES). For rows of hundreds or
+ * thousands of connections (the 2,048-fan-in multilayer network), where
+ * global-memory gathers, not HBM, bound a CSR sweep. */
+typedef struct plx_chunked {
+  const uint32_t* seg_ptr; /* [n_chunks * n_rows + 1], chunk-major          */
+  const uint16_t* src;     /* [n_padded]                                     */
+  const uint32_t* perm;    /* [n_padded]                                     */
+  uint32_t n_rows;
+  uint32_t n_src;          /* gathered values per sweep                      */
+  uint32_t n_chunks;
+} plx_chunked;
+
+/* Upper bound of the padded length (allocate src/perm/weights with it). */
+uint64_t plx_chunked_max_padded(uint64_t n_edges, uint32_t n_rows, uint32_t n_src);
+size_t plx_chunked_scratch_bytes(uint64_t n_edges, uint32_t n_rows, uint32_t n_src);
+
+/* Builds the layout of n_edges connections whose gathered unit is gather_id
+ * (units [src_base, src_base + n_src)) and whose row unit is row_id (units
+ * [row_base, row_base + n_rows)); connections outside either range are left
+ * out. Within a segment connections keep their index order. Forward sweep:
+ * gather_id = FromId, row_id = ToId; backward: gather_id = ToId,
+ * row_id = FromId. n_edges < 2^30 per call. */
+int plx_chunked_build(plx_ctx* ctx, uint64_t n_edges, const uint32_t* gather_id,
+                      uint32_t src_base, uint32_t n_src, const uint32_t* row_id,
+                      uint32_t row_base, uint32_t n_rows, uint32_t* seg_ptr,
+                      uint16_t* src, uint32_t* perm, void* scratch,
+                      size_t scratch_bytes);
+
+/* out[d] = field[perm[d]] (0 for padding): a connection field in layout order. */
+int plx_chunked_gather(plx_ctx* ctx, uint64_t n_padded, const uint32_t* perm,
+                       const float* field, float* out);
+
+/* Row sweep over the layout: acc[r] = sum over the row's connections of
+ * w * gathered[src] -- per chunk a lane-strided sum, chunks added in order
+ * (deterministic; not the reference's left fold) -- then the apply rule:
+ * out[r] = Apply(acc[r], value[r]). partial: n_chunks * n_rows floats. */
+int plx_chunked_fold(plx_ctx* ctx, const plx_chunked* layout, const float* w,
+                     const float* gathered, int apply_kind, const float* value,
+                     float* out, float* partial);
+
+/* Per-connection update over the layout with row_val[r] as the row value and
+ * gathered[src] as the other side, PLX_UPDATE_* rules with the rounding of
+ * plx_sweep_update (a weight updated here equals the same rule applied to the
+ * destination-major copy, bit for bit). Padding stays 0. */
+int plx_chunked_update(plx_ctx* ctx, const plx_chunked* layout, float* w,
+                       const float* gathered, const float* row_val, int update_kind,
+                       float rate);
 
 /* ---- SwiftTD (examples/swifttd/swifttd.cpp) ------------------------------ */
 

@@ -30,6 +30,7 @@ UPDATE_HEBBIAN = 2
 UPDATE_HEBBIAN_T = 3
 
 SEQ_ROW_MAX = 256
+CHUNK_SOURCES = 16384
 
 
 class PlxError(RuntimeError):
@@ -43,6 +44,11 @@ class Csr(ctypes.Structure):
                 ("n_edges", c_uint64), ("n_rows", c_uint32), ("row_base", c_uint32),
                 ("n_wide", c_uint32), ("n_long", c_uint32), ("n_short", c_uint32),
                 ("max_row", c_uint32)]
+
+
+class Chunked(ctypes.Structure):
+    _fields_ = [("seg_ptr", c_void_p), ("src", c_void_p), ("perm", c_void_p),
+                ("n_rows", c_uint32), ("n_src", c_uint32), ("n_chunks", c_uint32)]
 
 
 class Field(ctypes.Structure):
@@ -88,6 +94,16 @@ _SIGNATURES = {
     "plx_ipc_value_update": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_float,
                                      c_void_p, c_int]),
     "plx_mse_sigmoid_grad": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p]),
+    "plx_chunked_max_padded": (c_uint64, [c_uint64, c_uint32, c_uint32]),
+    "plx_chunked_scratch_bytes": (ctypes.c_size_t, [c_uint64, c_uint32, c_uint32]),
+    "plx_chunked_build": (c_int, [c_void_p, c_uint64, c_void_p, c_uint32, c_uint32, c_void_p,
+                                  c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  ctypes.c_size_t]),
+    "plx_chunked_gather": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p]),
+    "plx_chunked_fold": (c_int, [c_void_p, POINTER(Chunked), c_void_p, c_void_p, c_int,
+                                 c_void_p, c_void_p, c_void_p]),
+    "plx_chunked_update": (c_int, [c_void_p, POINTER(Chunked), c_void_p, c_void_p, c_void_p,
+                                   c_int, c_float]),
     "plx_swifttd_scratch_bytes": (c_uint64, [c_uint64, c_uint32]),
     "plx_swifttd_step": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),

@@ -143,6 +143,45 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// L2 cache policies for per-instruction hints: streamed connection data is
+// marked evict-first, the gathered activation array evict-last, so the
+// streams do not push the small, much re-read activation array out of L2.
+// The hints change no state beyond the accesses that carry them.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p, uint64_t pol) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ float ld_keep_f32(const float* p, uint64_t pol) {
+  float v;
+  asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ void st_stream_v4(void* p, float4 v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;"
+               ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol)
+               : "memory");
+}
+
+// Asks the TMA unit to bring [p, p + bytes) into L2 (no completion, no data
+// returned). p and bytes must be multiples of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
+               : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before subsequent
 // async-proxy (bulk store) reads of the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -151,6 +190,37 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ void record_status(int32_t* status, int32_t code) {
   if (status) atomicCAS(status, kStatusOk, code);
+}
+
+// ---------------------------------------------------------------------------
+// Apply rules of the row sweeps (one value per destination / source row).
+// Reference evaluation order, separate roundings.
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr bool apply_reads_value(int kind) {
+  return kind == PLX_APPLY_IPC_ERROR || kind == PLX_APPLY_SIGMOID_GRAD ||
+         kind == PLX_APPLY_TANH_GRAD;
+}
+
+template <int APPLY>
+__device__ __forceinline__ float apply_value(float acc, float v) {
+  if constexpr (APPLY == PLX_APPLY_IDENTITY) {
+    return acc;  // traits.hpp:115-117
+  } else if constexpr (APPLY == PLX_APPLY_SIGMOID) {
+    // mlp_xor.cpp:24-26. exp in double precision, rounded once to float: the
+    // correctly rounded single-precision exponential (up to rare near-halfway
+    // cases), which is also what the host's expf returns to within its
+    // half-ulp accuracy, so long training runs do not drift from the reference.
+    return 1.0f / __fadd_rn(1.0f, (float)exp(-(double)acc));
+  } else if constexpr (APPLY == PLX_APPLY_TANH) {
+    return tanhf(acc);
+  } else if constexpr (APPLY == PLX_APPLY_SIGMOID_GRAD) {
+    return __fmul_rn(__fmul_rn(acc, v), __fsub_rn(1.0f, v));  // mlp_xor.cpp:43-46
+  } else if constexpr (APPLY == PLX_APPLY_TANH_GRAD) {
+    const float t = tanhf(v);  // ipc_multilayer.cpp:128-131,170-175
+    return __fmul_rn(__fsub_rn(1.0f, __fmul_rn(t, t)), acc);
+  } else {
+    return __fsub_rn(v, acc);  // PLX_APPLY_IPC_ERROR, ipc_multilayer.cpp:147-150
+  }
 }
 
 template <typename T>

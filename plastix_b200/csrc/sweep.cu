@@ -190,26 +190,9 @@ __global__ void k_plan_rows(const uint32_t* __restrict__ row_ptr,
 template <int APPLY>
 __device__ __forceinline__ float apply_row(float acc, uint32_t r,
                                            const SweepArgs& a, bool owned) {
-  float post;
-  if constexpr (APPLY == PLX_APPLY_IDENTITY) {
-    post = acc;
-  } else if constexpr (APPLY == PLX_APPLY_SIGMOID) {
-    // exp in double precision, rounded once to float: the correctly rounded
-    // single-precision exponential (up to rare near-halfway cases), which is
-    // also what the host's expf returns to within its half-ulp accuracy, so
-    // long training runs do not drift from the reference.
-    post = 1.0f / __fadd_rn(1.0f, (float)exp(-(double)acc));
-  } else if constexpr (APPLY == PLX_APPLY_TANH) {
-    post = tanhf(acc);
-  } else if constexpr (APPLY == PLX_APPLY_SIGMOID_GRAD) {
-    const float v = __ldg(a.value + r);
-    post = __fmul_rn(__fmul_rn(acc, v), __fsub_rn(1.0f, v));
-  } else if constexpr (APPLY == PLX_APPLY_TANH_GRAD) {
-    const float t = tanhf(__ldg(a.value + r));
-    post = __fmul_rn(__fsub_rn(1.0f, __fmul_rn(t, t)), acc);
-  } else {
-    post = __fsub_rn(__ldg(a.value + r), acc);
-  }
+  float v = 0.0f;
+  if constexpr (apply_reads_value(APPLY)) v = __ldg(a.value + r);
+  const float post = apply_value<APPLY>(acc, v);
   if (owned) {
     if constexpr (APPLY == PLX_APPLY_IPC_ERROR) a.err_out[r] = post;
     else a.act_dst[r] = post;
@@ -944,8 +927,9 @@ __device__ __forceinline__ void storev(float* base, uint32_t k0, uint32_t mask,
 //      writes the row value over the row's products;
 //   3  (update) coalesced reloads of Weight/Trace, trace/weight update from
 //      the staged activation and row value, coalesced stores.
-template <uint32_t TB, int KB, int NW>
+template <uint32_t TB, int KB, int NW, int MINB = 1>
 struct WTileCfg {
+  static constexpr int kMinBlocks = MINB;  // CTAs per SM the register budget targets
   static constexpr uint32_t kTileBlocks = TB;                        // plan blocks per tile
   static constexpr uint32_t kTileCap = TB * kPlanG + kSeqMax + 8;    // connections
   static constexpr uint32_t kTileVec = (kTileCap + 127) / 128;       // 4-wide steps
@@ -957,7 +941,8 @@ struct WTileCfg {
 };
 
 template <class C, int APPLY, bool UPD, bool DEAD>
-__global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs a) {
+__global__ void __launch_bounds__(C::kWarpsPerCta * 32, C::kMinBlocks)
+    k_sweep_wtile(SweepArgs a) {
   constexpr uint32_t kTileBlocks = C::kTileBlocks;
   constexpr uint32_t kTileVec = C::kTileVec;
   constexpr int kWarpsPerCta = C::kWarpsPerCta;
@@ -974,12 +959,46 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs 
   float* sa = s_tile + (kWarpsPerCta + wid) * kStride;  // used only by update sweeps
   const uint64_t n = a.n_edges;
   const uint32_t len1 = a.act_src_len - 1u;
+  const uint64_t pol_first = l2_policy_evict_first();
+  const uint64_t pol_last = l2_policy_evict_last();
   bool bad = false;
+  // Each warp holds two tiles: the one it works on and the next, whose
+  // connection ranges (FromId, Weight, Trace, row offsets) it asks the TMA
+  // unit to prefetch into L2 right away. The DRAM stream then runs ahead of
+  // the warps without registers or shared memory; the warp's own loads of
+  // the next tile hit L2.
+  auto prefetch_tile = [&](uint32_t tp) {
+    const uint32_t pb0 = tp * kTileBlocks;
+    const uint32_t pb1 = (uint32_t)min_u64((uint64_t)pb0 + kTileBlocks, nb);
+    const uint32_t* Q0 = plan + kPlanHdr + 3 * pb0;
+    const uint32_t* Q1 = plan + kPlanHdr + 3 * pb1;
+    const uint32_t plo = Q0[2] & ~3u, phi = Q1[2];
+    const uint64_t end = min_u64((uint64_t)phi + 3, n) & ~3ull;  // whole 16 B, inside
+    if (end > plo) {
+      const uint32_t bytes = (uint32_t)(end - plo) * 4u;
+      prefetch_l2_bulk(a.src + plo, bytes);
+      prefetch_l2_bulk(a.w_in + plo, bytes);
+      if constexpr (UPD) prefetch_l2_bulk(a.e_in + plo, bytes);
+    }
+    const uint32_t r0 = Q0[0] & ~3u;
+    const uint32_t r1 = min(Q1[0] + 4u, a.n_rows) & ~3u;  // row_ptr has n_rows + 1 entries
+    if (r1 > r0) prefetch_l2_bulk(a.row_ptr + r0, (r1 - r0) * 4u);
+  };
+  uint32_t t_cur = 0;
+  if (lane == 0) {
+    t_cur = atomicAdd(a.queue, 1u);
+    if (t_cur < n_tiles) prefetch_tile(t_cur);
+  }
+  t_cur = __shfl_sync(kFull, t_cur, 0);
   for (;;) {
-    uint32_t t = 0;
-    if (lane == 0) t = atomicAdd(a.queue, 1u);
-    t = __shfl_sync(kFull, t, 0);
+    const uint32_t t = t_cur;
     if (t >= n_tiles) break;
+    uint32_t t_nxt = 0;
+    if (lane == 0) {
+      t_nxt = atomicAdd(a.queue, 1u);
+      if (t_nxt < n_tiles) prefetch_tile(t_nxt);
+    }
+    t_cur = __shfl_sync(kFull, t_nxt, 0);
     const uint32_t b0 = t * kTileBlocks;
     const uint32_t b1 = (uint32_t)min_u64((uint64_t)b0 + kTileBlocks, nb);
     const uint32_t* P0 = plan + kPlanHdr + 3 * b0;
@@ -999,7 +1018,12 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs 
       for (int h = 0; h < kB; ++h) {
         const uint32_t k = base + 128 * (v0 + h) + 4 * lane;
         if (v0 + h < nv) {
-          loadv<4>(a.src, k, n, sid[h]);
+          if ((uint64_t)k + 4 <= n) {
+            const uint4 x = ld_stream_v4(a.src + k, pol_first);
+            sid[h][0] = x.x; sid[h][1] = x.y; sid[h][2] = x.z; sid[h][3] = x.w;
+          } else {
+            loadv<4>(a.src, k, n, sid[h]);
+          }
           loadv<4>(a.w_in, k, n, w[h]);
           if constexpr (DEAD) loadv_u8<4>(a.dead, k, n, dd[h]);
         }
@@ -1014,7 +1038,7 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs 
           const bool in = v0 + h < nv && k + c >= lo && k + c < hi;
           const uint32_t sj = in ? sid[h][c] : 0u;
           smax = max(smax, sj);
-          av[h][c] = __ldg(a.act_src + min(sj, len1));
+          av[h][c] = ld_keep_f32(a.act_src + min(sj, len1), pol_last);
         }
       }
       bad |= smax > len1;
@@ -1055,8 +1079,17 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs 
         const uint32_t q = 128 * v + 4 * lane;
         float w[4], e[4];
         uint8_t dd[4];
-        loadv<4>(a.w_in, k, n, w);
-        loadv<4>(a.e_in, k, n, e);
+        if ((uint64_t)k + 4 <= n) {
+          const uint4 xw = ld_stream_v4(a.w_in + k, pol_first);
+          const uint4 xe = ld_stream_v4(a.e_in + k, pol_first);
+          w[0] = __uint_as_float(xw.x); w[1] = __uint_as_float(xw.y);
+          w[2] = __uint_as_float(xw.z); w[3] = __uint_as_float(xw.w);
+          e[0] = __uint_as_float(xe.x); e[1] = __uint_as_float(xe.y);
+          e[2] = __uint_as_float(xe.z); e[3] = __uint_as_float(xe.w);
+        } else {
+          loadv<4>(a.w_in, k, n, w);
+          loadv<4>(a.e_in, k, n, e);
+        }
         if constexpr (DEAD) loadv_u8<4>(a.dead, k, n, dd);
         const float4 av = *reinterpret_cast<const float4*>(sa + q);
         const float4 ps = *reinterpret_cast<const float4*>(sp + q);
@@ -1075,8 +1108,13 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32) k_sweep_wtile(SweepArgs 
             w[c] = __fadd_rn(w[c], __fmul_rn(a.rate, ne));
           }
         }
-        storev<4>(a.w_out, k, m, w);
-        storev<4>(a.e_out, k, m, e);
+        if (m == 0xFu) {
+          st_stream_v4(a.w_out + k, make_float4(w[0], w[1], w[2], w[3]), pol_first);
+          st_stream_v4(a.e_out + k, make_float4(e[0], e[1], e[2], e[3]), pol_first);
+        } else {
+          storev<4>(a.w_out, k, m, w);
+          storev<4>(a.e_out, k, m, e);
+        }
       }
     }
     __syncwarp();  // the next tile overwrites the staged values
@@ -1146,6 +1184,10 @@ int launch_warp(plx_ctx* ctx, const SweepArgs& args, uint32_t max_row) {
     case 2: return launch_wtile<WTileCfg<4, 8, 8>, APPLY, UPD, DEAD>(ctx, args);
     case 3: return launch_wtile<WTileCfg<4, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
     case 4: return launch_wtile<WTileCfg<8, 4, 8>, APPLY, UPD, DEAD>(ctx, args);
+    case 5: return launch_wtile<WTileCfg<2, 4, 8, 3>, APPLY, UPD, DEAD>(ctx, args);
+    case 6: return launch_wtile<WTileCfg<2, 3, 8, 3>, APPLY, UPD, DEAD>(ctx, args);
+    case 7: return launch_wtile<WTileCfg<1, 4, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
+    case 8: return launch_wtile<WTileCfg<1, 2, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
     default: return launch_wtile<WTileCfg<4, 4, 8>, APPLY, UPD, DEAD>(ctx, args);
   }
 }

@@ -15,7 +15,7 @@ from typing import Optional
 import torch
 
 from . import _abi
-from ._abi import Csr, Field, call
+from ._abi import Chunked, Csr, Field, call
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -517,6 +517,59 @@ class MlpTopoNet:
                          kind=_abi.UPDATE_GRADIENT, rate=self.lr)
 
 
+class ChunkedRows:
+    """Connections of a row set in the chunked-source layout (see
+    plx_chunked_build): rows are units [row_base, row_base + n_rows), the
+    gathered side units [src_base, src_base + n_src). ``weight`` is the
+    layout-order weight copy (padding 0); ``perm`` maps layout slots to the
+    original connection index (-1 for padding)."""
+
+    def __init__(self, ctx: Context, gather_id: torch.Tensor, row_id: torch.Tensor,
+                 weight: torch.Tensor, src_base: int, n_src: int, row_base: int, n_rows: int):
+        lib = _abi.lib()
+        n = int(gather_id.numel())
+        dev = ctx.device
+        self.ctx = ctx
+        self.n_pad_max = int(lib.plx_chunked_max_padded(n, n_rows, n_src))
+        n_chunks = (n_src + _abi.CHUNK_SOURCES - 1) // _abi.CHUNK_SOURCES
+        self.seg_ptr = torch.empty(n_chunks * n_rows + 1, dtype=torch.int32, device=dev)
+        self.src = torch.empty(self.n_pad_max, dtype=torch.int16, device=dev)
+        self.perm = torch.empty(self.n_pad_max, dtype=torch.int32, device=dev)
+        scratch = torch.empty(int(lib.plx_chunked_scratch_bytes(n, n_rows, n_src)),
+                              dtype=torch.uint8, device=dev)
+        call("plx_chunked_build", ctx.handle, n, _ptr(gather_id) if n else None, src_base, n_src,
+             _ptr(row_id) if n else None, row_base, n_rows, _ptr(self.seg_ptr), _ptr(self.src),
+             _ptr(self.perm), _ptr(scratch), scratch.numel())
+        del scratch
+        self.weight = torch.zeros(self.n_pad_max, dtype=torch.float32, device=dev)
+        if n:
+            call("plx_chunked_gather", ctx.handle, self.n_pad_max, _ptr(self.perm),
+                 _ptr(weight), _ptr(self.weight))
+        self.partial = torch.empty(max(n_chunks * n_rows, 1), dtype=torch.float32, device=dev)
+        self.struct = Chunked(_ptr(self.seg_ptr), _ptr(self.src), _ptr(self.perm), n_rows, n_src,
+                              n_chunks)
+        self.src_base, self.n_src, self.row_base, self.n_rows = src_base, n_src, row_base, n_rows
+
+    def fold(self, gathered: torch.Tensor, out: torch.Tensor, apply: int,
+             value: Optional[torch.Tensor] = None) -> None:
+        """out[r] = Apply(sum of weight * gathered[src] over row r, value[r]);
+        gathered holds the n_src values of the gathered range."""
+        call("plx_chunked_fold", self.ctx.handle, byref(self.struct), _ptr(self.weight),
+             _ptr(gathered), apply, _ptr(value), _ptr(out), _ptr(self.partial))
+
+    def update(self, gathered: torch.Tensor, row_val: torch.Tensor, kind: int,
+               rate: float) -> None:
+        call("plx_chunked_update", self.ctx.handle, byref(self.struct), _ptr(self.weight),
+             _ptr(gathered), _ptr(row_val), kind, rate)
+
+    def weights_in_original_order(self, n: int) -> torch.Tensor:
+        """The layout's weights scattered back to connection order (tests)."""
+        out = torch.zeros(n, dtype=torch.float32, device=self.weight.device)
+        valid = self.perm >= 0
+        out[self.perm[valid].long()] = self.weight[valid]
+        return out
+
+
 class PredictiveCodingNet:
     """Streaming iPC (examples/ipc-multilayer/ipc_multilayer.cpp) on a stack
     of sparse layers: layer 0 takes the input, the last layer is the output,
@@ -535,10 +588,13 @@ class PredictiveCodingNet:
     value update."""
 
     def __init__(self, ctx: Context, sizes, blocks, *, gamma: float = 0.1,
-                 alpha: float = 0.005):
+                 alpha: float = 0.005, layout: str = "csr"):
         """blocks[l] = (from_id, to_id, weight) device tensors of the
         connections into layer l + 1 (absolute unit ids, destination-major).
-        to_id is only used here to build the index."""
+        layout "csr": destination-major CSR sweeps and source-major copies
+        (exact left folds for rows up to PLX_SEQ_ROW_MAX); layout "chunked":
+        the chunked-source layout for both directions (for long rows such as
+        2,048 fan-in; folds in a fixed chunked order)."""
         self.ctx = ctx
         self.sizes = [int(s) for s in sizes]
         self.begin = [0]
@@ -547,8 +603,17 @@ class PredictiveCodingNet:
         self.n_units = self.begin[-1]
         self.gamma, self.alpha = float(gamma), float(alpha)
         dev = ctx.device
+        self.layout = layout
         self.from_id, self.w, self.csr, self.sm = [], [], [], {}
+        self.fwd, self.bwd = [], {}
         for l, (f, t, w) in enumerate(blocks):
+            if layout == "chunked":
+                self.fwd.append(ChunkedRows(ctx, f, t, w, self.begin[l], self.sizes[l],
+                                            self.begin[l + 1], self.sizes[l + 1]))
+                if l >= 1:
+                    self.bwd[l] = ChunkedRows(ctx, t, f, w, self.begin[l + 1], self.sizes[l + 1],
+                                              self.begin[l], self.sizes[l])
+                continue
             self.from_id.append(f)
             self.w.append(w)
             self.csr.append(DstCsr(ctx, t, self.begin[l + 1], self.sizes[l + 1],
@@ -576,7 +641,15 @@ class PredictiveCodingNet:
         call("plx_ipc_value_update", self.ctx.handle, hi - lo, _ptr(self.x[lo:hi]), None, None,
              0.0, _ptr(self.act[lo:hi]), 0)
 
+    def _layer(self, t: torch.Tensor, l: int) -> torch.Tensor:
+        return t[self.begin[l]:self.begin[l + 1]]
+
     def forward(self) -> None:
+        if self.layout == "chunked":
+            for l, ch in enumerate(self.fwd):
+                ch.fold(self._layer(self.act, l), self._layer(self.err, l + 1),
+                        _abi.APPLY_IPC_ERROR, value=self._layer(self.x, l + 1))
+            return
         for l in range(len(self.csr)):
             b0, b1 = self.begin[l + 1], self.begin[l + 2]
             sweep_forward(self.ctx, self.csr[l], self.from_id[l], self.w[l], self.act,
@@ -584,6 +657,11 @@ class PredictiveCodingNet:
                           err_out=self.err[b0:b1])
 
     def backward(self) -> None:
+        if self.layout == "chunked":
+            for l, ch in self.bwd.items():
+                ch.fold(self._layer(self.err, l + 1), self._layer(self.bu, l),
+                        _abi.APPLY_TANH_GRAD, value=self._layer(self.x, l))
+            return
         for l, sm in self.sm.items():
             b0, b1 = self.begin[l], self.begin[l + 1]
             sm.backward(self.err, self.bu[b0:b1], self.x[b0:b1], _abi.APPLY_TANH_GRAD)
@@ -594,6 +672,14 @@ class PredictiveCodingNet:
              _ptr(self.err[lo:hi]), _ptr(self.bu[lo:hi]), self.gamma, _ptr(self.act[lo:hi]), 1)
 
     def update(self) -> None:
+        if self.layout == "chunked":
+            for l, ch in enumerate(self.fwd):
+                ch.update(self._layer(self.act, l), self._layer(self.err, l + 1),
+                          _abi.UPDATE_HEBBIAN, self.alpha)
+                if l in self.bwd:
+                    self.bwd[l].update(self._layer(self.err, l + 1), self._layer(self.act, l),
+                                       _abi.UPDATE_HEBBIAN_T, self.alpha)
+            return
         for l in range(len(self.csr)):
             b0, b1 = self.begin[l + 1], self.begin[l + 2]
             sweep_update(self.ctx, self.csr[l], self.from_id[l], self.act, self.err[b0:b1],
@@ -604,6 +690,12 @@ class PredictiveCodingNet:
                 sweep_update(self.ctx, sm.csr, sm.to_id, self.err, self.act[s0:s1],
                              sm.weight, sm.weight, kind=_abi.UPDATE_HEBBIAN_T,
                              rate=self.alpha)
+
+    def weights(self, l: int, n: Optional[int] = None) -> torch.Tensor:
+        """Block l's weights in connection order."""
+        if self.layout == "chunked":
+            return self.fwd[l].weights_in_original_order(n)
+        return self.w[l]
 
     def iteration(self) -> None:
         self.forward()
