@@ -166,7 +166,9 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p, uint64_t pol) {
 }
 __device__ __forceinline__ float ld_keep_f32(const float* p, uint64_t pol) {
   float v;
-  asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;"
+      : "=f"(v)
+      : "l"(p), "l"(pol));
   return v;
 }
 __device__ __forceinline__ void st_stream_v4(void* p, float4 v, uint64_t pol) {

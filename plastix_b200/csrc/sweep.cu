@@ -1092,8 +1092,8 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32, C::kMinBlocks)
         }
         if constexpr (DEAD) loadv_u8<4>(a.dead, k, n, dd);
         const float4 av = *reinterpret_cast<const float4*>(sa + q);
-        const float4 ps = *reinterpret_cast<const float4*>(sp + q);
         const float avv[4] = {av.x, av.y, av.z, av.w};
+        const float4 ps = *reinterpret_cast<const float4*>(sp + q);
         const float pst[4] = {ps.x, ps.y, ps.z, ps.w};
         uint32_t m = 0;
 #pragma unroll
