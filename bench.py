@@ -50,6 +50,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ipc-units", type=int, default=1 << 18,
+                   help="units per layer of the ipc workload (2^18 in the configuration)")
+    p.add_argument("--ipc-fan-in", type=int, default=2048)
     p.add_argument("--workload", choices=["sweep", "swifttd", "ipc", "structural"],
                    default="sweep",
                    help="sweep: the single-layer fwd+Hebbian sweep (default, the headline); "
@@ -535,7 +538,7 @@ def bench_ipc(args):
 
     from plastix_b200.runtime import Context, PredictiveCodingNet
 
-    S, F, iters = 1 << 18, 2048, 20
+    S, F, iters = args.ipc_units, args.ipc_fan_in, 20
     torch.cuda.set_device(0)
     ctx = Context(0)
     g = torch.Generator(device="cuda").manual_seed(args.seed)

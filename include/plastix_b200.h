@@ -68,9 +68,10 @@ int plx_ctx_sync(plx_ctx* ctx);
 
 /* ---- CSR view of dst-sorted connections -------------------------------- */
 
-/* row_ptr[r] = first connection whose ToId >= row_base + r, r in [0,n_rows];
- * to_id must be sorted ascending and lie in [row_base, row_base + n_rows).
- * Derived index over the reference's ToId field (conn.hpp:13). */
+/* row_ptr[r] = first connection whose ToId >= row_base + r, r in [0,n_rows]
+ * (row_ptr[n_rows] = n_edges); to_id must be sorted ascending, 16-byte
+ * aligned. One pass over the connections. Derived index over the reference's
+ * ToId field (conn.hpp:13). */
 int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id, uint64_t n_edges,
                     uint32_t row_base, uint32_t n_rows, uint32_t* row_ptr);
 

@@ -101,6 +101,16 @@ __global__ void __launch_bounds__(kCT) k_compact(CompactArgs a) {
   __syncthreads();
   const uint64_t tile = s_tile;
   const uint64_t base = tile * kCTile;
+  // The fields are copied only after the lookback; ask for the tile's ranges
+  // in L2 now so those copies do not wait on DRAM.
+  if (tid < a.n_fields && base < a.n) {
+    const FieldDesc& fd = a.f[tid];
+    const uint64_t cnt = min((uint64_t)kCTile, a.n - base);
+    const uintptr_t p0 = reinterpret_cast<uintptr_t>(fd.src) + base * fd.bytes;
+    const uintptr_t lo = (p0 + 15) & ~uintptr_t(15);              // inside the range
+    const uintptr_t hi = (p0 + cnt * fd.bytes) & ~uintptr_t(15);
+    if (hi > lo) prefetch_l2_bulk(reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo));
+  }
 
   uint32_t masks[kCItems];
 #pragma unroll

@@ -10,9 +10,11 @@
 // (plastix.hpp:553-577, alloc.hpp:145-156). LSD radix sort is stable, so the
 // output equals a stable sort by key: unique, and checked bit for bit.
 //
-// Per pass and tile (256 threads x 16 keys, element order = item-major):
-//   * per 256-key round, warps rank keys by digit with __match_any_sync and
-//     shared per-warp digit counters, keeping the element order (stable);
+// Per pass and tile (256 threads x 16 keys; warp w owns 512 consecutive keys,
+// element order = (warp, item, lane)):
+//   * each warp ranks its keys by digit with __match_any_sync and warp-private
+//     shared digit counters (no block barrier per item), keeping the element
+//     order (stable); per-digit warp bases come from one scan over the warps;
 //   * the tile publishes its 256 digit counts, each thread looks back over
 //     the predecessors of its digit (bounded spin) and publishes the prefix;
 //   * keys are re-ordered by digit in shared memory and written out in
@@ -93,54 +95,66 @@ struct RadixPassArgs {
   uint64_t timeout_ns;
 };
 
-__global__ void __launch_bounds__(kRT) k_radix_pass(RadixPassArgs a) {
+__global__ void __launch_bounds__(kRT, 3) k_radix_pass(RadixPassArgs a) {
   __shared__ uint32_t s_keys[kRTile];
   __shared__ uint32_t s_vals[kRTile];
-  __shared__ uint16_t s_cnt[2][kRWarps][256];
+  __shared__ uint32_t s_wcnt[kRWarps][256];  // per-warp digit counts, then warp bases
   __shared__ uint32_t s_run[256];
   __shared__ uint32_t s_local[256];
   __shared__ uint32_t s_gbase[256];
   __shared__ uint32_t s_tile;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   if (tid == 0) s_tile = atomicAdd(a.ticket, 1u);
-  for (uint32_t w = 0; w < kRWarps; ++w) s_cnt[0][w][tid] = 0;
-  s_run[tid] = 0;
+  for (uint32_t w = 0; w < kRWarps; ++w) s_wcnt[w][tid] = 0;
   __syncthreads();
   const uint64_t tile = s_tile;
   const uint64_t base = tile * kRTile;
   const uint32_t lt = (1u << lane) - 1u;
 
+  // Warp w owns tile elements [w * 512, (w + 1) * 512): item j of lane l is
+  // element w * 512 + j * 32 + l, so element order is (warp, item, lane) and
+  // every load is a coalesced 128-byte row.
+  constexpr uint32_t kWarpSpan = kRItems * 32;
   uint32_t key[kRItems], val[kRItems], rank[kRItems];
 #pragma unroll
   for (int j = 0; j < kRItems; ++j) {
-    const uint64_t e = base + (uint64_t)j * kRT + tid;
+    const uint64_t e = base + (uint64_t)warp * kWarpSpan + (uint64_t)j * 32 + lane;
     const bool ok = e < a.n;
     key[j] = ok ? a.keys_in[e] : 0u;
     val[j] = ok ? (a.vals_in ? a.vals_in[e] : (uint32_t)e) : 0u;
   }
+  // Rank within the warp: lanes with the same digit are matched, counts kept
+  // per warp in shared memory -- no block-wide barrier per item.
+  uint32_t* wc = s_wcnt[warp];
 #pragma unroll
   for (int j = 0; j < kRItems; ++j) {
-    const int b = j & 1;
-    const uint64_t e = base + (uint64_t)j * kRT + tid;
+    const uint64_t e = base + (uint64_t)warp * kWarpSpan + (uint64_t)j * 32 + lane;
     const bool ok = e < a.n;
     const uint32_t d = (key[j] >> a.shift) & a.mask;
     const uint32_t peers = __match_any_sync(0xffffffffu, ok ? d : 0x100u);
     const uint32_t lrank = __popc(peers & lt);
-    if (ok && lrank == 0) s_cnt[b][warp][d] = (uint16_t)__popc(peers);
-    __syncthreads();
-    {  // digit tid: per-warp counts -> exclusive prefixes; clear the other buffer
-      uint32_t run = s_run[tid];
+    const uint32_t before = ok ? wc[d] : 0u;
+    __syncwarp();
+    if (ok && lrank == 0) wc[d] = before + __popc(peers);
+    __syncwarp();
+    rank[j] = before + lrank;
+  }
+  __syncthreads();
+  {  // digit tid: per-warp counts -> exclusive per-warp bases; tile count
+    uint32_t run = 0;
 #pragma unroll
-      for (int w = 0; w < kRWarps; ++w) {
-        const uint32_t c = s_cnt[b][w][tid];
-        s_cnt[b][w][tid] = (uint16_t)run;
-        run += c;
-        s_cnt[b ^ 1][w][tid] = 0;
-      }
-      s_run[tid] = run;
+    for (int w = 0; w < kRWarps; ++w) {
+      const uint32_t c = s_wcnt[w][tid];
+      s_wcnt[w][tid] = run;
+      run += c;
     }
-    __syncthreads();
-    rank[j] = ok ? s_cnt[b][warp][d] + lrank : 0u;
+    s_run[tid] = run;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kRItems; ++j) {
+    const uint32_t d = (key[j] >> a.shift) & a.mask;
+    rank[j] += wc[d];
   }
   // Tile digit counts: s_run. Publish, look back, publish prefix.
   const uint32_t cnt = s_run[tid];
@@ -187,7 +201,7 @@ __global__ void __launch_bounds__(kRT) k_radix_pass(RadixPassArgs a) {
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < kRItems; ++j) {
-    const uint64_t e = base + (uint64_t)j * kRT + tid;
+    const uint64_t e = base + (uint64_t)warp * kWarpSpan + (uint64_t)j * 32 + lane;
     if (e < a.n) {
       const uint32_t d = (key[j] >> a.shift) & a.mask;
       const uint32_t pos = s_local[d] + rank[j];

@@ -99,23 +99,43 @@ enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3
 // ---------------------------------------------------------------------------
 // Plan construction
 // ---------------------------------------------------------------------------
+// row_ptr[r] = first index whose ToId is >= row_base + r (ToId sorted),
+// row_ptr[n_rows] = n_edges. One pass over the connections: index i owns the
+// rows r with key(i-1) < r <= key(i), keys clamped to [-1, n_rows] (index
+// n_edges acts as key n_rows). Each thread takes four consecutive indices
+// with one 16-byte load (to_id is 16-byte aligned) plus the key before them.
+__device__ __forceinline__ int64_t row_key(uint32_t to, uint32_t row_base, uint32_t n_rows) {
+  const int64_t k = (int64_t)to - (int64_t)row_base;
+  return k < -1 ? -1 : (k > (int64_t)n_rows ? (int64_t)n_rows : k);
+}
+
 __global__ void k_row_ptr(const uint32_t* __restrict__ to_id, uint64_t n_edges,
                           uint32_t row_base, uint32_t n_rows,
                           uint32_t* __restrict__ row_ptr) {
-  uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (r > n_rows) return;
-  if (r == n_rows) {
-    row_ptr[r] = (uint32_t)n_edges;
-    return;
+  const uint64_t i0 = 4 * (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x);
+  if (i0 > n_edges) return;
+  int64_t k[5];  // keys of i0 - 1 .. i0 + 3
+  k[0] = i0 ? row_key(__ldg(to_id + i0 - 1), row_base, n_rows) : -1;
+  if (i0 + 4 <= n_edges) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(to_id + i0));
+    k[1] = row_key(v.x, row_base, n_rows);
+    k[2] = row_key(v.y, row_base, n_rows);
+    k[3] = row_key(v.z, row_base, n_rows);
+    k[4] = row_key(v.w, row_base, n_rows);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      k[j + 1] = i0 + j < n_edges ? row_key(__ldg(to_id + i0 + j), row_base, n_rows)
+                                  : (int64_t)n_rows;
   }
-  const uint64_t key = (uint64_t)row_base + r;
-  uint64_t lo = 0, hi = n_edges;  // first index with to_id >= key
-  while (lo < hi) {
-    uint64_t mid = (lo + hi) >> 1;
-    if ((uint64_t)__ldg(to_id + mid) < key) lo = mid + 1;
-    else hi = mid;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint64_t i = i0 + j;
+    if (i > n_edges) break;
+    const int64_t hi = min(k[j + 1], (int64_t)n_rows - 1);
+    for (int64_t r = k[j] + 1; r <= hi; ++r) row_ptr[r] = (uint32_t)i;
+    if (i == n_edges) row_ptr[n_rows] = (uint32_t)n_edges;
   }
-  row_ptr[r] = (uint32_t)lo;
 }
 
 __global__ void k_plan_blocks(const uint32_t* __restrict__ row_ptr,
@@ -145,43 +165,58 @@ __global__ void k_plan_blocks(const uint32_t* __restrict__ row_ptr,
 // counts short rows and lists wide and long rows (list order is irrelevant:
 // each row is reduced independently). Any violation clears the magic word so
 // every sweep using this plan stops and reports a bad-plan status.
-__global__ void k_plan_rows(const uint32_t* __restrict__ row_ptr,
-                            uint32_t n_rows, uint64_t n_edges,
-                            uint32_t* __restrict__ plan) {
+__global__ void __launch_bounds__(256) k_plan_rows(const uint32_t* __restrict__ row_ptr,
+                                                   uint32_t n_rows, uint64_t n_edges,
+                                                   uint32_t* __restrict__ plan) {
+  __shared__ uint32_t s_short[8], s_max[8];
   const uint64_t nb = plan_blocks(n_edges);
   const uint64_t max_wide = plan_max_wide(n_edges);
   const uint64_t max_long = plan_max_long(n_edges);
   uint32_t* wide = plan + plan_wide_off(nb);
   uint32_t* lng = wide + max_wide;
-  uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (r == 0) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
     if (row_ptr[0] != 0 || row_ptr[n_rows] != (uint32_t)n_edges) plan[0] = 0;
   }
-  bool is_short = false;
-  if (r < n_rows) {
+  uint32_t n_short = 0, longest = 0;
+  for (uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; r < n_rows;
+       r += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t a = row_ptr[r], b = row_ptr[r + 1];
     if (b < a || b > n_edges) {
       plan[0] = 0;
+      continue;
+    }
+    const uint32_t len = b - a;
+    longest = max(longest, len);
+    if (len <= kSeqMax) {
+      ++n_short;
+    } else if (len <= kLongRow) {
+      const uint32_t slot = atomicAdd(&plan[2], 1u);
+      if (slot < max_wide) wide[slot] = (uint32_t)r;
+      else plan[0] = 0;
     } else {
-      const uint32_t len = b - a;
-      if (len <= kSeqMax) {
-        is_short = true;
-      } else if (len <= kLongRow) {
-        uint32_t slot = atomicAdd(&plan[2], 1u);
-        if (slot < max_wide) wide[slot] = (uint32_t)r;
-        else plan[0] = 0;
-      } else {
-        uint32_t slot = atomicAdd(&plan[3], 1u);
-        if (slot < max_long) lng[slot] = (uint32_t)r;
-        else plan[0] = 0;
-      }
+      const uint32_t slot = atomicAdd(&plan[3], 1u);
+      if (slot < max_long) lng[slot] = (uint32_t)r;
+      else plan[0] = 0;
     }
   }
-  const uint32_t m = __ballot_sync(0xffffffffu, is_short);
-  if ((threadIdx.x & 31) == 0 && m) atomicAdd(&plan[4], (uint32_t)__popc(m));
-  uint32_t len = r < n_rows ? row_ptr[r + 1] - row_ptr[r] : 0u;
-  len = __reduce_max_sync(0xffffffffu, len);
-  if ((threadIdx.x & 31) == 0 && len) atomicMax(&plan[7], len);
+  // One atomic per block for the short-row count and the longest row.
+  n_short = __reduce_add_sync(0xffffffffu, n_short);
+  longest = __reduce_max_sync(0xffffffffu, longest);
+  const uint32_t lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    s_short[w] = n_short;
+    s_max[w] = longest;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t ts = 0, tm = 0;
+    for (uint32_t i = 0; i < blockDim.x / 32; ++i) {
+      ts += s_short[i];
+      tm = max(tm, s_max[i]);
+    }
+    if (ts) atomicAdd(&plan[4], ts);
+    if (tm) atomicMax(&plan[7], tm);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1272,8 +1307,12 @@ extern "C" int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id,
   PLX_CHECK_ARG(n_edges < 0xFFFF0000ull, "n_edges must be < 2^32 - 2^16");
   PLX_TRY_CUDA(cudaSetDevice(ctx->device));
   const uint64_t n = (uint64_t)n_rows + 1;
-  k_row_ptr<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
-      to_id, n_edges, row_base, n_rows, row_ptr);
+  (void)n;
+  PLX_CHECK_ARG(aligned16(to_id), "to_id must be 16-byte aligned");
+  const uint64_t threads = n_edges / 4 + 1;  // indices 0 .. n_edges, four per thread
+  k_row_ptr<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(to_id, n_edges,
+                                                                        row_base, n_rows,
+                                                                        row_ptr);
   PLX_LAUNCH_CHECK("k_row_ptr");
   return PLX_OK;
 }
@@ -1333,7 +1372,9 @@ static int csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
   k_plan_blocks<<<(unsigned)((nb + 1 + 255) / 256), 256, 0, ctx->stream>>>(
       row_ptr, n_rows, n_edges, plan);
   PLX_LAUNCH_CHECK("k_plan_blocks");
-  k_plan_rows<<<(unsigned)(((uint64_t)n_rows + 256) / 256), 256, 0, ctx->stream>>>(
+  k_plan_rows<<<(unsigned)std::max<uint64_t>(1, std::min<uint64_t>(((uint64_t)n_rows + 255) / 256,
+                                                                     4ull * ctx->num_sms)),
+                256, 0, ctx->stream>>>(
       row_ptr, n_rows, n_edges, plan);
   PLX_LAUNCH_CHECK("k_plan_rows");
   if (!sync) {
