@@ -531,30 +531,34 @@ def bench_ipc(args):
     """C5: 5 layers of 262,144 units, 2,048 random sources per destination
     (2^31 connections), weights N(0, 1/2048), inputs U(0,1); a sample = 20
     inference iterations (forward, Pipeline backward, value update) + one
-    weight update. One timed step = one sample."""
-    import math
-
+    weight update. One timed step = one sample. With --gpus N the same
+    network is sharded by unit range over N GPUs (strong scaling; all-gathers
+    of f(x) and eps per iteration)."""
     import torch
+    import torch.distributed as dist
 
-    from plastix_b200.runtime import Context, PredictiveCodingNet
+    from plastix_b200.runtime import Context
+    from plastix_b200.sharding import ShardedPCNet
 
-    S, F, iters = args.ipc_units, args.ipc_fan_in, 20
-    torch.cuda.set_device(0)
-    ctx = Context(0)
-    g = torch.Generator(device="cuda").manual_seed(args.seed)
-    begin = [i * S for i in range(6)]
-    blocks = []
-    for l in range(4):
-        f = torch.randint(begin[l], begin[l] + S, (S * F,), generator=g, device="cuda",
-                          dtype=torch.int32)
-        t = (torch.arange(S, device="cuda", dtype=torch.int32) + begin[l + 1]).repeat_interleave(F)
-        w = torch.randn(S * F, generator=g, device="cuda") * (1.0 / math.sqrt(F))
-        blocks.append((f, t, w))
-    net = PredictiveCodingNet(ctx, [S] * 5, blocks, gamma=0.1, alpha=0.005, layout="chunked")
-    blocks = None
-    inputs = torch.rand(S, generator=g, device="cuda")
-    targets = torch.rand(S, generator=g, device="cuda") * 2 - 1
-    E, Eb = 4 * S * F, 3 * S * F
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    S, F, iters, L = args.ipc_units, args.ipc_fan_in, 20, 5
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    else:  # a one-rank group keeps the all-gathers on the same code path
+        dist.init_process_group("nccl", init_method=f"file://{tempfile.mktemp(prefix='plx_pg_')}",
+                                rank=0, world_size=1, device_id=dev)
+    ctx = Context(local)
+    net = ShardedPCNet(ctx, S, F, L, rank, world, args.seed, gamma=0.1, alpha=0.005)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    inputs = torch.rand(S, generator=g, device=dev)
+    targets = torch.rand(S, generator=g, device=dev) * 2 - 1
+    E, Eb = (L - 1) * S * F, (L - 2) * S * F
 
     def sample(i):
         net.clamp(inputs, targets)
@@ -562,29 +566,61 @@ def bench_ipc(args):
             net.iteration()
         net.update()
     steps = max(1, min(args.steps, 5))
-    ms, clocks = _timed_loop(ctx.stream, sample, steps, min(args.warmup, 3))
-    # per-launch view of the dominant sweep (forward, all four blocks)
+    for _ in range(min(args.warmup, 3)):
+        sample(0)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    t0, t1 = _events(2)
+    t0.record(ctx.stream)
+    for i in range(steps):
+        sample(i)
+    t1.record(ctx.stream)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = t0.elapsed_time(t1)
+    # the dominant sweep alone: the forward folds of this rank's rows
     e = _events(2)
-    e[0].record()
+    e[0].record(ctx.stream)
     for _ in range(5):
-        net.forward()
-    e[1].record()
+        for l, ch in enumerate(net.fwd):
+            ch.fold(net.layer(net.act, l), net.own(net.err, l + 1), 3,
+                    value=net.own(net.x, l + 1))
+    e[1].record(ctx.stream)
     torch.cuda.synchronize()
     fwd_ms = e[0].elapsed_time(e[1]) / 5
+    t = torch.tensor([ms, fwd_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, fwd_ms = float(t[0]), float(t[1])
     ctx.sync()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return 0
     visits = iters * (E + Eb) + (E + Eb)
     per_sample = ms / steps
-    _line(args, "ipc", visits / (per_sample / 1e3), "connection-visits/s", per_sample,
-          {"workload": "multilayer sparse predictive coding (iPC)", "layers": 5,
-           "units_per_layer": S, "fan_in": F, "connections": E, "iterations_per_sample": iters,
-           "counting": "per sample: 20 x (forward over all connections + backward over the "
-                       "hidden-source ones) + one update of both copies",
-           "layout": "chunked-source (16-bit source offsets, 16384-source chunks in shared "
-                     "memory)",
-           "roofline_bytes": "forward: 6 B per connection (16-bit offset + weight)",
-           "l2": "inputs larger than L2: 12 GiB of destination-major connections"},
-          _roof(6 * E, fwd_ms, "ipc_forward_2G"), None,
-          None, clocks, None, extra={"forward_ms": fwd_ms, "samples": steps})
+    line = {"metric": "connection-visits/s (ipc)", "value": visits / (per_sample / 1e3),
+            "unit": "connection-visits/s", "n_gpus": world, "steps": steps,
+            "warmup": min(args.warmup, 3), "ms_per_step": per_sample, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (counter-based hash generator)",
+            "config": {"workload": "multilayer sparse predictive coding (iPC)", "layers": L,
+                       "units_per_layer": S, "fan_in": F, "connections": E,
+                       "iterations_per_sample": iters,
+                       "parallelism": f"unit-range shards x{world}, NCCL all-gather of f(x) "
+                                      "and eps per iteration",
+                       "counting": "per sample: 20 x (forward over all connections + backward "
+                                   "over the hidden-source ones) + one update of both copies",
+                       "layout": "chunked-source (16-bit source offsets, 16384-source chunks "
+                                 "in shared memory)",
+                       "roofline_bytes": "forward: 6 B per connection (16-bit offset + weight)",
+                       "l2": "inputs larger than L2"},
+            "roofline": _roof(6 * E / world, fwd_ms, "ipc_forward_2G"),
+            "cpu_baseline": None, "e2e": None, "clocks": clocks, "gpu_launches": None,
+            "forward_ms": fwd_ms}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def bench_structural(args):
@@ -620,7 +656,7 @@ def bench_structural(args):
 
 
 def run_other(args):
-    if args.gpus != 1:
+    if args.gpus != 1 and args.workload != "ipc":
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
     return {"swifttd": bench_swifttd, "ipc": bench_ipc,
             "structural": bench_structural}[args.workload](args) or 0

@@ -94,3 +94,176 @@ def allgather_rows(local, shards: Sequence[Shard], group=None):
         dist.all_gather(got, buf, group=group)
         parts = [got[r][:shards[r].n_rows] for r in range(world)]
     return torch.cat(parts)
+
+
+# ---------------------------------------------------------------------------
+# Sharded multilayer predictive-coding network (the 2^31-connection iPC
+# configuration across GPUs).
+# ---------------------------------------------------------------------------
+_M1 = 0xBF58476D1CE4E5B9 - (1 << 64)
+_M2 = 0x94D049BB133111EB - (1 << 64)
+_GOLD = 0x9E3779B97F4A7C15 - (1 << 64)
+
+
+def _srl(x, k):
+    """Logical right shift of int64 tensors holding uint64 bit patterns."""
+    return (x >> k) & ((1 << (64 - k)) - 1)
+
+
+def mix64(x):
+    """SplitMix64 finaliser on int64 tensors (uint64 bit patterns; products
+    wrap modulo 2^64)."""
+    x = x + _GOLD
+    x = (x ^ _srl(x, 30)) * _M1
+    x = (x ^ _srl(x, 27)) * _M2
+    return x ^ _srl(x, 31)
+
+
+def ipc_block_edges(l: int, size: int, fan_in: int, seed: int, device, row_lo: int = 0,
+                    row_hi=None):
+    """Connections of block l (into layer l + 1) of the multilayer network,
+    destination rows [row_lo, row_hi) of that layer, destination-major: row d
+    has fan_in sources in layer l chosen by a counter-based hash of (seed, l,
+    d, j), weights N(0, 1/fan_in) by Box-Muller on two more hash words. Every
+    rank can regenerate any part of the network without communication.
+    Returns (from_id, to_id, weight) with absolute unit ids (layer l starts
+    at l * size)."""
+    import math
+
+    import torch
+
+    row_hi = size if row_hi is None else row_hi
+    e = torch.arange(row_lo * fan_in, row_hi * fan_in, dtype=torch.int64, device=device)
+    key = mix64(torch.full((1,), seed * 1000003 + l, dtype=torch.int64, device=device))
+    h = mix64(e + key)
+    src = (((h & 0xFFFFFFFF) * size) >> 32) + l * size
+    u1 = (_srl(h, 32).to(torch.float64) + 0.5) * (1.0 / 4294967296.0)
+    h2 = mix64(h)
+    u2 = ((h2 & 0xFFFFFFFF).to(torch.float64) + 0.5) * (1.0 / 4294967296.0)
+    w = (torch.sqrt(-2.0 * torch.log(u1)) * torch.cos(2.0 * math.pi * u2)
+         * (1.0 / math.sqrt(fan_in))).to(torch.float32)
+    to = torch.div(e, fan_in, rounding_mode="floor") + (l + 1) * size
+    return src.to(torch.int32), to.to(torch.int32), w
+
+
+def allgather_owned(t, n_layers: int, size: int, rank: int, world: int, send, recv,
+                    group=None) -> None:
+    """t holds n_layers layers of `size` units; rank q owns units
+    [q*m, (q+1)*m) of each layer (m = size / world). Gathers every rank's
+    owned slices into t (one collective: a fixed-size all-gather of the
+    n_layers * m owned values, then one reordering copy)."""
+    import torch
+    import torch.distributed as dist
+
+    m = size // world
+    lo = rank * m
+    send.view(n_layers, m).copy_(t.view(n_layers, size)[:, lo:lo + m])
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(recv, send, group=group)
+    else:
+        parts = list(recv.view(world, n_layers * m).unbind(0))  # views of recv
+        dist.all_gather(parts, send, group=group)
+    t.view(n_layers, size).copy_(recv.view(world, n_layers, m).permute(1, 0, 2)
+                                 .reshape(n_layers, size))
+
+
+class ShardedPCNet:
+    """The multilayer iPC network (layers of `size` units, `fan_in` random
+    sources per destination) sharded by unit range: rank r owns units
+    [r*m, (r+1)*m) of every layer, m = size / world -- the destination rows of
+    every block in destination-major chunked layout, and the source rows of
+    every hidden layer in source-major chunked layout (built from the whole
+    block, keeping the connections whose source is owned). Per inference
+    iteration two all-gathers cross GPUs: f(x) of every layer before the
+    forward sweep and eps before the backward sweep (5 layers x size floats
+    each); the weight update all-gathers f(x) once more. Each copy of a
+    weight is updated by its owner with the same rule and inputs, so the
+    copies stay bit-identical, and every row is folded over the same segments
+    as on one GPU: results equal the single-GPU network's bit for bit."""
+
+    def __init__(self, ctx, size: int, fan_in: int, n_layers: int, rank: int, world: int,
+                 seed: int, *, gamma: float = 0.1, alpha: float = 0.005, group=None):
+        import torch
+
+        from . import _abi
+        from .runtime import ChunkedRows
+
+        if size % world:
+            raise ValueError("size must be divisible by the number of ranks")
+        self.ctx, self.size, self.L = ctx, size, n_layers
+        self.rank, self.world, self.group = rank, world, group
+        self.m = size // world
+        self.lo = rank * self.m
+        self.gamma, self.alpha = float(gamma), float(alpha)
+        dev = ctx.device
+        self.begin = [l * size for l in range(n_layers + 1)]
+        self.fwd, self.bwd = [], {}
+        for l in range(n_layers - 1):
+            f, t, w = ipc_block_edges(l, size, fan_in, seed, dev)
+            a, b = self.lo * fan_in, (self.lo + self.m) * fan_in
+            self.fwd.append(ChunkedRows(ctx, f[a:b], t[a:b], w[a:b], self.begin[l], size,
+                                        self.begin[l + 1] + self.lo, self.m))
+            if l >= 1:
+                self.bwd[l] = ChunkedRows(ctx, t, f, w, self.begin[l + 1], size,
+                                          self.begin[l] + self.lo, self.m)
+            del f, t, w
+        n_units = self.begin[-1]
+        self.x = torch.zeros(n_units, dtype=torch.float32, device=dev)
+        self.act = torch.zeros_like(self.x)
+        self.err = torch.zeros_like(self.x)
+        self.bu = torch.zeros_like(self.x)
+        self._send = torch.empty(n_layers * self.m, dtype=torch.float32, device=dev)
+        self._recv = torch.empty(world * n_layers * self.m, dtype=torch.float32, device=dev)
+        self._abi = _abi
+
+    def own(self, t, l):
+        """This rank's slice of layer l of a unit-sized tensor."""
+        s = self.begin[l] + self.lo
+        return t[s:s + self.m]
+
+    def layer(self, t, l):
+        return t[self.begin[l]:self.begin[l + 1]]
+
+    def allgather_layers(self, t) -> None:
+        """Every rank's owned slices of every layer -> the full vector."""
+        allgather_owned(t, self.L, self.size, self.rank, self.world, self._send, self._recv,
+                        self.group)
+
+    def clamp(self, inputs, targets) -> None:
+        """Clamps inputs and output targets (full vectors on every rank) and
+        runs the pre-step for the owned hidden units."""
+        from .runtime import _ptr, call
+
+        self.layer(self.x, 0).copy_(inputs)
+        self.layer(self.act, 0).copy_(inputs)
+        self.layer(self.x, self.L - 1).copy_(targets)
+        for l in range(1, self.L - 1):
+            call("plx_ipc_value_update", self.ctx.handle, self.m, _ptr(self.own(self.x, l)),
+                 None, None, 0.0, _ptr(self.own(self.act, l)), 0)
+
+    def iteration(self) -> None:
+        from .runtime import _ptr, call
+
+        A = self._abi
+        self.allgather_layers(self.act)
+        for l, ch in enumerate(self.fwd):
+            ch.fold(self.layer(self.act, l), self.own(self.err, l + 1), A.APPLY_IPC_ERROR,
+                    value=self.own(self.x, l + 1))
+        self.allgather_layers(self.err)
+        for l, ch in self.bwd.items():
+            ch.fold(self.layer(self.err, l + 1), self.own(self.bu, l), A.APPLY_TANH_GRAD,
+                    value=self.own(self.x, l))
+        for l in range(1, self.L - 1):
+            call("plx_ipc_value_update", self.ctx.handle, self.m, _ptr(self.own(self.x, l)),
+                 _ptr(self.own(self.err, l)), _ptr(self.own(self.bu, l)), self.gamma,
+                 _ptr(self.own(self.act, l)), 1)
+
+    def update(self) -> None:
+        A = self._abi
+        self.allgather_layers(self.act)
+        for l, ch in enumerate(self.fwd):
+            ch.update(self.layer(self.act, l), self.own(self.err, l + 1), A.UPDATE_HEBBIAN,
+                      self.alpha)
+        for l, ch in self.bwd.items():
+            ch.update(self.layer(self.err, l + 1), self.own(self.act, l), A.UPDATE_HEBBIAN_T,
+                      self.alpha)

@@ -1,0 +1,73 @@
+"""Worker for tests/test_multigpu.py (one process per GPU, launched with
+torch.distributed.run): the sharded multilayer iPC network against the same
+network on one GPU, bit for bit. Not collected by pytest."""
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+from plastix_b200.runtime import Context, PredictiveCodingNet  # noqa: E402
+from plastix_b200.sharding import ShardedPCNet, ipc_block_edges  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    S, F, L, seed, iters = 8192, 256, 5, 21, 3
+    ctx = Context(local)
+    net = ShardedPCNet(ctx, S, F, L, rank, world, seed)
+    g = torch.Generator(device=dev).manual_seed(5)
+    x0 = torch.rand(L * S, generator=g, device=dev) * 2 - 1
+    inp = torch.rand(S, generator=g, device=dev)
+    tgt = torch.rand(S, generator=g, device=dev) * 2 - 1
+    net.x.copy_(x0)
+    net.clamp(inp, tgt)
+    for _ in range(iters):
+        net.iteration()
+    net.update()
+    ref = PredictiveCodingNet(ctx, [S] * L,
+                              [ipc_block_edges(l, S, F, seed, dev) for l in range(L - 1)],
+                              layout="chunked")
+    ref.x.copy_(x0)
+    ref.clamp(inp, tgt)
+    for _ in range(iters):
+        ref.iteration()
+    ref.update()
+    ctx.sync()
+    bad = []
+    for l in range(1, L):
+        if not torch.equal(net.own(net.err, l), net.own(ref.err, l)):
+            bad.append(f"err layer {l}")
+    for l in range(1, L - 1):
+        if not torch.equal(net.own(net.x, l), net.own(ref.x, l)):
+            bad.append(f"x layer {l}")
+    for l in range(L - 1):
+        a, b = net.lo * F, (net.lo + net.m) * F
+        mine = net.fwd[l].weights_in_original_order(net.m * F)
+        if not torch.equal(mine, ref.weights(l, S * F)[a:b]):
+            bad.append(f"weights block {l}")
+        if l in net.bwd:
+            ch = net.bwd[l]
+            valid = ch.perm >= 0
+            full = ref.weights(l, S * F)
+            if not torch.equal(ch.weight[valid], full[ch.perm[valid].long()]):
+                bad.append(f"source-major weights block {l}")
+    flag = torch.tensor([len(bad)], device=dev)
+    dist.all_reduce(flag)
+    if bad:
+        print(f"rank {rank}: mismatch in {bad}", flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(1 if int(flag.item()) else 0)
+
+
+if __name__ == "__main__":
+    main()

@@ -92,3 +92,39 @@ def test_two_gloo_ranks_match_one_process():
                                sweeps=2)
     np.testing.assert_array_equal(got_act.view(np.uint32), a[n_src:].view(np.uint32))
     np.testing.assert_array_equal(got_w.view(np.uint32), w.view(np.uint32))
+
+
+def _owned_main(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        L, size = 5, 12
+        m = size // world
+        t = torch.full((L * size,), -1.0)
+        for l in range(L):  # each rank knows only its own units
+            for u in range(rank * m, (rank + 1) * m):
+                t[l * size + u] = 100 * l + u
+        send = torch.empty(L * m)
+        recv = torch.empty(world * L * m)
+        sharding.allgather_owned(t, L, size, rank, world, send, recv)
+        q.put((rank, t.numpy().copy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allgather_owned_slices_two_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_owned_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = np.array([100 * l + u for l in range(5) for u in range(12)], np.float32)
+    for r in range(world):
+        np.testing.assert_array_equal(got[r], want)
