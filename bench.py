@@ -50,6 +50,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--handoff", choices=["p2p", "nccl"], default="p2p",
+                   help="N > 1: hand the destination slices to every GPU with the sweep's "
+                        "own stores over NVLink (p2p) or with an NCCL all-gather after it")
     p.add_argument("--ipc-units", type=int, default=1 << 18,
                    help="units per layer of the ipc workload (2^18 in the configuration)")
     p.add_argument("--ipc-fan-in", type=int, default=2048)
@@ -246,12 +249,25 @@ def run_ours(args):
     layer = HebbianSweepLayer(ctx, n_src_total, n_dst, from_id, to_id, w)
     del from_id, to_id, w
     gathered = torch.empty(n_dst * world, device=device) if world > 1 else None
+    p2p = world > 1 and args.handoff == "p2p"
+    peer = None
+    if p2p:
+        from plastix_b200.sharding import PeerGather
+        peer = PeerGather(ctx, n_dst * world, rank, world)
+
+    def sweep(x):
+        """One sweep plus the hand-off of its destination slice to every GPU."""
+        if p2p:
+            out = layer.step_gather(x, peer, rank * n_dst)
+            peer.barrier()
+        else:
+            out = layer.step(x)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out)
+        return out
 
     def step():
-        out = layer.step(act_src)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-        return out
+        return sweep(act_src)
 
     def barrier_sync():
         if world > 1:
@@ -270,9 +286,14 @@ def run_ours(args):
     t0.record(stream)
     for i in range(args.steps):
         k0[i].record(stream)
-        layer.step(act_src)
+        if p2p:
+            layer.step_gather(act_src, peer, rank * n_dst)
+        else:
+            layer.step(act_src)
         k1[i].record(stream)
-        if world > 1:
+        if p2p:
+            peer.barrier()
+        elif world > 1:
             dist.all_gather_into_tensor(gathered, layer.act_dst)
     t1.record(stream)
     barrier_sync()
@@ -294,9 +315,7 @@ def run_ours(args):
 
     def e2e_step():
         dev_in.copy_(h_in, non_blocking=True)
-        out = layer.step(dev_in)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+        out = sweep(dev_in)
         h_out.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -324,6 +343,10 @@ def run_ours(args):
 
     if world > 1:
         dist.barrier()
+        if peer is not None:
+            torch.cuda.synchronize()
+            peer.close()
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
@@ -343,8 +366,10 @@ def run_ours(args):
                    "n_edges_per_gpu": n_edges, "parallelism": f"dst-range shards x{world}",
                    "l2": "inputs larger than L2: 1.36 GB of connection state streamed "
                          "per sweep vs 126 MB L2",
-                   "handoff": "NCCL all-gather of destination activations per sweep"
-                              if world > 1 else "none"},
+                   "handoff": ("destination slices stored by the sweep kernel into every "
+                               "GPU's buffer over NVLink (peer memory), bounded barrier"
+                               if p2p else "NCCL all-gather of destination activations per "
+                               "sweep") if world > 1 else "none"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS hbm_gbs)",
                      "traffic": traffic_per_launch("sweep_hebbian_64M"),
@@ -354,7 +379,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": 4 * n_src_total * world,
                 "d2h_bytes_per_step": 4 * n_dst * world},
         "clocks": clocks,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if p2p else 1),
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -162,6 +162,43 @@ int plx_sweep_forward_hebbian(plx_ctx* ctx, const plx_csr* csr,
                               float* trace_out, float decay, float rate,
                               float* act_dst);
 
+/* ---- hand-off over peer memory (one process per GPU, NVLink) ------------ */
+
+#define PLX_MAX_PEERS 8
+#define PLX_IPC_HANDLE_BYTES 64
+
+/* The fused sweep of plx_sweep_forward_hebbian that also hands the layer's
+ * output to the other GPUs: every destination value is stored, besides
+ * act_dst, to peer_out[p][peer_offset + r] for each of the n_peers buffers
+ * (the all-gather buffers of every GPU, this one's included, mapped with
+ * plx_peer_open), so the all-gather of destination slices after a sweep
+ * (the multi-GPU hand-off between layers) rides on the sweep's own stores
+ * over NVLink. Follow it with plx_peer_barrier before reading the buffer. */
+int plx_sweep_forward_hebbian_gather(
+    plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id, const uint8_t* dead,
+    const float* act_src, uint32_t act_src_len, const float* w_in, float* w_out,
+    const float* trace_in, float* trace_out, float decay, float rate, float* act_dst,
+    float* const* peer_out, uint32_t n_peers, uint32_t peer_offset);
+
+/* Device memory another process can map: cudaMalloc'd and zeroed, its IPC
+ * handle (PLX_IPC_HANDLE_BYTES bytes) written to ipc_handle. */
+int plx_peer_alloc(plx_ctx* ctx, size_t bytes, void** ptr, void* ipc_handle);
+int plx_peer_free(plx_ctx* ctx, void* ptr);
+/* Maps a peer's allocation into this process (peer access enabled). */
+int plx_peer_open(plx_ctx* ctx, const void* ipc_handle, void** ptr);
+int plx_peer_close(plx_ctx* ctx, void* ptr);
+
+/* Barrier over n GPUs: flags[p] is rank p's array of n uint64 counters
+ * (peer memory). Publishes epoch (increasing per call) to every rank after a
+ * system-scope fence over this GPU's earlier stores, then waits until every
+ * rank published it. A wait beyond the context's timeout records
+ * PLX_ERR_TIMEOUT (plx_ctx_sync) and returns; nothing blocks forever. */
+int plx_peer_barrier(plx_ctx* ctx, uint64_t* const* flags, uint32_t n, uint32_t rank,
+                     uint64_t epoch);
+
+/* Device-to-device copy on the context's stream (e.g. out of a peer buffer). */
+int plx_copy_device(plx_ctx* ctx, void* dst, const void* src, size_t bytes);
+
 /* Update kinds for plx_sweep_update (per-connection, reads a per-row value). */
 #define PLX_UPDATE_GRADIENT 1 /* w -= rate * post[dst] * act[src]
                                  (mlp_xor.cpp:51-56, linear_regression.cpp:31-36) */

@@ -31,6 +31,8 @@ UPDATE_HEBBIAN_T = 3
 
 SEQ_ROW_MAX = 256
 CHUNK_SOURCES = 16384
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
 
 
 class PlxError(RuntimeError):
@@ -104,6 +106,16 @@ _SIGNATURES = {
                                  c_void_p, c_void_p, c_void_p]),
     "plx_chunked_update": (c_int, [c_void_p, POINTER(Chunked), c_void_p, c_void_p, c_void_p,
                                    c_int, c_float]),
+    "plx_sweep_forward_hebbian_gather": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p,
+                                                 c_void_p, c_uint32, c_void_p, c_void_p,
+                                                 c_void_p, c_void_p, c_float, c_float,
+                                                 c_void_p, c_void_p, c_uint32, c_uint32]),
+    "plx_peer_alloc": (c_int, [c_void_p, ctypes.c_size_t, POINTER(c_void_p), c_void_p]),
+    "plx_peer_free": (c_int, [c_void_p, c_void_p]),
+    "plx_peer_open": (c_int, [c_void_p, c_void_p, POINTER(c_void_p)]),
+    "plx_peer_close": (c_int, [c_void_p, c_void_p]),
+    "plx_peer_barrier": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint64]),
+    "plx_copy_device": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
     "plx_swifttd_scratch_bytes": (c_uint64, [c_uint64, c_uint32]),
     "plx_swifttd_step": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),

@@ -92,6 +92,12 @@ struct SweepArgs {
   uint32_t row_base;      // unit id of row 0
   uint32_t* queue;        // stripe work counter (warp fast path), zeroed
   uint32_t only_long;     // warp fast path: run only if the longest row > 128
+  // Hand-off over peer memory: every row value is also stored to
+  // peer_out[p][peer_offset + r] for each of the n_peers destination buffers
+  // (this GPU's and the other GPUs' all-gather buffers, NVLink-mapped).
+  uint32_t n_peers;
+  uint32_t peer_offset;
+  float* peer_out[PLX_MAX_PEERS];
 };
 
 enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3, kUpdHebbT = 4 };
@@ -231,6 +237,7 @@ __device__ __forceinline__ float apply_row(float acc, uint32_t r,
   if (owned) {
     if constexpr (APPLY == PLX_APPLY_IPC_ERROR) a.err_out[r] = post;
     else a.act_dst[r] = post;
+    for (uint32_t p = 0; p < a.n_peers; ++p) a.peer_out[p][a.peer_offset + r] = post;
   }
   return post;
 }
@@ -1490,6 +1497,45 @@ extern "C" int plx_sweep_forward_hebbian(
   a.decay = decay;
   a.rate = rate;
   a.act_dst = act_dst;
+  return dead ? launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, true>(ctx, a, csr)
+              : launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, false>(ctx, a, csr);
+}
+
+extern "C" int plx_sweep_forward_hebbian_gather(
+    plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id, const uint8_t* dead,
+    const float* act_src, uint32_t act_src_len, const float* w_in, float* w_out,
+    const float* trace_in, float* trace_out, float decay, float rate, float* act_dst,
+    float* const* peer_out, uint32_t n_peers, uint32_t peer_offset) {
+  PLX_CHECK_ARG(n_peers <= PLX_MAX_PEERS, "at most %d peers", PLX_MAX_PEERS);
+  PLX_CHECK_ARG(n_peers == 0 || peer_out, "peer_out is required");
+  for (uint32_t p = 0; p < n_peers; ++p) PLX_CHECK_ARG(peer_out[p], "peer_out[%u] is NULL", p);
+  PLX_CHECK_ARG(ctx, "ctx is required");
+  if (int rc = validate_csr(csr)) return rc;
+  PLX_CHECK_ARG(act_dst, "act_dst is required");
+  PLX_CHECK_ARG(csr->n_edges == 0 ||
+                    (from_id && act_src && w_in && w_out && trace_in && trace_out),
+                "connection arrays and act_src are required");
+  PLX_CHECK_ARG(csr->n_edges == 0 || (w_in != w_out && trace_in != trace_out),
+                "the fused sweep needs distinct input and output weight/trace buffers");
+  PLX_CHECK_ARG(aligned16(from_id) && aligned16(dead) && aligned16(w_in) &&
+                    aligned16(w_out) && aligned16(trace_in) && aligned16(trace_out),
+                "connection arrays must be 16-byte aligned");
+  PLX_TRY_CUDA(cudaSetDevice(ctx->device));
+  SweepArgs a = base_args(ctx, csr);
+  a.src = from_id;
+  a.dead = dead;
+  a.act_src = act_src;
+  a.act_src_len = act_src_len;
+  a.w_in = w_in;
+  a.w_out = w_out;
+  a.e_in = trace_in;
+  a.e_out = trace_out;
+  a.decay = decay;
+  a.rate = rate;
+  a.act_dst = act_dst;
+  a.n_peers = n_peers;
+  a.peer_offset = peer_offset;
+  for (uint32_t p = 0; p < n_peers; ++p) a.peer_out[p] = peer_out[p];
   return dead ? launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, true>(ctx, a, csr)
               : launch_sweep<true, PLX_APPLY_IDENTITY, kUpdHebbTrace, true, false>(ctx, a, csr);
 }

@@ -207,6 +207,18 @@ class HebbianSweepLayer:
         self._cur = o
         return self.act_dst
 
+    def step_gather(self, act_src: torch.Tensor, peer, offset: int) -> torch.Tensor:
+        """``step`` whose destination values also land in every rank's
+        all-gather buffer (``peer``: sharding.PeerGather) at ``offset``, as
+        stores of the sweep itself; call ``peer.barrier()`` before reading."""
+        c, o = self._cur, 1 - self._cur
+        call("plx_sweep_forward_hebbian_gather", self.ctx.handle, byref(self.csr.struct),
+             _ptr(self.from_id), _ptr(self.dead), _ptr(act_src), int(act_src.numel()),
+             _ptr(self._w[c]), _ptr(self._w[o]), _ptr(self._e[c]), _ptr(self._e[o]),
+             self.decay, self.rate, _ptr(self.act_dst), peer.peer_out, peer.world, offset)
+        self._cur = o
+        return self.act_dst
+
 
 # ---------------------------------------------------------------------------
 # Structural change: compaction, gather, radix sort, regrowth

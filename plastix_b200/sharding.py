@@ -267,3 +267,80 @@ class ShardedPCNet:
         for l, ch in self.bwd.items():
             ch.update(self.layer(self.err, l + 1), self.own(self.act, l), A.UPDATE_HEBBIAN_T,
                       self.alpha)
+
+
+# ---------------------------------------------------------------------------
+# Hand-off over peer memory (one process per GPU): an all-gather buffer that
+# every rank's sweep writes into directly over NVLink.
+# ---------------------------------------------------------------------------
+class PeerGather:
+    """A buffer of n_total floats on every rank, mapped into every other rank
+    through CUDA IPC, plus a flag array per rank for plx_peer_barrier. A
+    producer passes ``peer_out`` (all ranks' buffers) to
+    plx_sweep_forward_hebbian_gather with its slice offset; ``barrier()``
+    then guarantees every rank's slice has landed in every buffer."""
+
+    def __init__(self, ctx, n_total: int, rank: int, world: int, group=None):
+        import ctypes
+        from ctypes import c_void_p
+
+        import torch.distributed as dist
+
+        from . import _abi
+        from .runtime import call
+
+        if world > _abi.MAX_PEERS:
+            raise ValueError(f"at most {_abi.MAX_PEERS} ranks")
+        self.ctx, self.rank, self.world, self.n_total = ctx, rank, world, n_total
+        self._own = []
+        handles = []
+        for nbytes in (4 * n_total, 8 * world):
+            ptr = c_void_p()
+            h = ctypes.create_string_buffer(_abi.IPC_HANDLE_BYTES)
+            call("plx_peer_alloc", ctx.handle, nbytes, ctypes.byref(ptr), h)
+            self._own.append(ptr.value)
+            handles.append(h.raw)
+        everyone = [None] * world
+        dist.all_gather_object(everyone, handles, group=group)
+        self._opened = []
+        bufs, flags = [], []
+        for q in range(world):
+            if q == rank:
+                bufs.append(self._own[0])
+                flags.append(self._own[1])
+                continue
+            got = []
+            for h in everyone[q]:
+                ptr = c_void_p()
+                call("plx_peer_open", ctx.handle, ctypes.create_string_buffer(h, len(h)),
+                     ctypes.byref(ptr))
+                self._opened.append(ptr.value)
+                got.append(ptr.value)
+            bufs.append(got[0])
+            flags.append(got[1])
+        self.peer_out = (c_void_p * world)(*bufs)
+        self.flags = (c_void_p * world)(*flags)
+        self.local = self._own[0]
+        self.epoch = 0
+
+    def barrier(self) -> None:
+        from .runtime import call
+
+        self.epoch += 1
+        call("plx_peer_barrier", self.ctx.handle, self.flags, self.world, self.rank,
+             self.epoch)
+
+    def copy_to(self, out) -> None:
+        """Copies this rank's gathered buffer into a float32 CUDA tensor."""
+        from .runtime import _ptr, call
+
+        call("plx_copy_device", self.ctx.handle, _ptr(out), self.local, 4 * self.n_total)
+
+    def close(self) -> None:
+        from .runtime import call
+
+        for p in self._opened:
+            call("plx_peer_close", self.ctx.handle, p)
+        for p in self._own:
+            call("plx_peer_free", self.ctx.handle, p)
+        self._opened, self._own = [], []

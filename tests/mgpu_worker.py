@@ -11,8 +11,36 @@ import torch.distributed as dist
 
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 
-from plastix_b200.runtime import Context, PredictiveCodingNet  # noqa: E402
-from plastix_b200.sharding import ShardedPCNet, ipc_block_edges  # noqa: E402
+from plastix_b200 import workloads  # noqa: E402
+from plastix_b200.runtime import Context, HebbianSweepLayer, PredictiveCodingNet  # noqa: E402
+from plastix_b200.sharding import PeerGather, ShardedPCNet, ipc_block_edges  # noqa: E402
+
+
+def check_peer_handoff(ctx, rank, world, dev):
+    """The fused sweep + peer-memory hand-off against the plain sweep and an
+    NCCL all-gather, over several steps (epochs)."""
+    n_src, n_dst, n = 50_000, 40_000, 2_000_000
+    f, t, w, _ = workloads.sparse_layer_device(n_src, n_dst, n, 100 + rank, dev)
+    act = torch.rand(n_src, generator=torch.Generator(device=dev).manual_seed(9), device=dev)
+    a = HebbianSweepLayer(ctx, n_src, n_dst, f, t, w.clone())
+    b = HebbianSweepLayer(ctx, n_src, n_dst, f, t, w.clone())
+    peer = PeerGather(ctx, n_dst * world, rank, world)
+    want = torch.empty(n_dst * world, device=dev)
+    got = torch.empty(n_dst * world, device=dev)
+    bad = []
+    for step in range(4):
+        a.step_gather(act, peer, rank * n_dst)
+        peer.barrier()
+        dist.all_gather_into_tensor(want, b.step(act))
+        peer.copy_to(got)
+        ctx.sync()
+        if not torch.equal(got, want):
+            bad.append(f"peer hand-off step {step}")
+    torch.cuda.synchronize()
+    dist.barrier()
+    peer.close()
+    dist.barrier()
+    return bad
 
 
 def main():
@@ -60,6 +88,7 @@ def main():
             full = ref.weights(l, S * F)
             if not torch.equal(ch.weight[valid], full[ch.perm[valid].long()]):
                 bad.append(f"source-major weights block {l}")
+    bad += check_peer_handoff(ctx, rank, world, dev)
     flag = torch.tensor([len(bad)], device=dev)
     dist.all_reduce(flag)
     if bad:

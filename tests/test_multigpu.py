@@ -1,6 +1,8 @@
 """Several GPUs (runs when the machine has at least two): the sharded
 multilayer iPC network (unit-range shards, NCCL all-gathers of f(x) and eps)
-equals the same network on one GPU bit for bit, on every rank."""
+equals the same network on one GPU bit for bit, on every rank; and the fused
+sweep + peer-memory hand-off (stores over NVLink, bounded barrier) equals the
+plain sweep + NCCL all-gather bit for bit."""
 import socket
 import subprocess
 import sys
@@ -21,7 +23,7 @@ def _port():
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_sharded_ipc_equals_single_gpu():
+def test_sharded_ipc_and_peer_handoff_on_two_gpus():
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
            str(_port()), str(WORKER)]
