@@ -77,7 +77,8 @@ def traffic_per_launch(workload_key: str):
     if f.exists():
         d = json.loads(f.read_text())
         if workload_key in d:
-            return d[workload_key]
+            v = d[workload_key]
+            return v["bytes_per_launch"] if isinstance(v, dict) else v
     return None
 
 
