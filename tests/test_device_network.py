@@ -1,0 +1,69 @@
+"""The device Network<Traits> (include/plastix/plastix.hpp): C++ programs
+whose policies carry PLASTIX_HD and run on the GPU through the same API as
+the reference header library, against the reference-made fixtures:
+
+* network_xor.cu -- the XOR MLP (Topological, sigmoid, MSE, backward,
+  gradient descent): initial weights bit for bit (same host generator as the
+  reference's RandomUniformWeight), weights and predictions after 200 epochs
+  at 1e-5 relative (device expf against the host's).
+* network_ipc.cu -- 30 streaming-iPC steps (Pipeline, tanh): weights, value
+  nodes and errors at 1e-5 relative.
+
+On the CPU the programs are compiled (nvcc cross-compiles for sm_100a)."""
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+GOLDEN = ROOT / "tests" / "golden"
+NVCC = "/usr/local/cuda/bin/nvcc"
+
+
+def compile_prog(name: str, out: Path) -> Path:
+    exe = out / name
+    cmd = [NVCC, "-std=c++20", "--expt-relaxed-constexpr", "-gencode",
+           "arch=compute_100a,code=sm_100a", "-O2", f"-I{ROOT / 'include'}",
+           str(ROOT / "tests" / "cpp" / f"{name}.cu"), "-o", str(exe)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    return exe
+
+
+def parse(out: str):
+    vals = {}
+    for line in out.splitlines():
+        k, v = line.split()
+        vals.setdefault(k, []).append(float.fromhex(v))
+    return {k: np.array(v, np.float32) for k, v in vals.items()}
+
+
+@pytest.mark.parametrize("name", ["network_xor", "network_ipc"])
+def test_device_network_programs_compile(tmp_path, name):
+    assert compile_prog(name, tmp_path).exists()
+
+
+@pytest.mark.gpu
+def test_device_network_xor_matches_reference(tmp_path):
+    z = np.load(GOLDEN / "mlp_xor_small.npz")
+    exe = compile_prog("network_xor", tmp_path)
+    r = subprocess.run([str(exe), "200"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    v = parse(r.stdout)
+    np.testing.assert_array_equal(v["w0"].view(np.uint32), z["w_init"].view(np.uint32))
+    np.testing.assert_allclose(v["w"], z["w_200"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(v["p"], z["preds_200"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_device_network_ipc_matches_reference(tmp_path):
+    z = np.load(GOLDEN / "ipc_small.npz")
+    for k in ("w0", "x0", "inputs", "targets"):
+        np.ascontiguousarray(z[k], np.float32).tofile(tmp_path / f"{k}.bin")
+    exe = compile_prog("network_ipc", tmp_path)
+    r = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    v = parse(r.stdout)
+    np.testing.assert_allclose(v["w"], z["w"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(v["x"], z["x"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(v["e"], z["err"], rtol=1e-5, atol=1e-6)
