@@ -8,6 +8,9 @@ the reference header library, against the reference-made fixtures:
   at 1e-5 relative (device expf against the host's).
 * network_ipc.cu -- 30 streaming-iPC steps (Pipeline, tanh): weights, value
   nodes and errors at 1e-5 relative.
+* network_swifttd.cu -- 200 SwiftTD steps (per-connection hooks that add
+  into the globals, run with the sequential connection update): V per step,
+  weights and log step sizes at 1e-5 relative.
 
 On the CPU the programs are compiled (nvcc cross-compiles for sm_100a)."""
 import subprocess
@@ -38,7 +41,7 @@ def parse(out: str):
     return {k: np.array(v, np.float32) for k, v in vals.items()}
 
 
-@pytest.mark.parametrize("name", ["network_xor", "network_ipc"])
+@pytest.mark.parametrize("name", ["network_xor", "network_ipc", "network_swifttd"])
 def test_device_network_programs_compile(tmp_path, name):
     assert compile_prog(name, tmp_path).exists()
 
@@ -67,3 +70,18 @@ def test_device_network_ipc_matches_reference(tmp_path):
     np.testing.assert_allclose(v["w"], z["w"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(v["x"], z["x"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(v["e"], z["err"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_device_network_swifttd_matches_reference(tmp_path):
+    z = np.load(GOLDEN / "swifttd_small.npz")
+    np.ascontiguousarray(z["features"], np.float32).tofile(tmp_path / "features.bin")
+    np.ascontiguousarray(z["rewards"], np.float32).tofile(tmp_path / "rewards.bin")
+    exe = compile_prog("network_swifttd", tmp_path)
+    r = subprocess.run([str(exe), str(tmp_path), str(int(z["n"]))], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    v = parse(r.stdout)
+    np.testing.assert_allclose(v["v"], z["v"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(v["w"], z["fields"][0], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(v["b"], z["fields"][9], rtol=1e-5, atol=1e-6)
