@@ -291,6 +291,15 @@ int plx_radix_sort_u32(plx_ctx* ctx, uint64_t n, const uint32_t* keys_in,
                        uint32_t begin_bit, uint32_t end_bit, void* scratch,
                        size_t scratch_bytes);
 
+size_t plx_sort_unique_u64_scratch_bytes(uint64_t n);
+
+/* Proposal commit of DoAddConnections (plastix.hpp:411-433): sorts n 64-bit
+ * keys ((To << 32) | From, CompactEdge::Bits) ascending and writes each
+ * distinct key once to out (the reference's std::sort + skip of repeats);
+ * *count_out (DEVICE memory) receives the number written. n < 2^30. */
+int plx_sort_unique_u64(plx_ctx* ctx, uint64_t n, const uint64_t* keys, uint64_t* out,
+                        uint64_t* count_out, void* scratch, size_t scratch_bytes);
+
 /* Regrowth after compaction: connections [*count, n) (count in DEVICE
  * memory) get FromId/ToId from a seeded counter-based generator, Weight 0
  * and age 0 (weight/age may be NULL). For the i-th regrown connection:

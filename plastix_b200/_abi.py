@@ -116,6 +116,9 @@ _SIGNATURES = {
     "plx_peer_close": (c_int, [c_void_p, c_void_p]),
     "plx_peer_barrier": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint64]),
     "plx_copy_device": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_sort_unique_u64_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
+    "plx_sort_unique_u64": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    ctypes.c_size_t]),
     "plx_swifttd_scratch_bytes": (c_uint64, [c_uint64, c_uint32]),
     "plx_swifttd_step": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_uint64]),

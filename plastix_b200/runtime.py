@@ -272,6 +272,18 @@ def radix_sort_u32(ctx: Context, keys: torch.Tensor, keys_out: torch.Tensor,
          begin_bit, end_bit, _ptr(s), s.numel())
 
 
+def sort_unique_u64(ctx: Context, keys: torch.Tensor, out: torch.Tensor,
+                    count_out: torch.Tensor, *, scratch: Optional[Scratch] = None) -> None:
+    """Proposal commit: distinct keys of ``keys`` (int64 tensor holding the
+    uint64 (To << 32 | From) bits) in ascending unsigned order into ``out``;
+    their number into ``count_out`` (1-element int64 device tensor)."""
+    n = int(keys.numel())
+    nbytes = _abi.lib().plx_sort_unique_u64_scratch_bytes(n)
+    s = (scratch or Scratch(ctx.device)).get(nbytes)
+    call("plx_sort_unique_u64", ctx.handle, n, _ptr(keys) if n else None,
+         _ptr(out) if n else None, _ptr(count_out), _ptr(s), s.numel())
+
+
 def regrow(ctx: Context, count: torch.Tensor, from_id: torch.Tensor, to_id: torch.Tensor,
            weight: Optional[torch.Tensor], age: Optional[torch.Tensor], *, src_base: int,
            n_src: int, dst_base: int, n_dst: int, seed: int, step_base: int):

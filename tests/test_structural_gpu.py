@@ -188,3 +188,49 @@ def test_full_size_structural_step(ctx, orc):
     a_full = np.concatenate([hact, np.zeros(n_dst, np.float32)])
     want, _ = orc.forward_pipeline(of, ot, ow, a_full, n_src)
     np.testing.assert_array_equal(host(out), want[n_src:])
+
+
+@pytest.mark.parametrize("n,dups", [(0, 0), (1, 0), (1000, 900), (500_003, 100_000),
+                                    (1 << 20, 0)])
+def test_proposal_sort_unique_matches_oracle(ctx, orc, n, dups):
+    """DoAddConnections phases 2-3: sort CompactEdge bits, commit each once."""
+    from plastix_b200.runtime import sort_unique_u64
+    rng = np.random.default_rng(n + dups)
+    frm = rng.integers(0, 2**32, n, dtype=np.uint64)
+    to = rng.integers(0, 2**32, n, dtype=np.uint64)
+    bits = (to << np.uint64(32)) | frm
+    if dups and n:
+        bits[rng.choice(n, dups)] = bits[rng.choice(n, dups)]
+    if n >= 1000:  # the all-ones key: the reference's "previous" sentinel skips it
+        bits[:3] = np.uint64(2**64 - 1)
+    keys = torch.from_numpy(bits.view(np.int64)).cuda() if n else \
+        torch.zeros(1, dtype=torch.int64, device="cuda")[:0]
+    out = torch.zeros(max(n, 1), dtype=torch.int64, device="cuda")
+    count = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+    sort_unique_u64(ctx, keys, out, count)
+    ctx.sync()
+    want = orc.sort_unique_u64(bits)
+    m = int(count.item())
+    assert m == want.size
+    np.testing.assert_array_equal(host(out)[:m].view(np.uint64), want)
+
+
+def test_level_sort_is_stable_counting_sort(ctx, orc):
+    """SortConnectionsByLevel (plastix.hpp:539-579): a stable sort of the
+    connections by SrcLevel and a Gather of every field -- the radix sort on
+    the 16-bit level key and plx_gather, against the oracle's stable sort."""
+    rng = np.random.default_rng(12)
+    n = 300_001
+    level = rng.integers(0, 1024, n).astype(np.uint32)
+    frm = rng.integers(0, 2**32, n, dtype=np.uint64).astype(np.uint32)
+    w = rng.normal(size=n).astype(np.float32)
+    keys_out = torch.zeros(n, dtype=torch.int32, device="cuda")
+    perm = torch.zeros(n, dtype=torch.int32, device="cuda")
+    radix_sort_u32(ctx, dev(level), keys_out, perm, 0, 16)
+    f2, w2 = torch.empty(n, dtype=torch.int32, device="cuda"), torch.empty(n, device="cuda")
+    gather(ctx, perm, [(dev(frm), f2), (dev(w), w2)])
+    ctx.sync()
+    want = orc.stable_sort_perm_u32(level)
+    np.testing.assert_array_equal(host(perm).view(np.uint32), want.astype(np.uint32))
+    np.testing.assert_array_equal(host(f2, np.uint32), orc.gather(want, frm))
+    np.testing.assert_array_equal(host(w2).view(np.uint32), orc.gather(want, w).view(np.uint32))
