@@ -183,6 +183,12 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
                : "memory");
 }
+// The same with an L2 cache policy for the prefetched lines.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p),
+               "r"(bytes), "l"(pol)
+               : "memory");
+}
 
 // Orders this thread's generic-proxy shared-memory writes before subsequent
 // async-proxy (bulk store) reads of the same shared memory.

@@ -1018,9 +1018,9 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32, C::kMinBlocks)
     const uint64_t end = min_u64((uint64_t)phi + 3, n) & ~3ull;  // whole 16 B, inside
     if (end > plo) {
       const uint32_t bytes = (uint32_t)(end - plo) * 4u;
-      prefetch_l2_bulk(a.src + plo, bytes);
-      prefetch_l2_bulk(a.w_in + plo, bytes);
-      if constexpr (UPD) prefetch_l2_bulk(a.e_in + plo, bytes);
+      prefetch_l2_bulk(a.src + plo, bytes, pol_first);
+      prefetch_l2_bulk(a.w_in + plo, bytes, pol_first);
+      if constexpr (UPD) prefetch_l2_bulk(a.e_in + plo, bytes, pol_first);
     }
     const uint32_t r0 = Q0[0] & ~3u;
     const uint32_t r1 = min(Q1[0] + 4u, a.n_rows) & ~3u;  // row_ptr has n_rows + 1 entries
