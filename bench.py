@@ -515,19 +515,55 @@ def bench_swifttd(args):
         e[2 * i + 1].record()
     torch.cuda.synchronize()
     dense_ms = statistics.mean(e[2 * i].elapsed_time(e[2 * i + 1]) for i in range(20))
-    # end to end: the active list and reward from pinned host memory, V back
+    # end to end: each step's active list and reward from pinned host memory,
+    # V back; uploads and read-backs on their own streams, double-buffered.
     h_sets = [s.cpu().pin_memory() for s in sets[:8]]
-    h_rw = rewards[:8].cpu().pin_memory()
-    d_idx = torch.empty(k, dtype=torch.int32, device="cuda")
-    d_rw = torch.empty(1, device="cuda")
-    h_v = torch.empty(1, pin_memory=True)
+    h_rw = [rewards[i:i + 1].cpu().pin_memory() for i in range(8)]
+    d_idx = [torch.empty(k, dtype=torch.int32, device="cuda") for _ in range(2)]
+    d_rw = [torch.empty(1, device="cuda") for _ in range(2)]
+    h_v = [torch.empty(1, pin_memory=True) for _ in range(2)]
+    d_v = [torch.empty(1, device="cuda") for _ in range(2)]
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_free = [torch.cuda.Event() for _ in range(2)]
+    for b in range(2):
+        in_free[b].record(ctx.stream)
+        out_free[b].record(ctx.stream)
 
     def e2e(i):
-        d_idx.copy_(h_sets[i % 8], non_blocking=True)
-        d_rw.copy_(h_rw[i % 8:i % 8 + 1], non_blocking=True)
-        v = td.step(d_idx, d_rw)
-        h_v.copy_(v, non_blocking=True)
-    ems, _ = _timed_loop(ctx.stream, e2e, args.steps, args.warmup)
+        b = i & 1
+        up.wait_event(in_free[b])
+        with torch.cuda.stream(up):
+            d_idx[b].copy_(h_sets[i % 8], non_blocking=True)
+            d_rw[b].copy_(h_rw[i % 8], non_blocking=True)
+        in_ready[b].record(up)
+        ctx.stream.wait_event(in_ready[b])
+        v = td.step(d_idx[b], d_rw[b])
+        in_free[b].record(ctx.stream)
+        ctx.stream.wait_event(out_free[b])
+        d_v[b].copy_(v, non_blocking=True)
+        out_ready[b].record(ctx.stream)
+        down.wait_event(out_ready[b])
+        with torch.cuda.stream(down):
+            h_v[b].copy_(d_v[b], non_blocking=True)
+        out_free[b].record(down)
+
+    def e2e_timed():
+        for i in range(args.warmup):
+            e2e(i)
+        torch.cuda.synchronize()
+        t0, t1 = _events(2)
+        t0.record(ctx.stream)
+        up.wait_event(t0)
+        for i in range(args.steps):
+            e2e(i)
+        ctx.stream.wait_event(out_free[(args.steps - 1) & 1])
+        t1.record(ctx.stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1)
+    ems = e2e_timed()
     ctx.sync()
     value = n * args.steps / (ms / 1e3)
     algo = 72 * n  # dense pass: 8 fields read, 10 written, 4 B each
