@@ -18,6 +18,7 @@ compiled from source, oracle/_ref) on the host cores instead.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -56,11 +57,12 @@ def parse_args():
     p.add_argument("--ipc-units", type=int, default=1 << 18,
                    help="units per layer of the ipc workload (2^18 in the configuration)")
     p.add_argument("--ipc-fan-in", type=int, default=2048)
-    p.add_argument("--workload", choices=["sweep", "swifttd", "ipc", "structural"],
+    p.add_argument("--workload", choices=["sweep", "swifttd", "ipc", "structural", "ceiling"],
                    default="sweep",
                    help="sweep: the single-layer fwd+Hebbian sweep (default, the headline); "
                         "swifttd: 4M-feature SwiftTD learner; ipc: 5-layer predictive-coding "
-                        "net; structural: prune/regrow/re-sort/forward step")
+                        "net; structural: prune/regrow/re-sort/forward step; ceiling: the sweep "
+                        "beside the same traffic without row folds and random gathers alone")
     return p.parse_args()
 
 
@@ -744,11 +746,57 @@ def bench_structural(args):
           None, None, None, clocks, None)
 
 
+def bench_ceiling(args):
+    """The sweep against the two pieces of its traffic no fold order removes:
+    the same connections swept without the row folds (FromId/Weight/Trace
+    loads, act[FromId] gathers, Weight/Trace stores) and as many random
+    gathers alone. Prints per-launch times (CUDA events, inputs > L2)."""
+    import torch
+
+    from plastix_b200 import _abi, workloads
+    from plastix_b200.runtime import Context, HebbianSweepLayer
+
+    ctx = Context(0)
+    device = ctx.device
+    n_src, n_dst, n = args.n_src, args.n_dst, args.n_edges
+    from_id, to_id, w, act = workloads.sparse_layer_device(n_src, n_dst, n, args.seed, device)
+    layer = HebbianSweepLayer(ctx, n_src, n_dst, from_id, to_id, w.clone())
+    e = torch.zeros(n, device=device)
+    w2, e2 = torch.empty_like(w), torch.empty_like(e)
+    sink = torch.zeros(1, device=device)
+    done = ctypes.c_uint64(0)
+
+    def nofold(i):
+        _abi.call("plx_probe_sweep_nofold", ctx.handle, n, from_id.data_ptr(), act.data_ptr(),
+                  n_src, w.data_ptr(), e.data_ptr(), 0.9, 1e-3, w2.data_ptr(), e2.data_ptr())
+
+    def gather(i):
+        _abi.call("plx_probe_gather", ctx.handle, act.data_ptr(), n_src, n, sink.data_ptr(),
+                  ctypes.byref(done))
+
+    out = {}
+    for name, fn in (("sweep", lambda i: layer.step(act)), ("nofold", nofold), ("gather", gather)):
+        ms, clocks = _timed_loop(ctx.stream, fn, args.steps, args.warmup)
+        out[name] = ms / args.steps
+    ctx.sync()
+    gathers = int(done.value)
+    line = {"metric": "ms per launch (sweep memory ceiling probes)", "unit": "ms",
+            "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "f32", "data": "synthetic (seeded generators)",
+            "config": {"workload": "sweep ceiling probes", "n_src": n_src, "n_dst": n_dst,
+                       "connections": n, "l2": "inputs larger than L2"},
+            "sweep_ms": out["sweep"], "nofold_ms": out["nofold"], "gather_ms": out["gather"],
+            "gathers": gathers, "gathers_per_s": gathers / (out["gather"] / 1e3),
+            "sweep_over_nofold": out["sweep"] / out["nofold"], "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def run_other(args):
     if args.gpus != 1 and args.workload != "ipc":
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
-    return {"swifttd": bench_swifttd, "ipc": bench_ipc,
-            "structural": bench_structural}[args.workload](args) or 0
+    return {"swifttd": bench_swifttd, "ipc": bench_ipc, "structural": bench_structural,
+            "ceiling": bench_ceiling}[args.workload](args) or 0
 
 
 def main():

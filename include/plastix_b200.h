@@ -199,6 +199,20 @@ int plx_peer_barrier(plx_ctx* ctx, uint64_t* const* flags, uint32_t n, uint32_t 
 /* Device-to-device copy on the context's stream (e.g. out of a peer buffer). */
 int plx_copy_device(plx_ctx* ctx, void* dst, const void* src, size_t bytes);
 
+/* Measurement kernels for the connection sweep's memory ceiling (no
+ * reference counterpart; used by the benchmark only).
+ * plx_probe_gather: about n_gathers random 4-byte loads from x (n_x a power
+ * of two) with the sweep's L2 policy; the exact count is written to *done and
+ * the loaded values are summed into *sink (device).
+ * plx_probe_sweep_nofold: the sweep's per-connection traffic without the row
+ * folds -- FromId, Weight, Trace loads, act[FromId] gathers, Weight and Trace
+ * stores (n a multiple of 4, arrays 16-byte aligned). */
+int plx_probe_gather(plx_ctx* ctx, const float* x, uint32_t n_x, uint64_t n_gathers,
+                     float* sink, uint64_t* done);
+int plx_probe_sweep_nofold(plx_ctx* ctx, uint64_t n, const uint32_t* from_id, const float* act,
+                           uint32_t n_act, const float* w_in, const float* e_in, float decay,
+                           float rate, float* w_out, float* e_out);
+
 /* Update kinds for plx_sweep_update (per-connection, reads a per-row value). */
 #define PLX_UPDATE_GRADIENT 1 /* w -= rate * post[dst] * act[src]
                                  (mlp_xor.cpp:51-56, linear_regression.cpp:31-36) */
