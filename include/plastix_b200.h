@@ -199,6 +199,31 @@ int plx_peer_barrier(plx_ctx* ctx, uint64_t* const* flags, uint32_t n, uint32_t 
 /* Device-to-device copy on the context's stream (e.g. out of a peer buffer). */
 int plx_copy_device(plx_ctx* ctx, void* dst, const void* src, size_t bytes);
 
+/* Unit levels: RecomputeLevels (include/plastix/plastix.hpp:466-537), the
+ * level-parallel Kahn pass over live connections. Resets level[i] = 0 for
+ * non-input units i in [n_input, n_units); then, from the input units as round
+ * 0's frontier, each round decrements the in-degree of every live outgoing
+ * target of the frontier, and a target whose in-degree reaches 0 in round L
+ * gets level L+1 (uint16) and joins the next frontier. Bit-identical levels
+ * to the reference (they do not depend on the order within a round).
+ * *rounds_out (device, optional) receives the number of non-empty frontiers.
+ * dead may be NULL (all live). Connections naming a unit >= n_units are
+ * skipped and recorded as PLX_ERR_ARG at plx_ctx_sync. Runs one cooperative
+ * kernel for all rounds; a grid barrier that waits past the context's
+ * timeout records PLX_ERR_TIMEOUT. */
+size_t plx_recompute_levels_scratch_bytes(uint64_t n_units, uint64_t n_conns);
+int plx_recompute_levels(plx_ctx* ctx, uint32_t n_units, uint32_t n_input, uint64_t n_conns,
+                         const uint32_t* from_id, const uint32_t* to_id, const uint8_t* dead,
+                         uint16_t* level, uint32_t* rounds_out, void* scratch,
+                         size_t scratch_bytes);
+
+/* src_level[c] = level[from_id[c]]: the SrcLevel refresh of
+ * SortConnectionsByLevel (plastix.hpp:546-549). Followed by
+ * plx_radix_sort_u32 on the 16-bit key and plx_gather, it is the whole
+ * re-sort (:551-577). */
+int plx_src_levels(plx_ctx* ctx, uint64_t n_conns, const uint32_t* from_id,
+                   const uint16_t* level, uint32_t n_units, uint16_t* src_level);
+
 /* Measurement kernels for the connection sweep's memory ceiling (no
  * reference counterpart; used by the benchmark only).
  * plx_probe_gather: about n_gathers random 4-byte loads from x (n_x a power

@@ -68,6 +68,9 @@ def orc() -> ctypes.CDLL:
         L.oracle_swifttd_step.argtypes = [c_uint64, c_void_p, c_void_p, c_float, c_void_p,
                                           c_int]
         L.oracle_swifttd_step.restype = c_float
+        L.oracle_recompute_levels.argtypes = [c_uint32, c_uint32, c_uint64, c_void_p, c_void_p,
+                                              c_void_p, c_void_p]
+        L.oracle_recompute_levels.restype = ctypes.c_int64
         _orc = L
     return _orc
 
@@ -94,6 +97,9 @@ def ref() -> Optional[ctypes.CDLL]:
         L.ref_ipc_run.restype = ctypes.c_int64
         L.ref_swifttd_example_run.argtypes = [c_uint64, c_void_p, c_void_p, c_int, c_float,
                                               c_void_p, c_void_p]
+        if hasattr(L, "ref_levels_run"):
+            L.ref_levels_run.argtypes = [c_uint64, c_uint64, c_uint64] + [c_void_p] * 8
+            L.ref_levels_run.restype = c_int
         _ref = L
     return _ref
 
@@ -448,3 +454,54 @@ def ref_ipc_run(inputs, targets, w, x):
     if m != w.size:
         raise RuntimeError("ref_ipc_run failed")
     return w, x, err
+
+
+# ---------------------------------------------------------------------------
+# Unit levels (RecomputeLevels, plastix.hpp:466-537)
+# ---------------------------------------------------------------------------
+def recompute_levels(n_units, n_input, from_id, to_id, dead=None, level=None):
+    """Returns (levels uint16[n_units], rounds). ``level`` gives the levels
+    before the call (input units keep theirs unless re-reached); zeros if
+    omitted."""
+    lv = np.zeros(n_units, np.uint16) if level is None else np.array(level, np.uint16)
+    f = np.ascontiguousarray(from_id, np.uint32)
+    t = np.ascontiguousarray(to_id, np.uint32)
+    d = None if dead is None else np.ascontiguousarray(dead, np.uint8)
+    r = orc().oracle_recompute_levels(n_units, n_input, f.size, _p(f), _p(t), _p(d), _p(lv))
+    if r < 0:
+        raise ValueError("connection names a unit outside [0, n_units)")
+    return lv, int(r)
+
+
+def sort_connections_by_level(n_units, n_input, from_id, to_id, dead=None, level=None):
+    """SortConnectionsByLevel (plastix.hpp:539-579): (levels, perm, sorted
+    SrcLevel, NumLevels); perm is the stable order by SrcLevel."""
+    lv, _ = recompute_levels(n_units, n_input, from_id, to_id, dead, level)
+    f = np.ascontiguousarray(from_id, np.uint32)
+    src_level = lv[f] if f.size else np.zeros(0, np.uint16)
+    perm = stable_sort_perm_u32(src_level.astype(np.uint32))
+    sorted_level = src_level[perm.astype(np.int64)] if f.size else src_level
+    num_levels = int(sorted_level[-1]) + 1 if f.size else 0
+    return lv, perm, sorted_level, num_levels
+
+
+def ref_levels_run(n_units, n_input, from_id, to_id, dead=None):
+    """The reference itself: a Topological Network built with these units and
+    connections (its constructor runs SortConnectionsByLevel). Returns
+    (levels, FromId, ToId, SrcLevel, Dead after the sort) or None when the
+    reference was not built here."""
+    R = ref()
+    if R is None:
+        return None
+    n = len(from_id)
+    f = np.ascontiguousarray(from_id, np.uint32)
+    t = np.ascontiguousarray(to_id, np.uint32)
+    d = None if dead is None else np.ascontiguousarray(dead, np.uint8)
+    lv = np.zeros(n_units, np.uint16)
+    fo, to_, so = (np.zeros(n, np.uint32), np.zeros(n, np.uint32), np.zeros(n, np.uint16))
+    do = np.zeros(n, np.uint8)
+    rc = R.ref_levels_run(n_units, n_input, n, _p(f), _p(t), _p(d), _p(lv), _p(fo), _p(to_),
+                          _p(so), _p(do))
+    if rc != 0:
+        raise RuntimeError(f"ref_levels_run failed ({rc})")
+    return lv, fo, to_, so, do

@@ -375,3 +375,73 @@ void oracle_mse_sigmoid_grad(uint64_t n, const float* act, const float* target,
     grad[i] = acc * act[i] * (1.0f - act[i]);
   }
 }
+
+/* RecomputeLevels (include/plastix/plastix.hpp:466-537), restated: levels of
+ * the non-input units go to 0; nothing more without connections (:470-474).
+ * Live connections give in-degrees by ToId and outgoing lists by FromId
+ * (:488-512). Round L walks frontier L (round 0: the input units, :515-517);
+ * every live outgoing connection of a frontier unit decrements its target's
+ * in-degree (uint32, wrapping), and the decrement reaching 0 gives the target
+ * level L+1 (uint16) and appends it to frontier L+1 (:519-535). Returns the
+ * number of non-empty frontiers; -1 when a connection names a unit outside
+ * [0, n_units) or memory runs out. */
+int64_t oracle_recompute_levels(uint32_t n_units, uint32_t n_input, uint64_t n_conns,
+                                const uint32_t* from, const uint32_t* to,
+                                const uint8_t* dead, uint16_t* level) {
+  for (uint32_t i = n_input; i < n_units; ++i) level[i] = 0;
+  if (n_conns == 0) return 0;
+  uint32_t* indeg = calloc((size_t)n_units + 1, sizeof(uint32_t));
+  uint32_t* start = calloc((size_t)n_units + 2, sizeof(uint32_t));
+  uint32_t* targets = malloc((n_conns ? n_conns : 1) * sizeof(uint32_t));
+  uint32_t* cur = malloc(((size_t)n_units + 1) * sizeof(uint32_t));
+  uint32_t* nxt = malloc(((size_t)n_units + 1) * sizeof(uint32_t));
+  int64_t rounds = -1;
+  if (!indeg || !start || !targets || !cur || !nxt) goto done;
+  for (uint64_t c = 0; c < n_conns; ++c) {
+    if (dead && dead[c]) continue;
+    if (from[c] >= n_units || to[c] >= n_units) goto done;
+    start[from[c] + 1]++;
+    indeg[to[c]]++;
+  }
+  for (uint32_t i = 0; i < n_units; ++i) start[i + 1] += start[i];
+  {
+    /* outgoing lists in connection order: targets[start[u] .. start[u+1]) */
+    uint32_t* fill = malloc(((size_t)n_units + 1) * sizeof(uint32_t));
+    if (!fill) goto done;
+    memcpy(fill, start, ((size_t)n_units + 1) * sizeof(uint32_t));
+    for (uint64_t c = 0; c < n_conns; ++c) {
+      if (dead && dead[c]) continue;
+      targets[fill[from[c]]++] = to[c];
+    }
+    free(fill);
+  }
+  uint32_t n_cur = n_input;
+  for (uint32_t i = 0; i < n_input; ++i) cur[i] = i;
+  rounds = 0;
+  for (uint32_t L = 0; n_cur > 0; ++L) {
+    uint32_t n_nxt = 0;
+    for (uint32_t f = 0; f < n_cur; ++f) {
+      const uint32_t u = cur[f];
+      for (uint32_t e = start[u]; e < start[u + 1]; ++e) {
+        const uint32_t t = targets[e];
+        indeg[t] -= 1u;
+        if (indeg[t] == 0) {
+          level[t] = (uint16_t)(L + 1u);
+          nxt[n_nxt++] = t;
+        }
+      }
+    }
+    uint32_t* sw = cur;
+    cur = nxt;
+    nxt = sw;
+    n_cur = n_nxt;
+    ++rounds;
+  }
+done:
+  free(indeg);
+  free(start);
+  free(targets);
+  free(cur);
+  free(nxt);
+  return rounds;
+}

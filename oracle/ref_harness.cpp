@@ -89,6 +89,34 @@ struct SweepShard {
   size_t NumSrc;
 };
 
+// A Topological network with default traits (their constructor runs
+// SortConnectionsByLevel, hence RecomputeLevels, plastix.hpp:91-93).
+using TopoNet = plastix::Network<plastix::DefaultNetworkTraits<>>;
+
+// Allocates `NumNew` non-input units and an explicit connection list over all
+// units (any FromId/ToId below the unit count, Dead flags optional).
+struct GraphLayer {
+  size_t NumNew;
+  const uint32_t *From;
+  const uint32_t *To;
+  const uint8_t *Dead;
+  uint64_t N;
+
+  template <typename UA, typename CA>
+  plastix::UnitRange operator()(UA &U, CA &C, plastix::UnitRange) const {
+    plastix::UnitRange Units = U.AllocateMany(NumNew);
+    for (uint64_t I = 0; I < N; ++I) {
+      auto Id = C.Allocate();
+      plastix::GetField<plastix::ToIdTag>(C, Id) = To[I];
+      plastix::GetField<plastix::FromIdTag>(C, Id) = From[I];
+      plastix::GetField<plastix::SrcLevelTag>(C, Id) = 0;
+      plastix::GetField<plastix::DeadTag>(C, Id) = Dead ? Dead[I] != 0 : false;
+      plastix::GetWeight(C, Id) = 0.0f;
+    }
+    return Units;
+  }
+};
+
 }  // namespace
 
 
@@ -167,6 +195,31 @@ void ref_sweep_shards_step(void *handle, const float *act_in) {
 // destructor); the shards are released but their arenas stay mapped.
 void ref_sweep_shards_destroy(void *handle) {
   delete static_cast<std::vector<SweepShard> *>(handle);
+}
+
+// Unit levels and the level sort through the reference's own constructor:
+// n_input input units, n_units - n_input more, the given connections. Outputs
+// every unit's Level and the connections (FromId, ToId, SrcLevel, Dead) in the
+// order SortConnectionsByLevel left them.
+int ref_levels_run(uint64_t n_units, uint64_t n_input, uint64_t n_conn, const uint32_t *from,
+                   const uint32_t *to, const uint8_t *dead, uint16_t *level_out,
+                   uint32_t *from_out, uint32_t *to_out, uint16_t *src_level_out,
+                   uint8_t *dead_out) {
+  if (n_input > n_units) return -2;
+  g_unit_cap = n_units + 1;
+  g_conn_cap = n_conn + 1;
+  TopoNet Net(n_input, GraphLayer{n_units - n_input, from, to, dead, n_conn});
+  auto &CA = Net.GetConnAlloc();
+  auto &UA = Net.GetUnitAlloc();
+  if (CA.Size() != n_conn || UA.Size() != n_units) return -1;
+  for (uint64_t I = 0; I < n_units; ++I) level_out[I] = plastix::GetLevel(UA, I);
+  for (uint64_t C = 0; C < n_conn; ++C) {
+    from_out[C] = plastix::GetField<plastix::FromIdTag>(CA, C);
+    to_out[C] = plastix::GetField<plastix::ToIdTag>(CA, C);
+    src_level_out[C] = plastix::GetField<plastix::SrcLevelTag>(CA, C);
+    dead_out[C] = plastix::GetField<plastix::DeadTag>(CA, C) ? 1 : 0;
+  }
+  return 0;
 }
 
 }  // extern "C"

@@ -116,6 +116,10 @@ _SIGNATURES = {
     "plx_peer_close": (c_int, [c_void_p, c_void_p]),
     "plx_peer_barrier": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint64]),
     "plx_copy_device": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_recompute_levels_scratch_bytes": (ctypes.c_size_t, [c_uint64, c_uint64]),
+    "plx_recompute_levels": (c_int, [c_void_p, c_uint32, c_uint32, c_uint64, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_src_levels": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32, c_void_p]),
     "plx_probe_gather": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p, c_void_p]),
     "plx_probe_sweep_nofold": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32,
                                        c_void_p, c_void_p, ctypes.c_float, ctypes.c_float,

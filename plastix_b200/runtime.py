@@ -272,6 +272,54 @@ def radix_sort_u32(ctx: Context, keys: torch.Tensor, keys_out: torch.Tensor,
          begin_bit, end_bit, _ptr(s), s.numel())
 
 
+def recompute_levels(ctx: Context, n_units: int, n_input: int, from_id: torch.Tensor,
+                     to_id: torch.Tensor, level: torch.Tensor, *,
+                     dead: Optional[torch.Tensor] = None, rounds: Optional[torch.Tensor] = None,
+                     scratch: Optional[Scratch] = None) -> None:
+    """RecomputeLevels (plastix.hpp:466-537) on the device: ``level`` (int16
+    tensor holding the uint16 levels of all ``n_units`` units) is reset for
+    the non-input units and refilled by the level-parallel Kahn pass over the
+    live connections. ``rounds`` (optional 1-element int32 device tensor)
+    receives the number of non-empty frontiers."""
+    n = int(from_id.numel())
+    nbytes = _abi.lib().plx_recompute_levels_scratch_bytes(n_units, n)
+    s = (scratch or Scratch(ctx.device)).get(nbytes)
+    call("plx_recompute_levels", ctx.handle, n_units, n_input, n, _ptr(from_id) if n else None,
+         _ptr(to_id) if n else None, _ptr(dead) if n else None, _ptr(level) if n_units else None,
+         _ptr(rounds), _ptr(s), s.numel())
+
+
+def sort_connections_by_level(ctx: Context, n_units: int, n_input: int,
+                              from_id: torch.Tensor, to_id: torch.Tensor, level: torch.Tensor,
+                              pairs, *, dead: Optional[torch.Tensor] = None,
+                              scratch: Optional[Scratch] = None):
+    """SortConnectionsByLevel (plastix.hpp:539-579) on the device: recompute
+    the unit levels, refresh SrcLevel = level[FromId], stable radix sort of the
+    connections on the 16-bit SrcLevel, Gather of every field in ``pairs``
+    ((src, dst) tensors; include FromId, ToId and Dead there to move them).
+    Returns (perm, sorted SrcLevel as int16, NumLevels as a 1-element int32
+    device tensor: the largest SrcLevel + 1, 0 without connections)."""
+    n = int(from_id.numel())
+    dev = from_id.device
+    recompute_levels(ctx, n_units, n_input, from_id, to_id, level, dead=dead, scratch=scratch)
+    src_level = torch.empty(n, dtype=torch.int16, device=dev)
+    if n:
+        call("plx_src_levels", ctx.handle, n, _ptr(from_id), _ptr(level), n_units,
+             _ptr(src_level))
+    keys = src_level.to(torch.int32)
+    keys_out = torch.empty(n, dtype=torch.int32, device=dev)
+    perm = torch.empty(n, dtype=torch.int32, device=dev)
+    num_levels = torch.zeros(1, dtype=torch.int32, device=dev)
+    if n:
+        radix_sort_u32(ctx, keys, keys_out, perm, 0, 16, scratch=scratch)
+        sorted_level = torch.empty_like(src_level)
+        gather(ctx, perm, list(pairs) + [(src_level, sorted_level)])
+        num_levels.copy_((keys_out[n - 1:] & 0xFFFF) + 1)
+    else:
+        sorted_level = src_level
+    return perm, sorted_level, num_levels
+
+
 def sort_unique_u64(ctx: Context, keys: torch.Tensor, out: torch.Tensor,
                     count_out: torch.Tensor, *, scratch: Optional[Scratch] = None) -> None:
     """Proposal commit: distinct keys of ``keys`` (int64 tensor holding the

@@ -72,3 +72,33 @@ def sparse_layer_device(n_src: int, n_dst: int, n_edges: int, seed: int, device,
     w = torch.randn(n_edges, generator=g, device=device, dtype=torch.float32) * w_std
     act = torch.rand(n_src, generator=g, device=device, dtype=torch.float32)
     return from_id, to_id, w, act
+
+
+def level_graph(n_units: int, n_input: int, n_conns: int, seed: int = 0, *,
+                back_edges: int = 0, dead_frac: float = 0.0, into_inputs: int = 0):
+    """Connections for level tests (RecomputeLevels): each connection runs
+    from a lower to a higher unit id, so the graph is acyclic, except
+    `back_edges` from higher to lower non-input ids (cycles) and `into_inputs`
+    from non-input units into input units. Returns (from_id, to_id, dead);
+    dead is None unless dead_frac > 0."""
+    rng = np.random.default_rng(seed)
+    n_dag = n_conns - back_edges - into_inputs
+    to = rng.integers(max(n_input, 1), n_units, n_dag).astype(np.int64)
+    frm = (rng.random(n_dag) * to).astype(np.int64)  # uniform in [0, to)
+    parts_f, parts_t = [frm], [to]
+    if back_edges:
+        a = rng.integers(n_input, n_units, back_edges)
+        b = rng.integers(n_input, n_units, back_edges)
+        parts_f.append(np.maximum(a, b))
+        parts_t.append(np.minimum(a, b))
+    if into_inputs:
+        parts_f.append(rng.integers(n_input, n_units, into_inputs))
+        parts_t.append(rng.integers(0, max(n_input, 1), into_inputs))
+    frm = np.concatenate(parts_f).astype(np.uint32)
+    to = np.concatenate(parts_t).astype(np.uint32)
+    order = rng.permutation(frm.size)
+    frm, to = np.ascontiguousarray(frm[order]), np.ascontiguousarray(to[order])
+    dead = None
+    if dead_frac > 0:
+        dead = (rng.random(frm.size) < dead_frac).astype(np.uint8)
+    return frm, to, dead

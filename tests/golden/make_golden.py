@@ -1,6 +1,7 @@
 """Regenerates the golden fixtures in this folder by running the REFERENCE
 implementation (oracle/_ref, compiled from the reference sources by
 oracle/build.py). Run from the repository root: python tests/golden/make_golden.py
+[fixture names]
 """
 import sys
 from pathlib import Path
@@ -77,12 +78,36 @@ def ipc_small():
                         w=rw, x=rx, err=rerr)
 
 
+LEVEL_CASES = {  # name: (n_units, n_input, n_conns, seed, back_edges, dead_frac, into_inputs)
+    "dag": (3000, 40, 12000, 1, 0, 0.0, 0),
+    "cyclic": (3000, 40, 12000, 2, 30, 0.0, 0),
+    "dead": (3000, 40, 12000, 3, 0, 0.15, 0),
+    "into_inputs": (3000, 40, 12000, 4, 0, 0.0, 25),
+}
+
+
+def levels_small():
+    """RecomputeLevels + SortConnectionsByLevel through the reference's own
+    Topological constructor, on the level_graph cases above."""
+    out = {}
+    for name, (nu, ni, nc, seed, back, dfrac, into) in LEVEL_CASES.items():
+        f, t, d = workloads.level_graph(nu, ni, nc, seed, back_edges=back, dead_frac=dfrac,
+                                        into_inputs=into)
+        lv, fo, to, so, do = oracle.ref_levels_run(nu, ni, f, t, d)
+        out.update({f"{name}_params": np.array([nu, ni, nc, seed, back, into], np.int64),
+                    f"{name}_dead_frac": np.float64(dfrac), f"{name}_level": lv,
+                    f"{name}_from": fo, f"{name}_to": to, f"{name}_src_level": so,
+                    f"{name}_dead": do})
+    np.savez_compressed(HERE / "levels_small.npz", **out)
+
+
 if __name__ == "__main__":
     ob.build()
     if oracle.ref() is None:
         sys.exit("reference build missing: the reference tree is needed to make fixtures")
-    sweep_hebbian_small()
-    swifttd_small()
-    mlp_xor_small()
-    ipc_small()
+    makers = {"sweep_hebbian_small": sweep_hebbian_small, "swifttd_small": swifttd_small,
+              "mlp_xor_small": mlp_xor_small, "ipc_small": ipc_small,
+              "levels_small": levels_small}
+    for name in sys.argv[1:] or list(makers):  # names given: only those fixtures
+        makers[name]()
     print("fixtures written to", HERE)

@@ -196,3 +196,73 @@ def test_backward_descending_order_known_answer(orc):
     dval[2] = 1.0
     out = orc.backward(f, t, w, dval, n, 0, 2)
     assert list(out[:2]) == [2.0, 3.0]
+
+
+# ---------------------------------------------------------------------------
+# RecomputeLevels / SortConnectionsByLevel (plastix.hpp:466-579)
+# ---------------------------------------------------------------------------
+def test_levels_known_answer(orc):
+    # reference tests/test_plastix.cpp:949-960 (FCLayerLevelProgression):
+    # 2 inputs -> FC 3 -> FC 1 gives levels 0,0,1,1,1,2
+    f, t, n = fc_edges([2, 3, 1])
+    lv, rounds = orc.recompute_levels(n, 2, f, t)
+    np.testing.assert_array_equal(lv, [0, 0, 1, 1, 1, 2])
+    assert rounds == 3
+    # :962-974 (ConnectionsSortedBySrcLevel): sorted SrcLevel non-decreasing
+    _, perm, sl, nl = orc.sort_connections_by_level(n, 2, f, t)
+    assert np.all(np.diff(sl.astype(np.int64)) >= 0) and nl == 2
+
+
+def _level_case(z, name):
+    nu, ni, nc, seed, back, into = (int(x) for x in z[f"{name}_params"])
+    return nu, ni, workloads.level_graph(nu, ni, nc, seed, back_edges=back,
+                                         dead_frac=float(z[f"{name}_dead_frac"]),
+                                         into_inputs=into)
+
+
+@pytest.mark.parametrize("name", ["dag", "cyclic", "dead", "into_inputs"])
+def test_levels_oracle_matches_reference_fixture(orc, name):
+    """The reference's own constructor (SortConnectionsByLevel) made the
+    fixture: levels of every unit and the connections in sorted order."""
+    z = np.load(GOLDEN / "levels_small.npz")
+    nu, ni, (f, t, d) = _level_case(z, name)
+    lv, perm, sl, _ = orc.sort_connections_by_level(nu, ni, f, t, d)
+    np.testing.assert_array_equal(lv, z[f"{name}_level"])
+    p = perm.astype(np.int64)
+    np.testing.assert_array_equal(f[p], z[f"{name}_from"])
+    np.testing.assert_array_equal(t[p], z[f"{name}_to"])
+    np.testing.assert_array_equal(sl, z[f"{name}_src_level"])
+    if d is not None:
+        np.testing.assert_array_equal(d[p], z[f"{name}_dead"])
+
+
+@pytest.mark.parametrize("seed", [11, 12])
+def test_levels_oracle_matches_reference_build(orc, seed):
+    if orc.ref() is None:
+        pytest.skip("reference build not present")
+    rng = np.random.default_rng(seed)
+    nu, ni = int(rng.integers(200, 4000)), int(rng.integers(0, 60))
+    f, t, d = workloads.level_graph(nu, ni, int(rng.integers(0, 20000)), seed,
+                                    back_edges=int(rng.integers(0, 20)), dead_frac=0.1,
+                                    into_inputs=int(rng.integers(0, 10)) if ni else 0)
+    lv_r, f_r, t_r, sl_r, d_r = orc.ref_levels_run(nu, ni, f, t, d)
+    lv, perm, sl, _ = orc.sort_connections_by_level(nu, ni, f, t, d)
+    np.testing.assert_array_equal(lv, lv_r)
+    np.testing.assert_array_equal(f[perm.astype(np.int64)], f_r)
+    np.testing.assert_array_equal(sl, sl_r)
+
+
+def test_levels_edge_cases(orc):
+    # no connections: only the reset of non-input levels (plastix.hpp:470-474)
+    lv, r = orc.recompute_levels(5, 2, [], [], level=[7, 8, 9, 9, 9])
+    np.testing.assert_array_equal(lv, [7, 8, 0, 0, 0])
+    assert r == 0
+    # no input units: frontier 0 is empty, every level 0
+    lv, r = orc.recompute_levels(4, 0, [0, 1, 2], [1, 2, 3])
+    assert r == 0 and not lv.any()
+    # a cycle and everything below it stays at 0
+    lv, _ = orc.recompute_levels(5, 1, [0, 1, 2, 1], [1, 2, 1, 4])
+    np.testing.assert_array_equal(lv, [0, 0, 0, 0, 0])
+    # an input unit fed by a reached unit is reached again and gets a level
+    lv, _ = orc.recompute_levels(3, 1, [0, 1], [1, 0])
+    np.testing.assert_array_equal(lv, [2, 1, 0])
