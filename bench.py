@@ -57,12 +57,14 @@ def parse_args():
     p.add_argument("--ipc-units", type=int, default=1 << 18,
                    help="units per layer of the ipc workload (2^18 in the configuration)")
     p.add_argument("--ipc-fan-in", type=int, default=2048)
-    p.add_argument("--workload", choices=["sweep", "swifttd", "ipc", "structural", "ceiling"],
+    p.add_argument("--workload",
+                   choices=["sweep", "swifttd", "ipc", "structural", "ceiling", "levels"],
                    default="sweep",
                    help="sweep: the single-layer fwd+Hebbian sweep (default, the headline); "
                         "swifttd: 4M-feature SwiftTD learner; ipc: 5-layer predictive-coding "
                         "net; structural: prune/regrow/re-sort/forward step; ceiling: the sweep "
-                        "beside the same traffic without row folds and random gathers alone")
+                        "beside the same traffic without row folds and random gathers alone; "
+                        "levels: RecomputeLevels + SortConnectionsByLevel at 2^24 connections")
     return p.parse_args()
 
 
@@ -792,11 +794,69 @@ def bench_ceiling(args):
     ctx.close()
 
 
+def bench_levels(args):
+    """Level re-sort after a structural step, Topological model, at the
+    structural configuration's size (2^23 input units, 2^23 destination
+    units, 2^24 connections, FromId/ToId/Weight/Age fields): RecomputeLevels
+    then SortConnectionsByLevel (SrcLevel refresh, stable radix sort on the
+    16-bit key, Gather of every field). The unit is connections per second
+    of the whole re-sort; the roofline is taken on RecomputeLevels alone."""
+    import numpy as np
+    import torch
+
+    from plastix_b200.runtime import (Context, Scratch, recompute_levels,
+                                      sort_connections_by_level)
+
+    ctx = Context(0)
+    device = ctx.device
+    n_in, n = 1 << 23, 1 << 24
+    n_units = 2 * n_in
+    g = torch.Generator(device=device)
+    g.manual_seed(args.seed)
+    f = torch.randint(0, n_in, (n,), generator=g, device=device, dtype=torch.int32)
+    t = torch.randint(n_in, n_units, (n,), generator=g, device=device, dtype=torch.int32)
+    w = torch.randn(n, generator=g, device=device)
+    age = torch.randint(0, 256, (n,), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    level = torch.zeros(n_units, dtype=torch.int16, device=device)
+    outs = [torch.empty_like(x) for x in (f, t, w, age)]
+    pairs = list(zip((f, t, w, age), outs))
+    scr = Scratch(device)
+
+    def resort(i):
+        sort_connections_by_level(ctx, n_units, n_in, f, t, level, pairs, scratch=scr)
+
+    def recompute(i):
+        recompute_levels(ctx, n_units, n_in, f, t, level, scratch=scr)
+
+    ms_r, _ = _timed_loop(ctx.stream, recompute, args.steps, args.warmup)
+    ms, clocks = _timed_loop(ctx.stream, resort, args.steps, args.warmup)
+    ctx.sync()
+    rec_ms, step_ms = ms_r / args.steps, ms / args.steps
+    # minimum traffic of RecomputeLevels: FromId + ToId once, every level written
+    roof = _roof(8 * n + 2 * n_units, rec_ms, "levels_recompute_16M")
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+        fh = f.cpu().numpy().view(np.uint32)
+        th = t.cpu().numpy().view(np.uint32)
+        sec = _cpu_time(lambda: oracle.sort_connections_by_level(n_units, n_in, fh, th),
+                        budget_s=8.0, min_steps=1)
+        cpu = {"value": n / sec, "unit": "connections/s", "cores": 1, "kind": "port",
+               "sample": "oracle restatement of RecomputeLevels + stable level sort, full "
+                         "size, one thread (fields not gathered)"}
+    _line(args, "levels", n / (step_ms / 1e3), "connections/s", step_ms,
+          {"workload": "level re-sort (RecomputeLevels + SortConnectionsByLevel)",
+           "n_units": n_units, "n_input": n_in, "connections": n,
+           "fields": "FromId, ToId, Weight, Age", "recompute_ms": rec_ms},
+          roof, cpu, None, clocks, None)
+    ctx.close()
+
+
 def run_other(args):
     if args.gpus != 1 and args.workload != "ipc":
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
     return {"swifttd": bench_swifttd, "ipc": bench_ipc, "structural": bench_structural,
-            "ceiling": bench_ceiling}[args.workload](args) or 0
+            "ceiling": bench_ceiling, "levels": bench_levels}[args.workload](args) or 0
 
 
 def main():

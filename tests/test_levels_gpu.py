@@ -104,6 +104,21 @@ def test_levels_random_graphs(ctx, orc, back, dead_frac, into):
     assert rounds == want_rounds
 
 
+@pytest.mark.parametrize("dead_frac", [0.0, 0.3])
+def test_levels_two_level_graph(ctx, orc, dead_frac):
+    """The structural configuration's shape (inputs -> destinations): the
+    pass ends within its edge-centric rounds, without outgoing lists."""
+    rng = np.random.default_rng(21)
+    n_in, n_out, n = 300_000, 300_000, 1_500_000
+    f = rng.integers(0, n_in, n).astype(np.uint32)
+    t = rng.integers(n_in, n_in + n_out, n).astype(np.uint32)
+    d = (rng.random(n) < dead_frac).astype(np.uint8) if dead_frac else None
+    lv, rounds = run_levels(ctx, n_in + n_out, n_in, f, t, d)
+    want, want_rounds = orc.recompute_levels(n_in + n_out, n_in, f, t, d)
+    np.testing.assert_array_equal(lv, want)
+    assert rounds == want_rounds == 2
+
+
 def test_levels_deep_chain_wraps_uint16(ctx, orc):
     """70,000 rounds in one launch; levels past 65535 wrap as the reference's
     uint16 cast does."""
