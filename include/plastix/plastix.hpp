@@ -19,9 +19,20 @@
 //     mutate the global state from those hooks (a reduction into a global, as
 //     SwiftTD does) set `static constexpr bool SequentialConnectionUpdate =
 //     true` in their traits to keep the reference's sequential semantics.
-//   * Structural policies (PruneUnit/PruneConn/AddUnit/AddConn) are not
-//     supported here; structural change runs through the C ABI (compaction,
-//     radix re-sort, regrowth).
+//   * Structural policies: PruneUnit and PruneConn run per unit / per
+//     connection on the device; AddConn's proposals are enumerated on the
+//     device in the reference's order (level window, unit pairs, the four
+//     checks), then sorted, de-duplicated and committed through the C ABI
+//     (libplastix_b200: link with -lplastix_b200), and Topological networks
+//     re-sort by source level on the device (RecomputeLevels included), as
+//     the reference's constructor and DoStep do. The predicates run in
+//     parallel, so they must not change the global state -- traits with
+//     `static constexpr bool SequentialStructure = true` run them in one
+//     thread in the reference's order instead. AddUnit is not supported.
+//   * Topological passes follow the reference level by level: level L folds
+//     the connections whose SrcLevel is L - 1 into their targets' forward
+//     accumulators (one thread per unit, stored order), then applies the
+//     units of level L.
 //   * No fixed capacity: networks of any size that fit the GPU.
 //   * GetUnitAlloc()/GetConnAlloc() return host copies (downloaded on call;
 //     edits made through them are uploaded before the next Do* call).
@@ -29,6 +40,10 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <plastix_b200.h>
+
+#include <cub/block/block_scan.cuh>
+#include <cub/device/device_scan.cuh>
 
 #include <algorithm>
 #include <cstddef>
@@ -444,6 +459,211 @@ __global__ void k_update_conn(UV U, CV C, G *g, size_t n, bool sequential) {
 
 template <class Tr, class G> __global__ void k_reset(G *g) { Tr::ResetGlobal::Reset(*g); }
 
+// Traits flag for structural policies that mutate the global state (an RNG
+// drawn inside a predicate): prune, proposal and commit hooks then run in one
+// thread, in the reference's order.
+template <class T> struct SequentialStructure {
+  static constexpr bool value = false;
+};
+template <class T>
+  requires requires { T::SequentialStructure; }
+struct SequentialStructure<T> {
+  static constexpr bool value = T::SequentialStructure;
+};
+
+// Topological forward accumulation of level L (plastix.hpp:111-119 of the
+// reference): every unit folds, in stored order, those incoming connections
+// whose SrcLevel is L - 1 -- whatever the unit's own level. Connections are
+// kept sorted by SrcLevel, so each unit's incoming list is too; `cur` is the
+// unit's position in it, advanced level by level.
+template <class Tr, class UV, class CV, class G>
+__global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
+                                uint32_t *cur, size_t n, int L) {
+  using FP = typename Tr::ForwardPass;
+  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I >= n) return;
+  uint32_t k = cur[I];
+  const uint32_t e = in_ptr[I + 1];
+  if (k >= e) return;
+  const uint16_t want = (uint16_t)(L - 1);
+  auto acc = GetForwardAcc(U, I);
+  bool any = false;
+  for (; k < e; ++k) {
+    const uint32_t c = in_conn[k];
+    const uint16_t sl = GetField<SrcLevelTag>(C, c);
+    if (sl > want) break;
+    if (sl != want || GetField<DeadTag>(C, c)) continue;
+    acc = FP::Combine(acc, FP::Map(U, I, GetField<FromIdTag>(C, c), C, c, *g));
+    any = true;
+  }
+  cur[I] = k;
+  if (any) GetForwardAcc(U, I) = acc;
+}
+
+// DoPruneUnits (reference plastix.hpp:257-267): Pruned = ShouldPrune.
+template <class Tr, class UV, class G> __global__ void k_prune_units(UV U, G *g, size_t n, bool seq) {
+  const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t step = seq ? 1 : (size_t)gridDim.x * blockDim.x;
+  if (seq && first != 0) return;
+  for (size_t I = first; I < n; I += step)
+    GetField<PrunedTag>(U, I) = Tr::PruneUnit::ShouldPrune(U, I, *g) ? 1 : 0;
+}
+
+// DoPruneConnections (reference plastix.hpp:269-299): a live connection dies
+// when either endpoint was pruned or the connection policy says so.
+template <class Tr, class UV, class CV, class G>
+__global__ void k_prune_conns(UV U, CV C, G *g, size_t m, bool seq) {
+  constexpr bool HasUnit = !std::is_same_v<typename Tr::PruneUnit, NoPruneUnit>;
+  constexpr bool HasConn = !std::is_same_v<typename Tr::PruneConn, NoPruneConn>;
+  const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t step = seq ? 1 : (size_t)gridDim.x * blockDim.x;
+  if (seq && first != 0) return;
+  for (size_t c = first; c < m; c += step) {
+    if (GetField<DeadTag>(C, c)) continue;
+    const size_t to = GetField<ToIdTag>(C, c), from = GetField<FromIdTag>(C, c);
+    bool rm = false;
+    if constexpr (HasUnit) rm = GetField<PrunedTag>(U, to) || GetField<PrunedTag>(U, from);
+    if constexpr (HasConn)
+      if (!rm) rm = Tr::PruneConn::ShouldPrune(U, to, from, C, c, *g);
+    if (rm) GetField<DeadTag>(C, c) = 1;
+  }
+}
+
+// One level pair of DoAddConnections' window (reference plastix.hpp:363-389):
+// units UnitsByLevel[a0, a0+na) x UnitsByLevel[b0, b0+nb), slots numbered
+// from `first` in the reference's enumeration order.
+struct LevelPair {
+  uint64_t first;
+  uint32_t a0, na, b0, nb, same;
+};
+constexpr int kPropItems = 4;                      // slots per thread
+constexpr uint64_t kPropChunk = 256 * kPropItems;  // slots per block and chunk
+
+PLASTIX_HD inline uint64_t compact_edge(size_t from, size_t to) {  // CompactEdge::Bits
+  return (uint64_t)(uint32_t)from | ((uint64_t)(uint32_t)to << 32);
+}
+
+__device__ inline uint32_t find_pair(const LevelPair *p, uint32_t n, uint64_t s) {
+  uint32_t lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) / 2;
+    if (p[mid].first <= s) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// The proposals of one slot (unit pair), in the reference's order of checks.
+template <class Tr, class UV, class G>
+__device__ uint32_t propose_slot(UV &U, G *g, const LevelPair *pairs, uint32_t np,
+                                 const uint32_t *ubl, uint64_t s, uint64_t *out) {
+  using AC = typename Tr::AddConn;
+  const LevelPair P = pairs[find_pair(pairs, np, s)];
+  const uint64_t r = s - P.first;
+  const size_t A = ubl[P.a0 + r / P.nb], B = ubl[P.b0 + r % P.nb];
+  if (A == B) return 0;
+  uint32_t k = 0;
+  if (AC::ShouldAddIncomingConnection(U, A, B, *g)) out[k++] = compact_edge(B, A);
+  if (AC::ShouldAddOutgoingConnection(U, A, B, *g)) out[k++] = compact_edge(A, B);
+  if (!P.same) {
+    if (AC::ShouldAddIncomingConnection(U, B, A, *g)) out[k++] = compact_edge(A, B);
+    if (AC::ShouldAddOutgoingConnection(U, B, A, *g)) out[k++] = compact_edge(B, A);
+  }
+  return k;
+}
+
+// Parallel proposal enumeration in two passes over chunks of slots: COUNT
+// writes each chunk's number of proposals; WRITE puts them at the chunk's
+// offset in slot order, dropping those at index >= cap (the reference stops
+// proposing at its capacity). The predicates are evaluated in both passes.
+template <class Tr, bool WRITE, class UV, class G>
+__global__ void __launch_bounds__(256)
+    k_propose(UV U, G *g, const LevelPair *pairs, uint32_t np, const uint32_t *ubl, uint64_t total,
+              uint64_t n_chunks, uint64_t *chunk_counts, const uint64_t *chunk_off, uint64_t cap,
+              uint64_t *props) {
+  using BS = cub::BlockScan<uint32_t, 256>;
+  __shared__ typename BS::TempStorage tmp;
+  for (uint64_t ch = blockIdx.x; ch < n_chunks; ch += gridDim.x) {
+    uint64_t bits[4 * kPropItems];
+    uint32_t cnt = 0;
+    const uint64_t s0 = ch * kPropChunk + (uint64_t)threadIdx.x * kPropItems;
+    for (int it = 0; it < kPropItems; ++it) {
+      const uint64_t s = s0 + it;
+      if (s >= total) break;
+      cnt += propose_slot<Tr>(U, g, pairs, np, ubl, s, bits + cnt);
+    }
+    uint32_t off, agg;
+    BS(tmp).ExclusiveSum(cnt, off, agg);
+    if constexpr (!WRITE) {
+      if (threadIdx.x == 0) chunk_counts[ch] = agg;
+    } else {
+      const uint64_t base = chunk_off[ch] + off;
+      for (uint32_t k = 0; k < cnt; ++k)
+        if (base + k < cap) props[base + k] = bits[k];
+    }
+    __syncthreads();
+  }
+}
+
+// The same enumeration in one thread, stopping at the capacity exactly as the
+// reference does (a predicate is not called once the list is full).
+template <class Tr, class UV, class G>
+__global__ void k_propose_seq(UV U, G *g, const LevelPair *pairs, uint32_t np, const uint32_t *ubl,
+                              uint64_t cap, uint64_t *props, uint64_t *count) {
+  using AC = typename Tr::AddConn;
+  uint64_t n = 0;
+  for (uint32_t p = 0; p < np; ++p) {
+    const LevelPair P = pairs[p];
+    for (uint32_t ai = 0; ai < P.na; ++ai) {
+      const size_t A = ubl[P.a0 + ai];
+      for (uint32_t bi = 0; bi < P.nb; ++bi) {
+        const size_t B = ubl[P.b0 + bi];
+        if (A == B) continue;
+        if (n < cap && AC::ShouldAddIncomingConnection(U, A, B, *g)) props[n++] = compact_edge(B, A);
+        if (n < cap && AC::ShouldAddOutgoingConnection(U, A, B, *g)) props[n++] = compact_edge(A, B);
+        if (!P.same) {
+          if (n < cap && AC::ShouldAddIncomingConnection(U, B, A, *g))
+            props[n++] = compact_edge(A, B);
+          if (n < cap && AC::ShouldAddOutgoingConnection(U, B, A, *g))
+            props[n++] = compact_edge(B, A);
+        }
+      }
+    }
+  }
+  *count = n;
+}
+
+// Commit of the unique proposals (reference plastix.hpp:421-431): connection
+// m0 + i gets FromId, ToId and SrcLevel = Level[FromId] (the other fields
+// were zeroed), then InitConnection.
+template <class Tr, class UV, class CV, class G>
+__global__ void k_commit_conns(UV U, CV C, G *g, const uint64_t *edges, size_t k, size_t m0,
+                               bool seq) {
+  const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t step = seq ? 1 : (size_t)gridDim.x * blockDim.x;
+  if (seq && first != 0) return;
+  for (size_t i = first; i < k; i += step) {
+    const uint64_t b = edges[i];
+    const size_t c = m0 + i, F = (uint32_t)b, T = (uint32_t)(b >> 32);
+    GetField<FromIdTag>(C, c) = (uint32_t)F;
+    GetField<ToIdTag>(C, c) = (uint32_t)T;
+    GetField<SrcLevelTag>(C, c) = GetLevel(U, F);
+    Tr::AddConn::InitConnection(U, F, T, C, c, *g);
+  }
+}
+
+__global__ inline void k_widen_u16(const uint16_t *in, size_t n, uint32_t *out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = in[i];
+}
+
+__global__ inline void k_level_hist(const uint16_t *level, size_t n, uint32_t *hist) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    atomicAdd(hist + level[i], 1u);
+}
+
 }  // namespace detail
 
 // ---------------------------------------------------------------------------
@@ -460,11 +680,8 @@ template <typename Traits> class Network {
   using UView = typename UnitAllocator::View;
   using CView = typename ConnAllocator::View;
 
-  static_assert(std::is_same_v<typename Traits::PruneUnit, NoPruneUnit> &&
-                    std::is_same_v<typename Traits::PruneConn, NoPruneConn> &&
-                    std::is_same_v<typename Traits::AddUnit, NoAddUnit> &&
-                    std::is_same_v<typename Traits::AddConn, NoAddConn>,
-                "structural policies run through the C ABI on this path");
+  static_assert(std::is_same_v<typename Traits::AddUnit, NoAddUnit>,
+                "AddUnit policies are not supported on the device");
   static_assert(std::is_trivially_copyable_v<GlobalState>, "global state is copied to the GPU");
 
   template <typename... Builders>
@@ -478,9 +695,12 @@ template <typename Traits> class Network {
     UnitRange Prev{0, InputDim};
     ((Prev = Layers(UA, CA, Prev)), ...);
     OutputRange = Prev;
-    if constexpr (Traits::Model == Propagation::Topological) SortByLevel();
-    BuildIndex();
+    cuda_check(cudaGetDevice(&Device), "device");
     Upload();
+    // As the reference's constructor: Topological networks recompute the
+    // unit levels and sort the connections by source level.
+    if constexpr (Traits::Model == Propagation::Topological) SortConnectionsByLevel();
+    RebuildIndex();
   }
 
   Network(size_t InputDim, size_t OutputDim = 1) : Network(InputDim, FullyConnected<>{OutputDim}) {}
@@ -499,14 +719,21 @@ template <typename Traits> class Network {
                  "inputs");
     const size_t n = UA.Size();
     if constexpr (Traits::Model == Propagation::Topological) {
+      if (NeedsResort) SortConnectionsByLevel();
+      if (IndexStale) RebuildIndex();
+      if (n)
+        cuda_check(cudaMemcpyAsync(d_cursor, d_in_ptr, n * sizeof(uint32_t),
+                                   cudaMemcpyDeviceToDevice, Stream),
+                   "cursor");
       for (int L = 1; L <= NumLevels; ++L) {
-        detail::k_fwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
-            UV(), CV(), d_g, d_in_ptr, d_in_conn, NumInput, n, L);
+        detail::k_fwd_acc_level<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
+            UV(), CV(), d_g, d_in_ptr, d_in_conn, d_cursor, n, L);
         detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, L);
       }
     } else {
+      if (IndexStale) RebuildIndex();
       detail::k_fwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), CV(), d_g, d_in_ptr,
-                                                                        d_in_conn, NumInput, n, -1);
+                                                                        d_in_conn, 0, n, -1);
       detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, -1);
     }
     cuda_check(cudaGetLastError(), "forward pass");
@@ -534,12 +761,14 @@ template <typename Traits> class Network {
   void DoBackwardPass() {
     if constexpr (!std::is_same_v<BP, NoBackwardPass>) {
       SyncToDevice();
+      if (IndexStale) RebuildIndex();
       const size_t n = UA.Size();
       if constexpr (Traits::Model == Propagation::Topological) {
         for (int L = NumLevels; L >= 1; --L) {
           detail::k_bwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
               UV(), CV(), d_g, d_out_ptr, d_out_conn, n, L, false);
-          detail::k_bwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, 0, n, L);
+          detail::k_bwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput,
+                                                                             n, L);
         }
       } else {
         detail::k_bwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
@@ -579,10 +808,129 @@ template <typename Traits> class Network {
     }
   }
 
-  void DoPruneUnits() {}
-  void DoPruneConnections() {}
+  void DoPruneUnits() {
+    if constexpr (!std::is_same_v<typename Traits::PruneUnit, NoPruneUnit>) {
+      SyncToDevice();
+      const size_t n = UA.Size();
+      detail::k_prune_units<Traits><<<kSeq ? 1 : detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, n,
+                                                                                     kSeq);
+      cuda_check(cudaGetLastError(), "prune units");
+    }
+  }
+
+  void DoPruneConnections() {
+    if constexpr (!std::is_same_v<typename Traits::PruneUnit, NoPruneUnit> ||
+                  !std::is_same_v<typename Traits::PruneConn, NoPruneConn>) {
+      SyncToDevice();
+      const size_t m = CA.Size();
+      const unsigned grid = kSeq ? 1 : std::min<unsigned>(detail::blocks(m), 4096);
+      detail::k_prune_conns<Traits><<<grid, 256, 0, Stream>>>(UV(), CV(), d_g, m, kSeq);
+      cuda_check(cudaGetLastError(), "prune connections");
+    }
+  }
+
   void DoAddUnits() {}
-  void DoAddConnections() {}
+
+  // DoAddConnections (reference plastix.hpp:320-435): units bucketed by level
+  // (phase 0), the level-pair window enumerated on the device in the
+  // reference's order (phase 1), sort + unique commit (phases 2-3) through the
+  // C ABI, new connections appended and initialised by InitConnection.
+  void DoAddConnections() {
+    if constexpr (!std::is_same_v<typename Traits::AddConn, NoAddConn>) {
+      SyncToDevice();
+      const size_t n = UA.Size();
+      if (n == 0) return;
+      plx_ctx *ctx = PlxCtx();
+      // phase 0: units by level (stable by id), level offsets
+      uint32_t *hist = Buf<uint32_t>(0, 65536);
+      cuda_check(cudaMemsetAsync(hist, 0, 65536 * sizeof(uint32_t), Stream), "histogram");
+      detail::k_level_hist<<<detail::blocks(n), 256, 0, Stream>>>(LevelPtr(), n, hist);
+      std::vector<uint32_t> h(65536);
+      cuda_check(cudaMemcpyAsync(h.data(), hist, h.size() * 4, cudaMemcpyDeviceToHost, Stream),
+                 "histogram");
+      cuda_check(cudaStreamSynchronize(Stream), "histogram");
+      uint32_t highest = 0;
+      for (uint32_t L = 0; L < 65536; ++L)
+        if (h[L]) highest = L;
+      std::vector<uint32_t> off(highest + 2, 0);
+      for (uint32_t L = 0; L <= highest; ++L) off[L + 1] = off[L] + h[L];
+      uint32_t *keys = Buf<uint32_t>(1, n), *keys_out = Buf<uint32_t>(2, n);
+      uint32_t *ubl = Buf<uint32_t>(3, n);
+      detail::k_widen_u16<<<detail::blocks(n), 256, 0, Stream>>>(LevelPtr(), n, keys);
+      RadixSort(n, keys, keys_out, ubl, 16);
+      // phase 1: the level pairs of the window, in the reference's order
+      std::vector<detail::LevelPair> pairs;
+      uint64_t total = 0;
+      auto add = [&](uint32_t La, uint32_t Lb) {
+        const uint32_t na = off[La + 1] - off[La], nb = off[Lb + 1] - off[Lb];
+        if (!na || !nb) return;
+        pairs.push_back({total, off[La], na, off[Lb], nb, La == Lb ? 1u : 0u});
+        total += (uint64_t)na * nb;
+      };
+      constexpr uint32_t N = Traits::Neighbourhood;
+      const uint32_t init_right = std::min<uint32_t>(N, highest);
+      for (uint32_t La = 0; La <= init_right; ++La)
+        for (uint32_t Lb = La; Lb <= init_right; ++Lb) add(La, Lb);
+      for (uint32_t R = N + 1; R <= highest; ++R)
+        for (uint32_t W = R - N; W <= R; ++W) add(W, R);
+      if (total == 0) return;
+      auto *d_pairs = Buf<detail::LevelPair>(4, pairs.size());
+      cuda_check(cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(detail::LevelPair),
+                                 cudaMemcpyHostToDevice, Stream),
+                 "level pairs");
+      const uint32_t np = (uint32_t)pairs.size();
+      uint64_t n_props = 0;
+      uint64_t *props = nullptr;
+      if constexpr (kSeq) {
+        const uint64_t cap = std::min<uint64_t>(ProposalCap, 4 * total);
+        props = Buf<uint64_t>(5, cap);
+        uint64_t *cnt = Buf<uint64_t>(6, 1);
+        detail::k_propose_seq<Traits><<<1, 1, 0, Stream>>>(UV(), d_g, d_pairs, np, ubl, cap, props,
+                                                           cnt);
+        cuda_check(cudaMemcpyAsync(&n_props, cnt, 8, cudaMemcpyDeviceToHost, Stream), "count");
+        cuda_check(cudaStreamSynchronize(Stream), "proposals");
+      } else {
+        const uint64_t n_chunks = (total + detail::kPropChunk - 1) / detail::kPropChunk;
+        uint64_t *counts = Buf<uint64_t>(6, n_chunks + 1), *coff = Buf<uint64_t>(7, n_chunks + 1);
+        const unsigned grid = (unsigned)std::min<uint64_t>(n_chunks, 8192);
+        detail::k_propose<Traits, false><<<grid, 256, 0, Stream>>>(
+            UV(), d_g, d_pairs, np, ubl, total, n_chunks, counts, nullptr, 0, nullptr);
+        cuda_check(cudaMemsetAsync(counts + n_chunks, 0, 8, Stream), "counts");
+        size_t tb = 0;
+        cuda_check(cub::DeviceScan::ExclusiveSum(nullptr, tb, counts, coff, n_chunks + 1, Stream),
+                   "scan");
+        void *tmp = Buf<uint8_t>(8, tb);
+        cuda_check(cub::DeviceScan::ExclusiveSum(tmp, tb, counts, coff, n_chunks + 1, Stream),
+                   "scan");
+        cuda_check(cudaMemcpyAsync(&n_props, coff + n_chunks, 8, cudaMemcpyDeviceToHost, Stream),
+                   "count");
+        cuda_check(cudaStreamSynchronize(Stream), "proposals");
+        n_props = std::min<uint64_t>(n_props, ProposalCap);
+        if (n_props == 0) return;
+        props = Buf<uint64_t>(5, n_props);
+        detail::k_propose<Traits, true><<<grid, 256, 0, Stream>>>(
+            UV(), d_g, d_pairs, np, ubl, total, n_chunks, nullptr, coff, n_props, props);
+      }
+      cuda_check(cudaGetLastError(), "proposals");
+      if (n_props == 0) return;
+      // phases 2-3: sorted unique proposals, committed in that order
+      uint64_t *uniq = Buf<uint64_t>(9, n_props), *ucnt = Buf<uint64_t>(10, 1);
+      const size_t sb = plx_sort_unique_u64_scratch_bytes(n_props);
+      plx_check(plx_sort_unique_u64(ctx, n_props, props, uniq, ucnt, Buf<uint8_t>(11, sb), sb),
+                "plx_sort_unique_u64");
+      uint64_t k = 0;
+      cuda_check(cudaMemcpyAsync(&k, ucnt, 8, cudaMemcpyDeviceToHost, Stream), "unique");
+      cuda_check(cudaStreamSynchronize(Stream), "unique");
+      if (k == 0) return;
+      const size_t m0 = CA.Size();
+      GrowConnections(k);
+      detail::k_commit_conns<Traits><<<kSeq ? 1 : detail::blocks(k), 256, 0, Stream>>>(
+          UV(), CV(), d_g, uniq, k, m0, kSeq);
+      cuda_check(cudaGetLastError(), "commit");
+      NeedsResort = Traits::Model == Propagation::Topological;
+      IndexStale = true;
+    }
+  }
 
   void DoStep(std::span<const float> Inputs, std::span<const float> Targets = {}) {
     DoForwardPass(Inputs);
@@ -594,6 +942,8 @@ template <typename Traits> class Network {
     DoPruneConnections();
     DoAddUnits();
     DoAddConnections();
+    if constexpr (Traits::Model == Propagation::Topological)
+      if (NeedsResort) SortConnectionsByLevel();
     DoResetGlobalState();
   }
 
@@ -630,10 +980,49 @@ template <typename Traits> class Network {
     cuda_check(cudaMemcpyAsync(d_g, &g, sizeof(g), cudaMemcpyHostToDevice, Stream), "globals");
     cuda_check(cudaStreamSynchronize(Stream), "globals");
   }
-  void SetStream(cudaStream_t s) { Stream = s; }
+  void SetStream(cudaStream_t s) {
+    Stream = s;
+    if (Ctx) plx_check(plx_ctx_set_stream(Ctx, s), "plx_ctx_set_stream");
+  }
+  // Upper bound on one DoAddConnections' proposal list (the reference's is its
+  // connection capacity): proposals past it are not made.
+  void SetProposalCapacity(uint64_t n) { ProposalCap = n; }
   UnitRange GetOutputRange() const { return OutputRange; }
+  int GetNumLevels() const { return NumLevels; }
 
  private:
+  static constexpr bool kSeq = detail::SequentialStructure<Traits>::value;
+
+  static void plx_check(int rc, const char *what) {
+    if (rc) throw std::runtime_error(std::string(what) + ": " + plx_last_error());
+  }
+  plx_ctx *PlxCtx() {
+    if (!Ctx) plx_check(plx_ctx_create(Device, Stream, &Ctx), "plx_ctx_create");
+    return Ctx;
+  }
+  // Grow-only device scratch buffer `slot` of at least `count` elements.
+  template <class T> T *Buf(int slot, size_t count) {
+    const size_t bytes = std::max<size_t>(count, 1) * sizeof(T);
+    if (ScratchBytes[slot] < bytes) {
+      cuda_check(cudaStreamSynchronize(Stream), "scratch");
+      if (Scratch[slot]) cudaFree(Scratch[slot]);
+      cuda_check(cudaMalloc(&Scratch[slot], bytes), "scratch");
+      ScratchBytes[slot] = bytes;
+    }
+    return static_cast<T *>(Scratch[slot]);
+  }
+  void RadixSort(size_t n, const uint32_t *keys, uint32_t *keys_out, uint32_t *perm, uint32_t bits) {
+    const size_t sb = plx_radix_sort_scratch_bytes(n);
+    plx_check(plx_radix_sort_u32(PlxCtx(), n, keys, keys_out, perm, 0, bits, Buf<uint8_t>(12, sb),
+                                 sb),
+              "plx_radix_sort_u32");
+  }
+  static uint32_t BitsFor(size_t n) {
+    uint32_t b = 1;
+    while (b < 32 && (size_t(1) << b) < n) ++b;
+    return b;
+  }
+
   UView UV() const {
     UView v{};
     for (size_t i = 0; i < UnitAllocator::NumFields; ++i) v.ptr[i] = d_uf[i];
@@ -646,48 +1035,100 @@ template <typename Traits> class Network {
     v.size = CA.Size();
     return v;
   }
+  // Field positions of the core schema (detail::UnitAllocT / ConnAllocT).
+  uint16_t *LevelPtr() const { return static_cast<uint16_t *>(d_uf[4]); }
+  uint32_t *FromPtr() const { return static_cast<uint32_t *>(d_cf[0]); }
+  uint32_t *ToPtr() const { return static_cast<uint32_t *>(d_cf[1]); }
+  uint8_t *DeadPtr() const { return static_cast<uint8_t *>(d_cf[2]); }
+  uint16_t *SrcLevelPtr() const { return static_cast<uint16_t *>(d_cf[3]); }
 
-  // Stable reorder of the connections by source level (the Topological
-  // processing order), as the reference does at construction.
-  void SortByLevel() {
-    std::vector<size_t> perm(CA.Size());
-    for (size_t i = 0; i < perm.size(); ++i) perm[i] = i;
-    std::stable_sort(perm.begin(), perm.end(), [&](size_t a, size_t b) {
-      return CA.template Get<SrcLevelTag>(a) < CA.template Get<SrcLevelTag>(b);
-    });
-    CA.Gather(perm);
+  // SortConnectionsByLevel (reference plastix.hpp:539-579) on the device:
+  // RecomputeLevels, SrcLevel = Level[FromId], stable radix sort on the
+  // 16-bit key, Gather of every connection field; NumLevels = highest
+  // SrcLevel + 1.
+  void SortConnectionsByLevel() {
+    SyncToDevice();
+    const size_t n = UA.Size(), m = CA.Size();
+    plx_ctx *ctx = PlxCtx();
+    const size_t lb = plx_recompute_levels_scratch_bytes(n, m);
+    plx_check(plx_recompute_levels(ctx, (uint32_t)n, (uint32_t)NumInput, m, FromPtr(), ToPtr(),
+                                   DeadPtr(), LevelPtr(), nullptr, Buf<uint8_t>(13, lb), lb),
+              "plx_recompute_levels");
+    NeedsResort = false;
+    if (m == 0) {
+      NumLevels = 0;
+      return;
+    }
+    plx_check(plx_src_levels(ctx, m, FromPtr(), LevelPtr(), (uint32_t)n, SrcLevelPtr()),
+              "plx_src_levels");
+    uint32_t *keys = Buf<uint32_t>(1, m), *keys_out = Buf<uint32_t>(2, m);
+    uint32_t *perm = Buf<uint32_t>(3, m);
+    detail::k_widen_u16<<<detail::blocks(m), 256, 0, Stream>>>(SrcLevelPtr(), m, keys);
+    RadixSort(m, keys, keys_out, perm, 16);
+    std::vector<plx_field> f(ConnAllocator::NumFields);
+    std::vector<void *> fresh(ConnAllocator::NumFields);
+    for (size_t i = 0; i < ConnAllocator::NumFields; ++i) {
+      const size_t fb = ConnAllocator::field_bytes(i);
+      if (fb != 1 && fb != 2 && fb != 4 && fb != 8)
+        throw std::runtime_error("connection fields must be 1, 2, 4 or 8 bytes to be re-sorted");
+      cuda_check(cudaMalloc(&fresh[i], std::max<size_t>(1, m) * fb), "field");
+      f[i] = plx_field{d_cf[i], fresh[i], (uint32_t)fb, 0};
+    }
+    plx_check(plx_gather(ctx, m, perm, f.data(), (uint32_t)f.size()), "plx_gather");
+    uint32_t last = 0;
+    cuda_check(cudaMemcpyAsync(&last, keys_out + m - 1, 4, cudaMemcpyDeviceToHost, Stream),
+               "levels");
+    cuda_check(cudaStreamSynchronize(Stream), "levels");
+    for (size_t i = 0; i < ConnAllocator::NumFields; ++i) {
+      cudaFree(d_cf[i]);
+      d_cf[i] = fresh[i];
+    }
+    NumLevels = (int)(last & 0xFFFFu) + 1;
+    IndexStale = true;
   }
 
   // Incoming connection lists per destination (stored order) and outgoing per
-  // source (ascending index), as CSR arrays on the device.
-  void BuildIndex() {
+  // source (ascending index), as CSR arrays on the device: stable radix sorts
+  // of ToId and FromId, row offsets from the sorted keys.
+  void RebuildIndex() {
     const size_t n = UA.Size(), m = CA.Size();
-    NumLevels = 0;
-    for (size_t i = 0; i < n; ++i)
-      NumLevels = std::max<int>(NumLevels, (int)UA.template Get<LevelTag>(i));
-    std::vector<uint32_t> in_ptr(n + 1, 0), out_ptr(n + 1, 0), in_conn(m), out_conn(m);
-    for (size_t c = 0; c < m; ++c) {
-      ++in_ptr[CA.template Get<ToIdTag>(c) + 1];
-      ++out_ptr[CA.template Get<FromIdTag>(c) + 1];
+    for (uint32_t *p : {d_in_ptr, d_out_ptr, d_in_conn, d_out_conn, d_cursor})
+      if (p) cudaFree(p);
+    cuda_check(cudaMalloc(&d_in_ptr, (n + 1) * 4), "index");
+    cuda_check(cudaMalloc(&d_out_ptr, (n + 1) * 4), "index");
+    cuda_check(cudaMalloc(&d_in_conn, std::max<size_t>(1, m) * 4), "index");
+    cuda_check(cudaMalloc(&d_out_conn, std::max<size_t>(1, m) * 4), "index");
+    cuda_check(cudaMalloc(&d_cursor, std::max<size_t>(1, n) * 4), "index");
+    IndexStale = false;
+    if (m == 0) {
+      cuda_check(cudaMemsetAsync(d_in_ptr, 0, (n + 1) * 4, Stream), "index");
+      cuda_check(cudaMemsetAsync(d_out_ptr, 0, (n + 1) * 4, Stream), "index");
+      return;
     }
-    for (size_t i = 0; i < n; ++i) {
-      in_ptr[i + 1] += in_ptr[i];
-      out_ptr[i + 1] += out_ptr[i];
+    plx_ctx *ctx = PlxCtx();
+    uint32_t *keys_out = Buf<uint32_t>(2, m);
+    const uint32_t bits = BitsFor(n);
+    RadixSort(m, ToPtr(), keys_out, d_in_conn, bits);
+    plx_check(plx_csr_row_ptr(ctx, keys_out, m, 0, (uint32_t)n, d_in_ptr), "plx_csr_row_ptr");
+    RadixSort(m, FromPtr(), keys_out, d_out_conn, bits);
+    plx_check(plx_csr_row_ptr(ctx, keys_out, m, 0, (uint32_t)n, d_out_ptr), "plx_csr_row_ptr");
+  }
+
+  // Appends k zeroed connections (device arrays and the host copy's size).
+  void GrowConnections(size_t k) {
+    const size_t m = CA.Size();
+    for (size_t i = 0; i < ConnAllocator::NumFields; ++i) {
+      const size_t fb = ConnAllocator::field_bytes(i);
+      void *p = nullptr;
+      cuda_check(cudaMalloc(&p, (m + k) * fb), "field");
+      if (m)
+        cuda_check(cudaMemcpyAsync(p, d_cf[i], m * fb, cudaMemcpyDeviceToDevice, Stream), "field");
+      cuda_check(cudaMemsetAsync(static_cast<char *>(p) + m * fb, 0, k * fb, Stream), "field");
+      cuda_check(cudaStreamSynchronize(Stream), "field");
+      cudaFree(d_cf[i]);
+      d_cf[i] = p;
     }
-    std::vector<uint32_t> fi(in_ptr.begin(), in_ptr.end() - 1), fo(out_ptr.begin(), out_ptr.end() - 1);
-    for (size_t c = 0; c < m; ++c) {
-      in_conn[fi[CA.template Get<ToIdTag>(c)]++] = (uint32_t)c;
-      out_conn[fo[CA.template Get<FromIdTag>(c)]++] = (uint32_t)c;
-    }
-    auto up = [&](uint32_t *&d, const std::vector<uint32_t> &h) {
-      cuda_check(cudaMalloc(&d, std::max<size_t>(1, h.size()) * 4), "index");
-      if (!h.empty())
-        cuda_check(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice), "index");
-    };
-    up(d_in_ptr, in_ptr);
-    up(d_out_ptr, out_ptr);
-    up(d_in_conn, in_conn);
-    up(d_out_conn, out_conn);
+    for (size_t i = 0; i < k; ++i) CA.Allocate();
   }
 
   template <class A> void UploadAlloc(A &a, std::vector<void *> &d, bool alloc) {
@@ -727,11 +1168,16 @@ template <typename Traits> class Network {
     }
   }
   void Release() {
+    if (Stream) cudaStreamSynchronize(Stream);
+    else cudaDeviceSynchronize();
     for (void *p : d_uf) cudaFree(p);
     for (void *p : d_cf) cudaFree(p);
     for (void *p : {(void *)d_g, (void *)d_in_ptr, (void *)d_out_ptr, (void *)d_in_conn,
-                    (void *)d_out_conn, (void *)d_targets})
+                    (void *)d_out_conn, (void *)d_cursor, (void *)d_targets})
       if (p) cudaFree(p);
+    for (void *p : Scratch)
+      if (p) cudaFree(p);
+    if (Ctx) plx_ctx_destroy(Ctx);
   }
 
   size_t NumInput;
@@ -740,13 +1186,20 @@ template <typename Traits> class Network {
   ConnAllocator CA;
   int NumLevels = 0;
   size_t Step = 0;
+  int Device = 0;
   std::vector<void *> d_uf, d_cf;
   GlobalState *d_g = nullptr;
   uint32_t *d_in_ptr = nullptr, *d_out_ptr = nullptr, *d_in_conn = nullptr, *d_out_conn = nullptr;
+  uint32_t *d_cursor = nullptr;
   float *d_targets = nullptr;
   size_t TargetCap = 0;
   bool UnitDirty = false, ConnDirty = false;
+  bool NeedsResort = false, IndexStale = true;
+  uint64_t ProposalCap = uint64_t(1) << 26;
   cudaStream_t Stream = nullptr;
+  plx_ctx *Ctx = nullptr;
+  void *Scratch[16] = {};
+  size_t ScratchBytes[16] = {};
   std::vector<float> Output;
 };
 

@@ -97,6 +97,10 @@ def ref() -> Optional[ctypes.CDLL]:
         L.ref_ipc_run.restype = ctypes.c_int64
         L.ref_swifttd_example_run.argtypes = [c_uint64, c_void_p, c_void_p, c_int, c_float,
                                               c_void_p, c_void_p]
+        if hasattr(L, "ref_structural_run"):
+            L.ref_structural_run.argtypes = ([ctypes.c_int] + [c_uint32] * 4 + [ctypes.c_int]
+                                             + [c_void_p, c_uint64] + [c_void_p] * 10)
+            L.ref_structural_run.restype = c_int
         if hasattr(L, "ref_levels_run"):
             L.ref_levels_run.argtypes = [c_uint64, c_uint64, c_uint64] + [c_void_p] * 8
             L.ref_levels_run.restype = c_int
@@ -505,3 +509,44 @@ def ref_levels_run(n_units, n_input, from_id, to_id, dead=None):
     if rc != 0:
         raise RuntimeError(f"ref_levels_run failed ({rc})")
     return lv, fo, to_, so, do
+
+
+# ---------------------------------------------------------------------------
+# Structural policies through the reference's Network (oracle/structural_policies.hpp)
+# ---------------------------------------------------------------------------
+STRUCTURAL_CASES = {  # name: (variant, n_in, h1, h2, seed, steps, cap)
+    "small": (0, 4, 6, 3, 5, 5, 4096),
+    "medium": (1, 32, 200, 50, 9, 3, 200_000),
+}
+
+
+def structural_inputs(name):
+    variant, n_in, h1, h2, seed, steps, cap = STRUCTURAL_CASES[name]
+    return np.random.default_rng(100 + seed).uniform(-1, 1, (steps, n_in)).astype(np.float32)
+
+
+def ref_structural_run(name):
+    """A Topological reference network n_in -> FC h1 -> FC h2 stepped with the
+    structural test policies; returns a dict of the per-step outputs, the final
+    connections (storage order) and the units' levels and activations, or None
+    when the reference was not built here."""
+    R = ref()
+    if R is None:
+        return None
+    variant, n_in, h1, h2, seed, steps, cap = STRUCTURAL_CASES[name]
+    x = structural_inputs(name)
+    outs = np.zeros((steps, h2), np.float32)
+    frm, to = np.zeros(cap, np.uint32), np.zeros(cap, np.uint32)
+    dead, sl = np.zeros(cap, np.uint8), np.zeros(cap, np.uint16)
+    w = np.zeros(cap, np.float32)
+    nu_cap = n_in + h1 + h2
+    level, act = np.zeros(nu_cap, np.uint16), np.zeros(nu_cap, np.float32)
+    n_conn, n_units = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    rc = R.ref_structural_run(variant, n_in, h1, h2, seed, steps, _p(x), cap, _p(outs), _p(frm),
+                              _p(to), _p(dead), _p(sl), _p(w), ctypes.byref(n_conn), _p(level),
+                              _p(act), ctypes.byref(n_units))
+    if rc != 0:
+        raise RuntimeError(f"ref_structural_run failed ({rc})")
+    m, n = n_conn.value, n_units.value
+    return {"outputs": outs, "from": frm[:m], "to": to[:m], "dead": dead[:m],
+            "src_level": sl[:m], "w": w[:m], "level": level[:n], "act": act[:n]}

@@ -19,6 +19,8 @@ std::size_t plx_ref_conn_capacity() { return g_conn_cap; }
 
 #include <plastix/plastix.hpp>
 
+#include "structural_policies.hpp"
+
 #include <algorithm>
 #include <cstring>
 #include <memory>
@@ -120,6 +122,47 @@ struct GraphLayer {
 }  // namespace
 
 
+// Structural parity run: a Topological network n_in -> FC h1 -> FC h2
+// (weights RandomUniformWeight(seed, -0.3, 0.3), seed + 1 for the second
+// layer) with the policies of
+// structural_policies.hpp, `steps` DoStep calls on the given inputs
+// (steps x n_in). Outputs the per-step outputs (steps x h2), the final
+// connections in storage order (capacity `cap`), every unit's Level and
+// Activation.
+template <class Tr>
+static int structural_run(uint32_t n_in, uint32_t h1, uint32_t h2, uint32_t seed, int steps,
+                          const float *inputs, uint64_t cap, float *outputs, uint32_t *from,
+                          uint32_t *to, uint8_t *dead, uint16_t *src_level, float *w,
+                          uint64_t *n_conn, uint16_t *level, float *act, uint64_t *n_units) {
+  using Net = plastix::Network<Tr>;
+  g_unit_cap = n_in + h1 + h2 + 1;
+  g_conn_cap = cap + 1;
+  Net N(n_in, plastix::FullyConnected{h1, plastix::RandomUniformWeight{seed, -0.3f, 0.3f}},
+        plastix::FullyConnected{h2, plastix::RandomUniformWeight{seed + 1, -0.3f, 0.3f}});
+  for (int S = 0; S < steps; ++S) {
+    N.DoStep(std::span<const float>(inputs + (size_t)S * n_in, n_in));
+    auto out = N.GetOutput();
+    for (uint32_t I = 0; I < h2; ++I) outputs[(size_t)S * h2 + I] = out[I];
+  }
+  auto &CA = N.GetConnAlloc();
+  auto &UA = N.GetUnitAlloc();
+  if (CA.Size() > cap) return -1;
+  for (size_t C = 0; C < CA.Size(); ++C) {
+    from[C] = plastix::GetField<plastix::FromIdTag>(CA, C);
+    to[C] = plastix::GetField<plastix::ToIdTag>(CA, C);
+    dead[C] = plastix::GetField<plastix::DeadTag>(CA, C) ? 1 : 0;
+    src_level[C] = plastix::GetField<plastix::SrcLevelTag>(CA, C);
+    w[C] = plastix::GetWeight(CA, C);
+  }
+  *n_conn = CA.Size();
+  for (size_t I = 0; I < UA.Size(); ++I) {
+    level[I] = plastix::GetLevel(UA, I);
+    act[I] = plastix::GetActivation(UA, I);
+  }
+  *n_units = UA.Size();
+  return 0;
+}
+
 extern "C" {
 
 const char *ref_version() { return plastix::version(); }
@@ -195,6 +238,20 @@ void ref_sweep_shards_step(void *handle, const float *act_in) {
 // destructor); the shards are released but their arenas stay mapped.
 void ref_sweep_shards_destroy(void *handle) {
   delete static_cast<std::vector<SweepShard> *>(handle);
+}
+
+int ref_structural_run(int variant, uint32_t n_in, uint32_t h1, uint32_t h2, uint32_t seed,
+                       int steps, const float *inputs, uint64_t cap, float *outputs,
+                       uint32_t *from, uint32_t *to, uint8_t *dead, uint16_t *src_level, float *w,
+                       uint64_t *n_conn, uint16_t *level, float *act, uint64_t *n_units) {
+  using namespace structural_test;
+  if (variant == 0)
+    return structural_run<SmallTraits>(n_in, h1, h2, seed, steps, inputs, cap, outputs,
+                                                from, to, dead, src_level, w, n_conn, level, act,
+                                                n_units);
+  return structural_run<MediumTraits>(n_in, h1, h2, seed, steps, inputs, cap, outputs,
+                                                from, to, dead, src_level, w, n_conn, level, act,
+                                                n_units);
 }
 
 // Unit levels and the level sort through the reference's own constructor:

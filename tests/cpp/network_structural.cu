@@ -1,0 +1,84 @@
+// Structural parity program: the pure prune / add-connection policies of
+// oracle/structural_policies.hpp on the device Network (Topological), the
+// same network and inputs as the reference run that made the fixture.
+// Usage: network_structural <variant 0|1> <n_in> <h1> <h2> <seed> <steps> <dir>
+// Reads <dir>/inputs.bin (steps x n_in floats); writes outputs.bin and the
+// final connections (from, to, dead, src_level, w) and units (level, act).
+#include <plastix/plastix.hpp>
+
+#include "../../oracle/structural_policies.hpp"
+
+#include <cstdio>
+#include <cstdlib>
+#include <string>
+#include <vector>
+
+namespace {
+
+template <class T> void put(const std::string &dir, const char *name, const std::vector<T> &v) {
+  FILE *f = std::fopen((dir + "/" + name).c_str(), "wb");
+  if (!f) std::exit(3);
+  if (!v.empty()) std::fwrite(v.data(), sizeof(T), v.size(), f);
+  std::fclose(f);
+}
+
+template <class Tr> int run(uint32_t n_in, uint32_t h1, uint32_t h2, uint32_t seed, int steps,
+                            const std::string &dir) {
+  std::vector<float> x((size_t)steps * n_in);
+  FILE *f = std::fopen((dir + "/inputs.bin").c_str(), "rb");
+  if (!f || std::fread(x.data(), 4, x.size(), f) != x.size()) return 2;
+  std::fclose(f);
+  plastix::Network<Tr> N(n_in,
+                         plastix::FullyConnected{h1, plastix::RandomUniformWeight{seed, -0.3f, 0.3f}},
+                         plastix::FullyConnected{h2, plastix::RandomUniformWeight{seed + 1, -0.3f, 0.3f}});
+  std::vector<float> outs;
+  for (int s = 0; s < steps; ++s) {
+    N.DoStep(std::span<const float>(x.data() + (size_t)s * n_in, n_in));
+    auto o = N.GetOutput();
+    outs.insert(outs.end(), o.begin(), o.end());
+  }
+  auto &CA = N.GetConnAlloc();
+  auto &UA = N.GetUnitAlloc();
+  const size_t m = CA.Size(), n = UA.Size();
+  std::vector<uint32_t> from(m), to(m);
+  std::vector<uint8_t> dead(m);
+  std::vector<uint16_t> sl(m), level(n);
+  std::vector<float> w(m), act(n);
+  for (size_t c = 0; c < m; ++c) {
+    from[c] = plastix::GetField<plastix::FromIdTag>(CA, c);
+    to[c] = plastix::GetField<plastix::ToIdTag>(CA, c);
+    dead[c] = plastix::GetField<plastix::DeadTag>(CA, c) ? 1 : 0;
+    sl[c] = plastix::GetField<plastix::SrcLevelTag>(CA, c);
+    w[c] = plastix::GetWeight(CA, c);
+  }
+  for (size_t i = 0; i < n; ++i) {
+    level[i] = plastix::GetLevel(UA, i);
+    act[i] = plastix::GetActivation(UA, i);
+  }
+  put(dir, "outputs.bin", outs);
+  put(dir, "from.bin", from);
+  put(dir, "to.bin", to);
+  put(dir, "dead.bin", dead);
+  put(dir, "src_level.bin", sl);
+  put(dir, "w.bin", w);
+  put(dir, "level.bin", level);
+  put(dir, "act.bin", act);
+  return 0;
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+  if (argc != 8) return 1;
+  const int variant = std::atoi(argv[1]);
+  const uint32_t n_in = std::atoi(argv[2]), h1 = std::atoi(argv[3]), h2 = std::atoi(argv[4]);
+  const uint32_t seed = std::atoi(argv[5]);
+  const int steps = std::atoi(argv[6]);
+  try {
+    return variant == 0 ? run<structural_test::SmallTraits>(n_in, h1, h2, seed, steps, argv[7])
+                        : run<structural_test::MediumTraits>(n_in, h1, h2, seed, steps, argv[7]);
+  } catch (const std::exception &e) {
+    std::fprintf(stderr, "%s\n", e.what());
+    return 4;
+  }
+}

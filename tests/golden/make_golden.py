@@ -101,13 +101,34 @@ def levels_small():
     np.savez_compressed(HERE / "levels_small.npz", **out)
 
 
+def structural_net():
+    """The structural test policies (oracle/structural_policies.hpp) through the
+    reference's own Topological Network: the small case whole, the medium case
+    as sizes and SHA-256 digests of each array."""
+    import hashlib
+    out = {}
+    for name in ("small", "medium"):
+        variant, n_in, h1, h2, seed, steps, cap = oracle.STRUCTURAL_CASES[name]
+        r = oracle.ref_structural_run(name)
+        out[f"{name}_params"] = np.array([variant, n_in, h1, h2, seed, steps], np.int64)
+        out[f"{name}_inputs"] = oracle.structural_inputs(name)
+        for k, v in r.items():
+            v = np.ascontiguousarray(v).reshape(-1)
+            if name == "small":
+                out[f"{name}_{k}"] = v
+            else:
+                out[f"{name}_{k}_size"] = np.int64(v.size)
+                out[f"{name}_{k}_sha256"] = np.array(hashlib.sha256(v.tobytes()).hexdigest())
+    np.savez_compressed(HERE / "structural_net.npz", **out)
+
+
 if __name__ == "__main__":
     ob.build()
     if oracle.ref() is None:
         sys.exit("reference build missing: the reference tree is needed to make fixtures")
     makers = {"sweep_hebbian_small": sweep_hebbian_small, "swifttd_small": swifttd_small,
               "mlp_xor_small": mlp_xor_small, "ipc_small": ipc_small,
-              "levels_small": levels_small}
+              "levels_small": levels_small, "structural_net": structural_net}
     for name in sys.argv[1:] or list(makers):  # names given: only those fixtures
         makers[name]()
     print("fixtures written to", HERE)

@@ -11,6 +11,11 @@ the reference header library, against the reference-made fixtures:
 * network_swifttd.cu -- 200 SwiftTD steps (per-connection hooks that add
   into the globals, run with the sequential connection update): V per step,
   weights and log step sizes at 1e-5 relative.
+* network_structural.cu -- the structural policies of
+  oracle/structural_policies.hpp (unit and connection pruning, hash-chosen
+  connection proposals, commit with InitConnection, Topological re-sort with
+  RecomputeLevels) on a small and a medium network: every output, connection
+  field and unit level bit for bit (the medium case through digests).
 
 On the CPU the programs are compiled (nvcc cross-compiles for sm_100a)."""
 import subprocess
@@ -26,10 +31,14 @@ NVCC = "/usr/local/cuda/bin/nvcc"
 
 def compile_prog(name: str, out: Path) -> Path:
     exe = out / name
+    lib = ROOT / "plastix_b200"
     cmd = [NVCC, "-std=c++20", "--expt-relaxed-constexpr", "-gencode",
-           "arch=compute_100a,code=sm_100a", "-O2", f"-I{ROOT / 'include'}",
-           str(ROOT / "tests" / "cpp" / f"{name}.cu"), "-o", str(exe)]
-    subprocess.run(cmd, check=True, capture_output=True, text=True)
+           "arch=compute_100a,code=sm_100a", "-O2", "--fmad=false", f"-I{ROOT / 'include'}",
+           str(ROOT / "tests" / "cpp" / f"{name}.cu"), "-o", str(exe),
+           f"-L{lib}", "-lplastix_b200", f"-Xlinker=-rpath,{lib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode:
+        raise RuntimeError(f"nvcc failed:\n{r.stdout}\n{r.stderr}")
     return exe
 
 
@@ -41,7 +50,8 @@ def parse(out: str):
     return {k: np.array(v, np.float32) for k, v in vals.items()}
 
 
-@pytest.mark.parametrize("name", ["network_xor", "network_ipc", "network_swifttd"])
+@pytest.mark.parametrize("name", ["network_xor", "network_ipc", "network_swifttd",
+                                  "network_structural"])
 def test_device_network_programs_compile(tmp_path, name):
     assert compile_prog(name, tmp_path).exists()
 
@@ -85,3 +95,39 @@ def test_device_network_swifttd_matches_reference(tmp_path):
     np.testing.assert_allclose(v["v"], z["v"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(v["w"], z["fields"][0], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(v["b"], z["fields"][9], rtol=1e-5, atol=1e-6)
+
+
+def _run_structural(tmp_path, name):
+    z = np.load(GOLDEN / "structural_net.npz")
+    variant, n_in, h1, h2, seed, steps = (int(v) for v in z[f"{name}_params"])
+    np.ascontiguousarray(z[f"{name}_inputs"], np.float32).tofile(tmp_path / "inputs.bin")
+    exe = compile_prog("network_structural", tmp_path)
+    r = subprocess.run([str(exe), str(variant), str(n_in), str(h1), str(h2), str(seed),
+                        str(steps), str(tmp_path)], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    types = {"outputs": np.float32, "from": np.uint32, "to": np.uint32, "dead": np.uint8,
+             "src_level": np.uint16, "w": np.float32, "level": np.uint16, "act": np.float32}
+    got = {k: np.fromfile(tmp_path / f"{k}.bin", dtype=t) for k, t in types.items()}
+    return z, got
+
+
+@pytest.mark.gpu
+def test_device_network_structural_small_matches_reference(tmp_path):
+    """Two-way proposals (into input units, cycles), a unit pruned at step 2,
+    weights pruned below 0.02: five steps, every array bit for bit."""
+    z, got = _run_structural(tmp_path, "small")
+    for k, v in got.items():
+        want = z[f"small_{k}"].reshape(-1)
+        assert v.size == want.size, k
+        np.testing.assert_array_equal(v.view(np.uint8), want.view(np.uint8), err_msg=k)
+
+
+@pytest.mark.gpu
+def test_device_network_structural_medium_matches_reference(tmp_path):
+    """32 -> 200 -> 50 with forward proposals over ~60k unit pairs per step
+    (the parallel enumeration runs over many chunks): digests of every array."""
+    import hashlib
+    z, got = _run_structural(tmp_path, "medium")
+    for k, v in got.items():
+        assert v.size == int(z[f"medium_{k}_size"]), k
+        assert hashlib.sha256(v.tobytes()).hexdigest() == str(z[f"medium_{k}_sha256"]), k
