@@ -36,7 +36,8 @@
 //   * No fixed capacity: networks of any size that fit the GPU.
 //   * GetUnitAlloc()/GetConnAlloc() return host copies (downloaded on call;
 //     edits made through them are uploaded before the next Do* call).
-//     GetGlobals() (an addition) returns the global state.
+//     GetGlobals()/SetGlobals() and Save(path)/Load(path) (checkpoints of
+//     every field plus the global state) are additions.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -48,6 +49,7 @@
 #include <algorithm>
 #include <cstddef>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <random>
 #include <ranges>
@@ -124,6 +126,11 @@ template <typename Entity, typename... Fs> class SOAAllocator {
     return {B, n_};
   }
   size_t Size() const { return n_; }
+  // Sets the number of entities (new ones value-initialised).
+  void Resize(size_t N) {
+    resize(N, std::index_sequence_for<Fs...>{});
+    n_ = N;
+  }
   template <typename Tag> auto &Get(size_t Id) {
     return std::get<FieldIndex<Tag, Fs...>::value>(store_)[Id];
   }
@@ -142,6 +149,9 @@ template <typename Entity, typename... Fs> class SOAAllocator {
   void Gather(const std::vector<size_t> &Perm) { gather(Perm, std::index_sequence_for<Fs...>{}); }
 
  private:
+  template <size_t... Is> void resize(size_t N, std::index_sequence<Is...>) {
+    (std::get<Is>(store_).resize(N), ...);
+  }
   template <size_t... Is> void push(std::index_sequence<Is...>) {
     (std::get<Is>(store_).emplace_back(), ...);
   }
@@ -990,8 +1000,114 @@ template <typename Traits> class Network {
   UnitRange GetOutputRange() const { return OutputRange; }
   int GetNumLevels() const { return NumLevels; }
 
+  // Checkpoint: a header (counts, output range, step, level state, field
+  // sizes, global-state size), every unit and connection field, the global
+  // state. Load replaces this network's state with the file's; the traits
+  // (field schema and global state) must be the ones that wrote it.
+  void Save(const std::string &Path) {
+    SyncToDevice();
+    Download(UA, d_uf);
+    Download(CA, d_cf);
+    const GlobalState G = GetGlobals();
+    CheckpointHeader H = Header();
+    FILE *F = std::fopen(Path.c_str(), "wb");
+    if (!F) throw std::runtime_error("cannot write " + Path);
+    bool ok = std::fwrite(&H, sizeof(H), 1, F) == 1;
+    ok = ok && WriteFieldSizes<UnitAllocator>(F) && WriteFieldSizes<ConnAllocator>(F);
+    for (size_t i = 0; ok && i < UnitAllocator::NumFields; ++i)
+      ok = WriteAll(F, UA.field_data(i), UA.Size() * UnitAllocator::field_bytes(i));
+    for (size_t i = 0; ok && i < ConnAllocator::NumFields; ++i)
+      ok = WriteAll(F, CA.field_data(i), CA.Size() * ConnAllocator::field_bytes(i));
+    ok = ok && WriteAll(F, &G, sizeof(G));
+    ok = (std::fclose(F) == 0) && ok;
+    if (!ok) throw std::runtime_error("short write to " + Path);
+  }
+
+  void Load(const std::string &Path) {
+    FILE *F = std::fopen(Path.c_str(), "rb");
+    if (!F) throw std::runtime_error("cannot read " + Path);
+    auto fail = [&](const char *why) {
+      std::fclose(F);
+      throw std::runtime_error(Path + ": " + why);
+    };
+    CheckpointHeader H{}, Want = Header();
+    if (std::fread(&H, sizeof(H), 1, F) != 1) fail("truncated header");
+    if (std::memcmp(H.Magic, Want.Magic, sizeof(H.Magic)) != 0) fail("not a checkpoint");
+    if (H.UnitFields != Want.UnitFields || H.ConnFields != Want.ConnFields ||
+        H.GlobalBytes != Want.GlobalBytes)
+      fail("field schema or global state differs from these traits");
+    if (!CheckFieldSizes<UnitAllocator>(F) || !CheckFieldSizes<ConnAllocator>(F))
+      fail("field sizes differ from these traits");
+    cuda_check(cudaStreamSynchronize(Stream), "load");
+    UA.Resize(H.Units);
+    CA.Resize(H.Conns);
+    for (size_t i = 0; i < UnitAllocator::NumFields; ++i)
+      if (!ReadAll(F, UA.field_data(i), UA.Size() * UnitAllocator::field_bytes(i)))
+        fail("truncated unit field");
+    for (size_t i = 0; i < ConnAllocator::NumFields; ++i)
+      if (!ReadAll(F, CA.field_data(i), CA.Size() * ConnAllocator::field_bytes(i)))
+        fail("truncated connection field");
+    GlobalState G{};
+    if (!ReadAll(F, &G, sizeof(G))) fail("truncated global state");
+    std::fclose(F);
+    for (void *p : d_uf) cudaFree(p);
+    for (void *p : d_cf) cudaFree(p);
+    UploadAlloc(UA, d_uf, true);
+    UploadAlloc(CA, d_cf, true);
+    SetGlobals(G);
+    NumInput = H.NumInput;
+    OutputRange = UnitRange(H.OutBegin, H.OutEnd);
+    Step = H.Step;
+    NumLevels = H.NumLevels;
+    NeedsResort = (H.Flags & 1u) != 0;
+    UnitDirty = ConnDirty = false;
+    RebuildIndex();
+  }
+
  private:
   static constexpr bool kSeq = detail::SequentialStructure<Traits>::value;
+
+  struct CheckpointHeader {
+    char Magic[8];
+    uint64_t NumInput, Step, Units, Conns, OutBegin, OutEnd;
+    int32_t NumLevels;
+    uint32_t Flags;  // bit 0: a level re-sort is pending
+    uint32_t UnitFields, ConnFields, GlobalBytes, Reserved;
+  };
+  CheckpointHeader Header() const {
+    CheckpointHeader H{};
+    std::memcpy(H.Magic, "PLXCKPT1", 8);
+    H.NumInput = NumInput;
+    H.Step = Step;
+    H.Units = UA.Size();
+    H.Conns = CA.Size();
+    H.OutBegin = OutputRange.Begin;
+    H.OutEnd = OutputRange.End;
+    H.NumLevels = NumLevels;
+    H.Flags = NeedsResort ? 1u : 0u;
+    H.UnitFields = (uint32_t)UnitAllocator::NumFields;
+    H.ConnFields = (uint32_t)ConnAllocator::NumFields;
+    H.GlobalBytes = (uint32_t)sizeof(GlobalState);
+    return H;
+  }
+  static bool WriteAll(FILE *F, const void *P, size_t N) {
+    return N == 0 || std::fwrite(P, 1, N, F) == N;
+  }
+  static bool ReadAll(FILE *F, void *P, size_t N) { return N == 0 || std::fread(P, 1, N, F) == N; }
+  template <class A> static bool WriteFieldSizes(FILE *F) {
+    for (size_t i = 0; i < A::NumFields; ++i) {
+      const uint32_t b = (uint32_t)A::field_bytes(i);
+      if (std::fwrite(&b, 4, 1, F) != 1) return false;
+    }
+    return true;
+  }
+  template <class A> static bool CheckFieldSizes(FILE *F) {
+    for (size_t i = 0; i < A::NumFields; ++i) {
+      uint32_t b = 0;
+      if (std::fread(&b, 4, 1, F) != 1 || b != A::field_bytes(i)) return false;
+    }
+    return true;
+  }
 
   static void plx_check(int rc, const char *what) {
     if (rc) throw std::runtime_error(std::string(what) + ": " + plx_last_error());

@@ -195,6 +195,19 @@ class HebbianSweepLayer:
     def weight(self) -> torch.Tensor:
         return self._w[self._cur]
 
+    def _state_tensors(self):
+        return {"weight": self._w[self._cur], "trace": self._e[self._cur],
+                "act_dst": self.act_dst}
+
+    def save(self, path) -> None:
+        """Checkpoint: current Weight and Trace, destination activations."""
+        from .checkpoint import save_state
+        save_state(self, path)
+
+    def load(self, path) -> None:
+        from .checkpoint import load_state
+        load_state(self, path)
+
     @property
     def trace(self) -> torch.Tensor:
         return self._e[self._cur]
@@ -370,6 +383,28 @@ class StructuralLayer:
         self.step_index = 0
         self.csr = DstCsr.from_sorted_async(ctx, self.t, n_src, n_dst)
 
+    def _state_tensors(self):
+        return {"from_id": self.f, "to_id": self.t, "weight": self.w, "age": self.age,
+                "act_dst": self.act_dst}
+
+    def _state_meta(self):
+        return {"step_index": self.step_index}
+
+    def _load_meta(self, meta):
+        self.step_index = int(meta["step_index"])
+        self.csr = DstCsr.from_sorted_async(self.ctx, self.t, self.n_src, self.n_dst,
+                                            self.csr.row_ptr, self.csr.plan)
+
+    def save(self, path) -> None:
+        """Checkpoint: the connection fields, destination activations and the
+        step counter that seeds regrowth."""
+        from .checkpoint import save_state
+        save_state(self, path)
+
+    def load(self, path) -> None:
+        from .checkpoint import load_state
+        load_state(self, path)
+
     def step(self, act_src: torch.Tensor) -> torch.Tensor:
         ctx = self.ctx
         compact(ctx, self.n, _abi.KEEP_ABS_GE, self.w,
@@ -437,6 +472,18 @@ class SwiftTDLearner:
 
     def field(self, name: str) -> torch.Tensor:
         return self.state[TD_FIELDS.index(name), :self.n]
+
+    def _state_tensors(self):
+        return {"state": self.state, "globals": self.globals, "v": self.v}
+
+    def save(self, path) -> None:
+        """Checkpoint: the ten connection fields, the globals record, V."""
+        from .checkpoint import save_state
+        save_state(self, path)
+
+    def load(self, path) -> None:
+        from .checkpoint import load_state
+        load_state(self, path)
 
     def fields(self) -> torch.Tensor:
         return self.state[:, :self.n]
@@ -700,6 +747,30 @@ class PredictiveCodingNet:
     @property
     def hidden(self):
         return self.begin[1], self.begin[-2]
+
+    def _state_tensors(self):
+        t = {"x": self.x, "act": self.act, "err": self.err, "bu": self.bu}
+        if self.layout == "chunked":
+            for l, rows in enumerate(self.fwd):
+                t[f"w_fwd{l}"] = rows.weight
+            for l, rows in self.bwd.items():
+                t[f"w_bwd{l}"] = rows.weight
+        else:
+            for l, w in enumerate(self.w):
+                t[f"w{l}"] = w
+            for l, sm in self.sm.items():
+                t[f"w_src_major{l}"] = sm.weight
+        return t
+
+    def save(self, path) -> None:
+        """Checkpoint: value nodes, activations, errors, bottom-up sums and
+        every weight copy (both orders) in this network's layout."""
+        from .checkpoint import save_state
+        save_state(self, path)
+
+    def load(self, path) -> None:
+        from .checkpoint import load_state
+        load_state(self, path)
 
     def clamp(self, inputs: torch.Tensor, targets: torch.Tensor) -> None:
         """Clamps the input and output value nodes (ipc_multilayer.cpp:299-304)

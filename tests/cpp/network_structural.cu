@@ -2,14 +2,18 @@
 // oracle/structural_policies.hpp on the device Network (Topological), the
 // same network and inputs as the reference run that made the fixture.
 // Usage: network_structural <variant 0|1> <n_in> <h1> <h2> <seed> <steps> <dir>
+//        [resume_at]
 // Reads <dir>/inputs.bin (steps x n_in floats); writes outputs.bin and the
 // final connections (from, to, dead, src_level, w) and units (level, act).
+// With resume_at, the network is saved before that step and the run goes on
+// in a newly built network loaded from the checkpoint.
 #include <plastix/plastix.hpp>
 
 #include "../../oracle/structural_policies.hpp"
 
 #include <cstdio>
 #include <cstdlib>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -23,20 +27,30 @@ template <class T> void put(const std::string &dir, const char *name, const std:
 }
 
 template <class Tr> int run(uint32_t n_in, uint32_t h1, uint32_t h2, uint32_t seed, int steps,
-                            const std::string &dir) {
+                            const std::string &dir, int resume_at) {
   std::vector<float> x((size_t)steps * n_in);
   FILE *f = std::fopen((dir + "/inputs.bin").c_str(), "rb");
   if (!f || std::fread(x.data(), 4, x.size(), f) != x.size()) return 2;
   std::fclose(f);
-  plastix::Network<Tr> N(n_in,
-                         plastix::FullyConnected{h1, plastix::RandomUniformWeight{seed, -0.3f, 0.3f}},
-                         plastix::FullyConnected{h2, plastix::RandomUniformWeight{seed + 1, -0.3f, 0.3f}});
+  auto make = [&] {
+    return std::make_unique<plastix::Network<Tr>>(
+        n_in, plastix::FullyConnected{h1, plastix::RandomUniformWeight{seed, -0.3f, 0.3f}},
+        plastix::FullyConnected{h2, plastix::RandomUniformWeight{seed + 1, -0.3f, 0.3f}});
+  };
+  auto net = make();
   std::vector<float> outs;
   for (int s = 0; s < steps; ++s) {
-    N.DoStep(std::span<const float>(x.data() + (size_t)s * n_in, n_in));
-    auto o = N.GetOutput();
+    if (s == resume_at) {
+      // checkpoint, then continue in a freshly built network from the file
+      net->Save(dir + "/ckpt.bin");
+      net = make();
+      net->Load(dir + "/ckpt.bin");
+    }
+    net->DoStep(std::span<const float>(x.data() + (size_t)s * n_in, n_in));
+    auto o = net->GetOutput();
     outs.insert(outs.end(), o.begin(), o.end());
   }
+  auto &N = *net;
   auto &CA = N.GetConnAlloc();
   auto &UA = N.GetUnitAlloc();
   const size_t m = CA.Size(), n = UA.Size();
@@ -69,14 +83,16 @@ template <class Tr> int run(uint32_t n_in, uint32_t h1, uint32_t h2, uint32_t se
 }  // namespace
 
 int main(int argc, char **argv) {
-  if (argc != 8) return 1;
+  if (argc != 8 && argc != 9) return 1;
+  const int resume_at = argc == 9 ? std::atoi(argv[8]) : -1;
   const int variant = std::atoi(argv[1]);
   const uint32_t n_in = std::atoi(argv[2]), h1 = std::atoi(argv[3]), h2 = std::atoi(argv[4]);
   const uint32_t seed = std::atoi(argv[5]);
   const int steps = std::atoi(argv[6]);
   try {
-    return variant == 0 ? run<structural_test::SmallTraits>(n_in, h1, h2, seed, steps, argv[7])
-                        : run<structural_test::MediumTraits>(n_in, h1, h2, seed, steps, argv[7]);
+    return variant == 0
+               ? run<structural_test::SmallTraits>(n_in, h1, h2, seed, steps, argv[7], resume_at)
+               : run<structural_test::MediumTraits>(n_in, h1, h2, seed, steps, argv[7], resume_at);
   } catch (const std::exception &e) {
     std::fprintf(stderr, "%s\n", e.what());
     return 4;

@@ -97,13 +97,14 @@ def test_device_network_swifttd_matches_reference(tmp_path):
     np.testing.assert_allclose(v["b"], z["fields"][9], rtol=1e-5, atol=1e-6)
 
 
-def _run_structural(tmp_path, name):
+def _run_structural(tmp_path, name, resume_at=None):
     z = np.load(GOLDEN / "structural_net.npz")
     variant, n_in, h1, h2, seed, steps = (int(v) for v in z[f"{name}_params"])
     np.ascontiguousarray(z[f"{name}_inputs"], np.float32).tofile(tmp_path / "inputs.bin")
     exe = compile_prog("network_structural", tmp_path)
-    r = subprocess.run([str(exe), str(variant), str(n_in), str(h1), str(h2), str(seed),
-                        str(steps), str(tmp_path)], capture_output=True, text=True, timeout=600)
+    args = [str(exe), str(variant), str(n_in), str(h1), str(h2), str(seed), str(steps),
+            str(tmp_path)] + ([] if resume_at is None else [str(resume_at)])
+    r = subprocess.run(args, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr
     types = {"outputs": np.float32, "from": np.uint32, "to": np.uint32, "dead": np.uint8,
              "src_level": np.uint16, "w": np.float32, "level": np.uint16, "act": np.float32}
@@ -112,10 +113,13 @@ def _run_structural(tmp_path, name):
 
 
 @pytest.mark.gpu
-def test_device_network_structural_small_matches_reference(tmp_path):
+@pytest.mark.parametrize("resume_at", [None, 2, 4])
+def test_device_network_structural_small_matches_reference(tmp_path, resume_at):
     """Two-way proposals (into input units, cycles), a unit pruned at step 2,
-    weights pruned below 0.02: five steps, every array bit for bit."""
-    z, got = _run_structural(tmp_path, "small")
+    weights pruned below 0.02: five steps, every array bit for bit -- also
+    when the run is checkpointed before step `resume_at` and resumed in a
+    newly built network (Save / Load)."""
+    z, got = _run_structural(tmp_path, "small", resume_at)
     for k, v in got.items():
         want = z[f"small_{k}"].reshape(-1)
         assert v.size == want.size, k
@@ -123,11 +127,13 @@ def test_device_network_structural_small_matches_reference(tmp_path):
 
 
 @pytest.mark.gpu
-def test_device_network_structural_medium_matches_reference(tmp_path):
+@pytest.mark.parametrize("resume_at", [None, 1])
+def test_device_network_structural_medium_matches_reference(tmp_path, resume_at):
     """32 -> 200 -> 50 with forward proposals over ~60k unit pairs per step
-    (the parallel enumeration runs over many chunks): digests of every array."""
+    (the parallel enumeration runs over many chunks): digests of every array,
+    straight through and resumed from a checkpoint."""
     import hashlib
-    z, got = _run_structural(tmp_path, "medium")
+    z, got = _run_structural(tmp_path, "medium", resume_at)
     for k, v in got.items():
         assert v.size == int(z[f"medium_{k}_size"]), k
         assert hashlib.sha256(v.tobytes()).hexdigest() == str(z[f"medium_{k}_sha256"]), k
