@@ -719,33 +719,71 @@ def bench_ipc(args):
 def bench_structural(args):
     """C3: 2^23 sources, 2^23 destinations, 2^24 connections dst-sorted,
     w N(0, 0.1^2), u8 age; prune |w| < 0.02 by compaction, regrow the same
-    number, radix-sort by destination, forward sweep."""
+    number, radix-sort by destination, forward sweep. Under torchrun each rank
+    holds its own destination shard of that size (weak scaling): compaction,
+    regrowth (rank-keyed seed) and the re-sort are shard-local, so no
+    collective touches the step; the barrier and the max over ranks only
+    bracket the timing."""
     import torch
+    import torch.distributed as dist
 
     from plastix_b200.runtime import Context, StructuralLayer
 
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     n_src = n_dst = 1 << 23
     n = 1 << 24
-    torch.cuda.set_device(0)
-    ctx = Context(0)
-    g = torch.Generator(device="cuda").manual_seed(args.seed)
-    src = torch.randint(0, n_src, (n,), generator=g, device="cuda")
-    dst = torch.randint(0, n_dst, (n,), generator=g, device="cuda")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    ctx = Context(local)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 7919 * rank)
+    src = torch.randint(0, n_src, (n,), generator=g, device=dev)
+    dst = torch.randint(0, n_dst, (n,), generator=g, device=dev)
     dst, order = torch.sort(dst, stable=True)
     f = src[order].to(torch.int32)
     t = (dst + n_src).to(torch.int32)
-    w = torch.randn(n, generator=g, device="cuda") * 0.1
-    age = torch.randint(0, 256, (n,), generator=g, device="cuda").to(torch.uint8)
-    act = torch.rand(n_src, generator=g, device="cuda")
+    w = torch.randn(n, generator=g, device=dev) * 0.1
+    age = torch.randint(0, 256, (n,), generator=g, device=dev).to(torch.uint8)
+    act = torch.rand(n_src, generator=g, device=dev)
     del src, dst, order
-    layer = StructuralLayer(ctx, n_src, n_dst, f, t, w, age, threshold=0.02, seed=11)
+    layer = StructuralLayer(ctx, n_src, n_dst, f, t, w, age, threshold=0.02, seed=11 + rank)
     steps = max(1, min(args.steps, 50))
-    ms, clocks = _timed_loop(ctx.stream, lambda i: layer.step(act), steps, args.warmup)
+    for _ in range(args.warmup):
+        layer.step(act)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    t0, t1 = _events(2)
+    t0.record(ctx.stream)
+    for _ in range(steps):
+        layer.step(act)
+    t1.record(ctx.stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tm = torch.tensor([ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm[0])
+        dist.barrier()
+        dist.destroy_process_group()
     ctx.sync()
-    _line(args, "structural", n * steps / (ms / 1e3), "connections/s", ms / steps,
-          {"workload": "structural plasticity step", "n_src": n_src, "n_dst": n_dst,
-           "connections": n, "prune": "|w| < 0.02", "steps": steps},
-          None, None, None, clocks, None)
+    if rank != 0:
+        return 0
+    _line(args, "structural", world * n * steps / (ms / 1e3), "connections/s", ms / steps,
+          {"workload": "structural plasticity step", "n_src": n_src, "n_dst_per_gpu": n_dst,
+           "connections_per_gpu": n, "prune": "|w| < 0.02", "steps": steps,
+           "parallelism": f"destination shards x{world}, shard-local (no collective)"},
+          None, None, None, clocks, None, extra={"n_gpus": world})
+    return 0
 
 
 def bench_ceiling(args):
@@ -853,7 +891,7 @@ def bench_levels(args):
 
 
 def run_other(args):
-    if args.gpus != 1 and args.workload != "ipc":
+    if args.gpus != 1 and args.workload not in ("ipc", "structural"):
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
     return {"swifttd": bench_swifttd, "ipc": bench_ipc, "structural": bench_structural,
             "ceiling": bench_ceiling, "levels": bench_levels}[args.workload](args) or 0

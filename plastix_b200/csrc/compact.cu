@@ -145,39 +145,52 @@ __global__ void __launch_bounds__(kCT) k_compact(CompactArgs a) {
     if (lane == 31) s_total = incl;
   }
   __syncthreads();
-  if (tid == 0) {
+  if (warp == 0) {
+    // Warp-cooperative lookback: lane l reads predecessor p - l, so 32 status
+    // words are in flight per step; values are consumed in order up to the
+    // first inclusive prefix, or up to the first predecessor not yet
+    // published (read again in the next step).
     const uint64_t agg = s_total;
     uint64_t prefix = 0;
     bool ok = true;
     if (tile == 0) {
-      st_release_u64(&a.status[0], kFlagP | agg);
+      if (lane == 0) st_release_u64(&a.status[0], kFlagP | agg);
     } else {
-      st_release_u64(&a.status[tile], kFlagA | agg);
+      if (lane == 0) st_release_u64(&a.status[tile], kFlagA | agg);
       int64_t p = (int64_t)tile - 1;
-      const uint64_t t0 = global_timer_ns();
+      const uint64_t t0 = __shfl_sync(0xffffffffu, global_timer_ns(), 0);
       uint32_t spin = 0;
-      while (p >= 0) {
-        const uint64_t s = ld_acquire_u64(&a.status[p]);
-        if (s & kFlagP) {
-          prefix += s & kValMask;
-          break;
-        }
-        if (s & kFlagA) {
-          prefix += s & kValMask;
-          --p;
-          continue;
-        }
-        if ((++spin & 255u) == 0 && global_timer_ns() - t0 > a.timeout_ns) {
-          ok = false;
-          break;
+      for (;;) {
+        const int64_t q = p - (int64_t)lane;
+        const uint64_t sv = q >= 0 ? ld_acquire_u64(&a.status[q]) : 0ull;
+        const uint32_t m_p = __ballot_sync(0xffffffffu, (sv & kFlagP) != 0);
+        const uint32_t m_v = __ballot_sync(0xffffffffu, (sv & (kFlagA | kFlagP)) != 0);
+        const int first_inv = ~m_v ? __ffs(~m_v) - 1 : 32;
+        const int first_p = m_p ? __ffs(m_p) - 1 : 32;
+        const bool done = first_p < first_inv;
+        const int take = done ? first_p + 1 : first_inv;
+        uint64_t v = (int)lane < take ? (sv & kValMask) : 0ull;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        prefix += v;
+        if (done) break;
+        p -= take;
+        if (take == 0 && (++spin & 255u) == 0) {
+          const uint64_t now = __shfl_sync(0xffffffffu, global_timer_ns(), 0);
+          if (now - t0 > a.timeout_ns) {
+            ok = false;
+            break;
+          }
         }
       }
-      st_release_u64(&a.status[tile], kFlagP | (prefix + agg));
+      if (lane == 0) st_release_u64(&a.status[tile], kFlagP | (prefix + agg));
     }
-    if (!ok) record_status(a.dstatus, kStatusTimeout);
-    s_prefix = prefix;
-    const uint64_t n_tiles = (a.n + kCTile - 1) / kCTile;
-    if (tile == n_tiles - 1 || a.n == 0) *a.count_out = prefix + agg;
+    if (lane == 0) {
+      if (!ok) record_status(a.dstatus, kStatusTimeout);
+      s_prefix = prefix;
+      const uint64_t n_tiles = (a.n + kCTile - 1) / kCTile;
+      if (tile == n_tiles - 1 || a.n == 0) *a.count_out = prefix + agg;
+    }
   }
   __syncthreads();
   const uint64_t prefix = s_prefix;

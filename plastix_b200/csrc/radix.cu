@@ -93,9 +93,17 @@ struct RadixPassArgs {
   uint32_t* ticket;             // zeroed
   int32_t* dstatus;
   uint64_t timeout_ns;
+  uint32_t ahead;  // tiles resident at once: the tile this far ahead is prefetched
 };
 
-__global__ void __launch_bounds__(kRT, 3) k_radix_pass(RadixPassArgs a) {
+// Asks L2 for the 16-byte-aligned part of [p, p + bytes).
+__device__ __forceinline__ void prefetch_range(const void* p, uint64_t bytes) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(p);
+  const uintptr_t lo = (a0 + 15) & ~uintptr_t(15), hi = (a0 + bytes) & ~uintptr_t(15);
+  if (hi > lo) prefetch_l2_bulk(reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo));
+}
+
+__global__ void __launch_bounds__(kRT, 4) k_radix_pass(RadixPassArgs a) {
   __shared__ uint32_t s_keys[kRTile];
   __shared__ uint32_t s_vals[kRTile];
   __shared__ uint32_t s_wcnt[kRWarps][256];  // per-warp digit counts, then warp bases
@@ -110,6 +118,16 @@ __global__ void __launch_bounds__(kRT, 3) k_radix_pass(RadixPassArgs a) {
   const uint64_t tile = s_tile;
   const uint64_t base = tile * kRTile;
   const uint32_t lt = (1u << lane) - 1u;
+  // The tile one resident wave ahead starts after this one: bring its keys
+  // and values into L2 now so its loads hit there.
+  if (tid < 2) {
+    const uint64_t b2 = (tile + a.ahead) * kRTile;
+    if (b2 < a.n) {
+      const uint64_t cnt = min((uint64_t)kRTile, a.n - b2);
+      if (tid == 0) prefetch_range(a.keys_in + b2, cnt * 4);
+      else if (a.vals_in) prefetch_range(a.vals_in + b2, cnt * 4);
+    }
+  }
 
   // Warp w owns tile elements [w * 512, (w + 1) * 512): item j of lane l is
   // element w * 512 + j * 32 + l, so element order is (warp, item, lane) and
@@ -302,6 +320,7 @@ extern "C" int plx_radix_sort_u32(plx_ctx* ctx, uint64_t n, const uint32_t* keys
     a.ticket = s.ticket + p;
     a.dstatus = ctx->d_status;
     a.timeout_ns = ctx->timeout_ns;
+    a.ahead = 4u * (uint32_t)ctx->num_sms;
     k_radix_pass<<<(unsigned)tiles, kRT, 0, ctx->stream>>>(a);
     PLX_LAUNCH_CHECK("k_radix_pass");
     kin = kout;
