@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kRT, 4) k_radix_pass(RadixPassArgs a) {
   __shared__ uint32_t s_run[256];
   __shared__ uint32_t s_local[256];
   __shared__ uint32_t s_gbase[256];
+  __shared__ uint32_t s_wsum[kRWarps];
   __shared__ uint32_t s_tile;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   if (tid == 0) s_tile = atomicAdd(a.ticket, 1u);
@@ -206,16 +207,20 @@ __global__ void __launch_bounds__(kRT, 4) k_radix_pass(RadixPassArgs a) {
   }
   if (!ok) record_status(a.dstatus, kStatusTimeout);
   s_gbase[tid] = a.digit_start[tid] + prefix;
-  // local exclusive scan of the tile's digit counts
-  s_local[tid] = cnt;
-  __syncthreads();
-  for (uint32_t o = 1; o < 256; o <<= 1) {
-    const uint32_t t = tid >= o ? s_local[tid - o] : 0u;
-    __syncthreads();
-    s_local[tid] += t;
-    __syncthreads();
+  // local exclusive scan of the tile's digit counts: warp scans by shuffle,
+  // then the eight warp totals
+  uint32_t incl = cnt;
+#pragma unroll
+  for (uint32_t o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
-  s_local[tid] -= cnt;
+  if (lane == 31) s_wsum[warp] = incl;
+  __syncthreads();
+  uint32_t wbase = 0;
+#pragma unroll
+  for (int w = 0; w < kRWarps; ++w) wbase += (uint32_t)w < warp ? s_wsum[w] : 0u;
+  s_local[tid] = wbase + incl - cnt;
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < kRItems; ++j) {
