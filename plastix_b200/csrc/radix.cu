@@ -16,7 +16,9 @@
 //     shared digit counters (no block barrier per item), keeping the element
 //     order (stable); per-digit warp bases come from one scan over the warps;
 //   * the tile publishes its 256 digit counts, each thread looks back over
-//     the predecessors of its digit (bounded spin) and publishes the prefix;
+//     the predecessors of its digit, eight status words per step (relaxed
+//     loads: a status word carries its own flag and value; bounded spin), and
+//     publishes the prefix;
 //   * keys are re-ordered by digit in shared memory and written out in
 //     digit runs (coalesced).
 #include "common.cuh"
@@ -30,13 +32,16 @@ constexpr int kRWarps = kRT / 32;
 constexpr uint32_t kRFlagA = 1u << 30;
 constexpr uint32_t kRFlagP = 2u << 30;
 constexpr uint32_t kRValMask = (1u << 30) - 1;
+constexpr int kRLook = 8;  // most predecessor status words loaded per look-back step
 
-__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Status words carry their flag and value in one 32-bit word and publish
+// nothing else, so relaxed (non-fencing) accesses suffice.
+__device__ __forceinline__ void st_status_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_status_u32(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -181,29 +186,41 @@ __global__ void __launch_bounds__(kRT, 4) k_radix_pass(RadixPassArgs a) {
   bool ok = true;
   uint32_t prefix = 0;
   if (tile == 0) {
-    st_release_u32(&st[tid], kRFlagP | cnt);
+    st_status_u32(&st[tid], kRFlagP | cnt);
   } else {
-    st_release_u32(&st[tid], kRFlagA | cnt);
+    st_status_u32(&st[tid], kRFlagA | cnt);
+    // Look back kRLook predecessors per step (independent loads in flight),
+    // consuming them in order: aggregates add up until the first
+    // inclusive prefix; a predecessor not yet published is read again.
     int64_t p = (int64_t)tile - 1;
     const uint64_t t0 = global_timer_ns();
     uint32_t spin = 0;
-    while (p >= 0) {
-      const uint32_t s = ld_acquire_u32(a.status + (uint64_t)p * 256 + tid);
-      if (s & kRFlagP) {
-        prefix += s & kRValMask;
-        break;
+    bool done = false;
+    while (!done && p >= 0) {
+      uint32_t sv[kRLook];
+#pragma unroll
+      for (int i = 0; i < kRLook; ++i)
+        sv[i] = p - i >= 0 ? ld_status_u32(a.status + (uint64_t)(p - i) * 256 + tid) : 0u;
+      int used = 0;
+#pragma unroll
+      for (int i = 0; i < kRLook; ++i) {
+        if (done || used != i) continue;
+        if (sv[i] & kRFlagP) {
+          prefix += sv[i] & kRValMask;
+          done = true;
+        } else if (sv[i] & kRFlagA) {
+          prefix += sv[i] & kRValMask;
+          ++used;
+        }
       }
-      if (s & kRFlagA) {
-        prefix += s & kRValMask;
-        --p;
-        continue;
-      }
-      if ((++spin & 255u) == 0 && global_timer_ns() - t0 > a.timeout_ns) {
+      if (done) break;
+      p -= used;
+      if (used == 0 && (++spin & 255u) == 0 && global_timer_ns() - t0 > a.timeout_ns) {
         ok = false;
         break;
       }
     }
-    st_release_u32(&st[tid], kRFlagP | (prefix + cnt));
+    st_status_u32(&st[tid], kRFlagP | (prefix + cnt));
   }
   if (!ok) record_status(a.dstatus, kStatusTimeout);
   s_gbase[tid] = a.digit_start[tid] + prefix;
