@@ -48,12 +48,14 @@ struct CompactArgs {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// A status word holds its flag and value together and publishes nothing else,
+// so relaxed (non-fencing) accesses suffice.
+__device__ __forceinline__ void st_status_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
+__device__ __forceinline__ uint64_t ld_status_u64(const uint64_t* p) {
   uint64_t v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -154,15 +156,15 @@ __global__ void __launch_bounds__(kCT) k_compact(CompactArgs a) {
     uint64_t prefix = 0;
     bool ok = true;
     if (tile == 0) {
-      if (lane == 0) st_release_u64(&a.status[0], kFlagP | agg);
+      if (lane == 0) st_status_u64(&a.status[0], kFlagP | agg);
     } else {
-      if (lane == 0) st_release_u64(&a.status[tile], kFlagA | agg);
+      if (lane == 0) st_status_u64(&a.status[tile], kFlagA | agg);
       int64_t p = (int64_t)tile - 1;
       const uint64_t t0 = __shfl_sync(0xffffffffu, global_timer_ns(), 0);
       uint32_t spin = 0;
       for (;;) {
         const int64_t q = p - (int64_t)lane;
-        const uint64_t sv = q >= 0 ? ld_acquire_u64(&a.status[q]) : 0ull;
+        const uint64_t sv = q >= 0 ? ld_status_u64(&a.status[q]) : 0ull;
         const uint32_t m_p = __ballot_sync(0xffffffffu, (sv & kFlagP) != 0);
         const uint32_t m_v = __ballot_sync(0xffffffffu, (sv & (kFlagA | kFlagP)) != 0);
         const int first_inv = ~m_v ? __ffs(~m_v) - 1 : 32;
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(kCT) k_compact(CompactArgs a) {
           }
         }
       }
-      if (lane == 0) st_release_u64(&a.status[tile], kFlagP | (prefix + agg));
+      if (lane == 0) st_status_u64(&a.status[tile], kFlagP | (prefix + agg));
     }
     if (lane == 0) {
       if (!ok) record_status(a.dstatus, kStatusTimeout);
