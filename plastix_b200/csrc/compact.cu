@@ -72,6 +72,29 @@ __device__ __forceinline__ bool keep_pred(const CompactArgs& a, uint64_t e) {
   }
 }
 
+__device__ __forceinline__ uint64_t load_elem(const FieldDesc& f, uint64_t from) {
+  switch (f.bytes) {
+    case 1: return static_cast<const uint8_t*>(f.src)[from];
+    case 2: return static_cast<const uint16_t*>(f.src)[from];
+    case 4: return static_cast<const uint32_t*>(f.src)[from];
+    default: return static_cast<const uint64_t*>(f.src)[from];
+  }
+}
+
+__device__ __forceinline__ void store_elem(const FieldDesc& f, uint64_t to, uint64_t v) {
+  switch (f.bytes) {
+    case 1: {
+      uint8_t b = (uint8_t)v;
+      if (f.flags & PLX_FIELD_INC_SAT_U8) b = b == 255 ? 255 : (uint8_t)(b + 1);
+      static_cast<uint8_t*>(f.dst)[to] = b;
+      break;
+    }
+    case 2: static_cast<uint16_t*>(f.dst)[to] = (uint16_t)v; break;
+    case 4: static_cast<uint32_t*>(f.dst)[to] = (uint32_t)v; break;
+    default: static_cast<uint64_t*>(f.dst)[to] = v; break;
+  }
+}
+
 __device__ __forceinline__ void copy_elem(const FieldDesc& f, uint64_t from,
                                           uint64_t to) {
   switch (f.bytes) {
@@ -202,7 +225,16 @@ __global__ void __launch_bounds__(kCT) k_compact(CompactArgs a) {
     if (!((masks[j] >> lane) & 1u)) continue;
     const uint64_t e = base + (uint64_t)j * kCT + tid;
     const uint64_t pos = prefix + s_cnt[j * (kCT / 32) + warp] + __popc(masks[j] & lt);
-    for (uint32_t f = 0; f < a.n_fields; ++f) copy_elem(a.f[f], e, pos);
+    // fields four at a time: the group's loads are issued before its stores
+    for (uint32_t f0 = 0; f0 < a.n_fields; f0 += 4) {
+      uint64_t v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (f0 + q < a.n_fields) v[q] = load_elem(a.f[f0 + q], e);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (f0 + q < a.n_fields) store_elem(a.f[f0 + q], pos, v[q]);
+    }
     if (a.perm_out) a.perm_out[pos] = (uint32_t)e;
   }
 }
