@@ -373,13 +373,14 @@ class StructuralLayer:
         self.w, self.age = mk(weight, torch.float32), mk(age, torch.uint8)
         self.f2, self.t2 = torch.empty_like(self.f), torch.empty_like(self.t)
         self.w2, self.age2 = torch.empty_like(self.w), torch.empty_like(self.age)
-        self.keys = torch.empty_like(self.t)
         self.keys_sorted = torch.empty_like(self.t)
         self.perm = torch.empty_like(self.t)
         self.count = torch.zeros(1, dtype=torch.int64, device=dev)
         self.scratch = Scratch(dev)
         self.act_dst = torch.zeros(n_dst, dtype=torch.float32, device=dev)
-        self.key_bits = max(1, (n_dst - 1).bit_length())
+        # ToId itself is the sort key (the same stable order as ToId - n_src),
+        # on the bits its largest value needs
+        self.key_bits = max(1, (n_src + n_dst - 1).bit_length())
         self.step_index = 0
         self.csr = DstCsr.from_sorted_async(ctx, self.t, n_src, n_dst)
 
@@ -414,8 +415,7 @@ class StructuralLayer:
         regrow(ctx, self.count, self.f2, self.t2, self.w2, self.age2, src_base=0,
                n_src=self.n_src, dst_base=self.n_src, n_dst=self.n_dst, seed=self.seed,
                step_base=self.step_index * self.n)
-        torch.sub(self.t2, self.n_src, out=self.keys)
-        radix_sort_u32(ctx, self.keys, self.keys_sorted, self.perm, 0, self.key_bits,
+        radix_sort_u32(ctx, self.t2, self.keys_sorted, self.perm, 0, self.key_bits,
                        scratch=self.scratch)
         gather(ctx, self.perm, [(self.f2, self.f), (self.t2, self.t), (self.w2, self.w),
                                 (self.age2, self.age)])
