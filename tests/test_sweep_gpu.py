@@ -211,3 +211,37 @@ def test_full_size_sweep_matches_oracle(ctx, orc):
     np.testing.assert_array_equal(host(out), aa[n_src:])
     np.testing.assert_array_equal(host(layer.weight), ww)
     np.testing.assert_array_equal(host(layer.trace), ee)
+
+
+@pytest.mark.parametrize("case", ["dense", "gaps", "outside", "tail", "big"])
+def test_row_ptr_equals_searchsorted(ctx, case):
+    """plx_csr_row_ptr: row_ptr[r] = first connection whose ToId >= row_base + r
+    (keys below the range count as before row 0, above it as after the last
+    row), row_ptr[n_rows] = n_edges."""
+    from ctypes import c_void_p
+    from plastix_b200._abi import call
+    rng = np.random.default_rng(hash(case) % 1000)
+    row_base = 1000
+    if case == "dense":
+        n_rows, keys = 50_000, rng.integers(0, 50_000, 200_001)
+    elif case == "gaps":  # spans wider than one block's staging window
+        n_rows = 10_000_000
+        keys = np.concatenate([rng.integers(0, 10, 3000), rng.integers(0, n_rows, 5000),
+                               rng.integers(n_rows - 10, n_rows, 3000)])
+    elif case == "outside":
+        n_rows = 3000
+        keys = rng.integers(-800, n_rows + 800, 100_003)
+    elif case == "tail":
+        n_rows, keys = 7, rng.integers(0, 7, 1_026)
+    else:
+        n_rows, keys = 1 << 23, rng.integers(0, 1 << 23, 1 << 24)
+    to_id = np.sort(keys.astype(np.int64) + row_base).astype(np.uint32)
+    t = torch.from_numpy(to_id.view(np.int32)).cuda()
+    rp = torch.full((n_rows + 1,), -1, dtype=torch.int32, device="cuda")
+    call("plx_csr_row_ptr", ctx.handle, c_void_p(t.data_ptr()), to_id.size, row_base, n_rows,
+         c_void_p(rp.data_ptr()))
+    ctx.sync()
+    want = np.searchsorted(to_id.astype(np.int64), np.arange(n_rows + 1) + row_base,
+                           side="left")
+    want[-1] = to_id.size
+    np.testing.assert_array_equal(rp.cpu().numpy().astype(np.int64), want)
