@@ -98,6 +98,7 @@ struct SweepArgs {
   uint32_t n_peers;
   uint32_t peer_offset;
   float* peer_out[PLX_MAX_PEERS];
+  uint32_t no_prefetch;  // skip the next-tile L2 prefetch (large source arrays)
 };
 
 enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3, kUpdHebbT = 4 };
@@ -1029,7 +1030,7 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32, C::kMinBlocks)
   uint32_t t_cur = 0;
   if (lane == 0) {
     t_cur = atomicAdd(a.queue, 1u);
-    if (t_cur < n_tiles) prefetch_tile(t_cur);
+    if (t_cur < n_tiles && !a.no_prefetch) prefetch_tile(t_cur);
   }
   t_cur = __shfl_sync(kFull, t_cur, 0);
   for (;;) {
@@ -1038,7 +1039,7 @@ __global__ void __launch_bounds__(C::kWarpsPerCta * 32, C::kMinBlocks)
     uint32_t t_nxt = 0;
     if (lane == 0) {
       t_nxt = atomicAdd(a.queue, 1u);
-      if (t_nxt < n_tiles) prefetch_tile(t_nxt);
+      if (t_nxt < n_tiles && !a.no_prefetch) prefetch_tile(t_nxt);
     }
     t_cur = __shfl_sync(kFull, t_nxt, 0);
     const uint32_t b0 = t * kTileBlocks;
@@ -1211,6 +1212,12 @@ int launch_wtile(plx_ctx* ctx, const SweepArgs& args) {
   PLX_TRY_CUDA(cudaMemsetAsync(ctx->d_queue, 0, sizeof(uint32_t), ctx->stream));
   SweepArgs wa = args;
   wa.queue = ctx->d_queue;
+  // The next-tile L2 prefetch keeps upcoming streams resident in L2; with a
+  // source array of 2^22 or more units (16 MB) it evicts the gathered
+  // activations instead (measured at 64M connections: 2^23 sources
+  // 0.667 ms with it, 0.527 ms without; 2^20 sources 0.474 ms with, 0.496
+  // without; equal at 2^22).
+  wa.no_prefetch = args.act_src_len >= (1u << 22) ? 1u : 0u;
   kern<<<(unsigned)std::max<uint64_t>(grid, 1), C::kWarpsPerCta * 32, smem, ctx->stream>>>(wa);
   PLX_LAUNCH_CHECK("k_sweep_wtile");
   return PLX_OK;
