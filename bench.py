@@ -141,6 +141,19 @@ class ClockSampler:
                 "samples": len(self.samples), "source": "nvml"}
 
 
+def merge_clocks(per_rank):
+    """One clock record for several GPUs: the lowest median SM clock, every
+    reason any GPU reported, the sample counts added."""
+    got = [c for c in per_rank if c]
+    if not got:
+        return None
+    return {"sm_mhz": min(c["sm_mhz"] for c in got),
+            "sm_max_mhz": max(c["sm_max_mhz"] or 0 for c in got),
+            "reasons": sorted({r for c in got for r in c["reasons"]}),
+            "samples": sum(c["samples"] for c in got), "gpus": len(got),
+            "source": "nvml, every rank"}
+
+
 # ---------------------------------------------------------------------------
 def cpu_reference_sample(n_src, n_dst, n_edges, seed, budget_s, warmup=1, steps=None):
     """Times the reference implementation (oracle/_ref, all host threads, one
@@ -279,13 +292,24 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def align_ranks():
+        """Host barrier, then a device-side rendezvous on the timed stream, so
+        every rank's first timed kernel starts together (a rank that arrives
+        late cannot push its start-up delay into the others' timed region)."""
+        barrier_sync()
+        if p2p:
+            peer.barrier()
+        elif world > 1:
+            dist.all_reduce(torch.zeros(1, device=device))
+
     # ---- device-resident timing -------------------------------------------
     for _ in range(args.warmup):
         step()
-    barrier_sync()
-    sampler = ClockSampler(local) if rank == 0 else None
+    sampler = ClockSampler(local)  # every rank samples its own GPU
+    align_ranks()
     k0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     k1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    k2 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -300,15 +324,20 @@ def run_ours(args):
             peer.barrier()
         elif world > 1:
             dist.all_gather_into_tensor(gathered, layer.act_dst)
+        k2[i].record(stream)
     t1.record(stream)
     barrier_sync()
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop()
     ms = t0.elapsed_time(t1)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(k0, k1))
+    handoff_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(k1, k2))
     if world > 1:
-        t = torch.tensor([ms, kern_ms], device=device)
+        t = torch.tensor([ms, kern_ms, handoff_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, kern_ms = float(t[0]), float(t[1])
+        ms, kern_ms, handoff_ms = float(t[0]), float(t[1]), float(t[2])
+        every = [None] * world
+        dist.all_gather_object(every, clocks)
+        clocks = merge_clocks(every)
     ms_per_step = ms / args.steps
     value = world * n_edges * args.steps / (ms / 1e3)
 
@@ -316,9 +345,12 @@ def run_ours(args):
     # Every step copies its inputs from pinned host memory and reads its
     # destination activations back; the copies run on their own streams,
     # double-buffered, so step i+1's upload and step i's read-back overlap
-    # the sweeps (the device-side hand-off of each step is unchanged).
-    gen = torch.Generator().manual_seed(args.seed)
-    h_in = [torch.rand(n_src_total, generator=gen).pin_memory() for _ in range(2)]
+    # the sweeps (the device-side hand-off of each step is unchanged). With
+    # several GPUs each rank uploads only its own slice of the source vector
+    # and the slices are all-gathered on the devices (NCCL over NVLink).
+    n_in = n_src_total // world
+    gen = torch.Generator().manual_seed(args.seed + rank)
+    h_in = [torch.rand(n_in, generator=gen).pin_memory() for _ in range(2)]
     h_out = [torch.empty(n_dst, pin_memory=True) for _ in range(2)]
     dev_in = [torch.empty(n_src_total, device=device) for _ in range(2)]
     dev_out = [torch.empty(n_dst, device=device) for _ in range(2)]
@@ -335,7 +367,12 @@ def run_ours(args):
         b = i & 1
         up.wait_event(in_free[b])
         with torch.cuda.stream(up):
-            dev_in[b].copy_(h_in[b], non_blocking=True)
+            if world > 1:
+                mine = dev_in[b][rank * n_in:(rank + 1) * n_in]
+                mine.copy_(h_in[b], non_blocking=True)
+                dist.all_gather_into_tensor(dev_in[b], mine)
+            else:
+                dev_in[b].copy_(h_in[b], non_blocking=True)
         in_ready[b].record(up)
         stream.wait_event(in_ready[b])
         out = sweep(dev_in[b])
@@ -350,7 +387,7 @@ def run_ours(args):
 
     for i in range(args.warmup):
         e2e_step(i)
-    barrier_sync()
+    align_ranks()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -406,9 +443,10 @@ def run_ours(args):
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS hbm_gbs)",
                      "traffic": traffic_per_launch("sweep_hebbian_64M"),
                      "kernel_ms": kern_ms, "algorithmic_bytes_per_launch": algo_bytes},
+        "handoff_ms": handoff_ms if world > 1 else None,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT,
-                "h2d_bytes_per_step": 4 * n_src_total * world,
+                "h2d_bytes_per_step": 4 * n_in * world,
                 "d2h_bytes_per_step": 4 * n_dst * world},
         "clocks": clocks,
         "gpu_launches": args.steps * (2 if p2p else 1),
@@ -786,6 +824,25 @@ def bench_structural(args):
     return 0
 
 
+def _probe_lib():
+    """The measurement-only library of the ceiling workload (its kernels are
+    not part of the product library)."""
+    from ctypes import POINTER, c_float, c_int, c_uint32, c_uint64, c_void_p
+
+    from plastix_b200 import _abi, build
+
+    _abi.lib()  # the product library first: the probes use its contexts
+    lib = ctypes.CDLL(str(build.PROBE_LIB))
+    lib.plx_probe_gather.restype = c_int
+    lib.plx_probe_gather.argtypes = [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p,
+                                     POINTER(c_uint64)]
+    lib.plx_probe_sweep_nofold.restype = c_int
+    lib.plx_probe_sweep_nofold.argtypes = [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32,
+                                           c_void_p, c_void_p, c_float, c_float, c_void_p,
+                                           c_void_p]
+    return lib
+
+
 def bench_ceiling(args):
     """The sweep against the two pieces of its traffic no fold order removes:
     the same connections swept without the row folds (FromId/Weight/Trace
@@ -797,6 +854,7 @@ def bench_ceiling(args):
     from plastix_b200.runtime import Context, HebbianSweepLayer
 
     ctx = Context(0)
+    probe = _probe_lib()
     device = ctx.device
     n_src, n_dst, n = args.n_src, args.n_dst, args.n_edges
     from_id, to_id, w, act = workloads.sparse_layer_device(n_src, n_dst, n, args.seed, device)
@@ -806,13 +864,18 @@ def bench_ceiling(args):
     sink = torch.zeros(1, device=device)
     done = ctypes.c_uint64(0)
 
+    def probe_call(name, *a):
+        rc = getattr(probe, name)(*a)
+        if rc != 0:
+            raise _abi.PlxError(rc, name, _abi.lib().plx_last_error().decode())
+
     def nofold(i):
-        _abi.call("plx_probe_sweep_nofold", ctx.handle, n, from_id.data_ptr(), act.data_ptr(),
-                  n_src, w.data_ptr(), e.data_ptr(), 0.9, 1e-3, w2.data_ptr(), e2.data_ptr())
+        probe_call("plx_probe_sweep_nofold", ctx.handle, n, from_id.data_ptr(), act.data_ptr(),
+                   n_src, w.data_ptr(), e.data_ptr(), 0.9, 1e-3, w2.data_ptr(), e2.data_ptr())
 
     def gather(i):
-        _abi.call("plx_probe_gather", ctx.handle, act.data_ptr(), n_src, n, sink.data_ptr(),
-                  ctypes.byref(done))
+        probe_call("plx_probe_gather", ctx.handle, act.data_ptr(), n_src, n, sink.data_ptr(),
+                   ctypes.byref(done))
 
     out = {}
     for name, fn in (("sweep", lambda i: layer.step(act)), ("nofold", nofold), ("gather", gather)):

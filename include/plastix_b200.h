@@ -173,12 +173,16 @@ int plx_sweep_forward_hebbian(plx_ctx* ctx, const plx_csr* csr,
  * (the all-gather buffers of every GPU, this one's included, mapped with
  * plx_peer_open), so the all-gather of destination slices after a sweep
  * (the multi-GPU hand-off between layers) rides on the sweep's own stores
- * over NVLink. Follow it with plx_peer_barrier before reading the buffer. */
+ * over NVLink. Follow it with plx_peer_barrier before reading the buffer.
+ * peer_len is the length (floats) of every peer buffer: the call fails with
+ * PLX_ERR_ARG, before touching any device, unless
+ * peer_offset + csr->n_rows <= peer_len, so a wrong offset or shard size can
+ * never store past the end of another GPU's buffer. */
 int plx_sweep_forward_hebbian_gather(
     plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id, const uint8_t* dead,
     const float* act_src, uint32_t act_src_len, const float* w_in, float* w_out,
     const float* trace_in, float* trace_out, float decay, float rate, float* act_dst,
-    float* const* peer_out, uint32_t n_peers, uint32_t peer_offset);
+    float* const* peer_out, uint32_t n_peers, uint32_t peer_offset, uint32_t peer_len);
 
 /* Device memory another process can map: cudaMalloc'd and zeroed, its IPC
  * handle (PLX_IPC_HANDLE_BYTES bytes) written to ipc_handle. */
@@ -223,20 +227,6 @@ int plx_recompute_levels(plx_ctx* ctx, uint32_t n_units, uint32_t n_input, uint6
  * re-sort (:551-577). */
 int plx_src_levels(plx_ctx* ctx, uint64_t n_conns, const uint32_t* from_id,
                    const uint16_t* level, uint32_t n_units, uint16_t* src_level);
-
-/* Measurement kernels for the connection sweep's memory ceiling (no
- * reference counterpart; used by the benchmark only).
- * plx_probe_gather: about n_gathers random 4-byte loads from x (n_x a power
- * of two) with the sweep's L2 policy; the exact count is written to *done and
- * the loaded values are summed into *sink (device).
- * plx_probe_sweep_nofold: the sweep's per-connection traffic without the row
- * folds -- FromId, Weight, Trace loads, act[FromId] gathers, Weight and Trace
- * stores (n a multiple of 4, arrays 16-byte aligned). */
-int plx_probe_gather(plx_ctx* ctx, const float* x, uint32_t n_x, uint64_t n_gathers,
-                     float* sink, uint64_t* done);
-int plx_probe_sweep_nofold(plx_ctx* ctx, uint64_t n, const uint32_t* from_id, const float* act,
-                           uint32_t n_act, const float* w_in, const float* e_in, float decay,
-                           float rate, float* w_out, float* e_out);
 
 /* Update kinds for plx_sweep_update (per-connection, reads a per-row value). */
 #define PLX_UPDATE_GRADIENT 1 /* w -= rate * post[dst] * act[src]

@@ -5,7 +5,8 @@
   ``-ffp-contract=off`` (no fused multiply-add), like the reference's own
   ``-std=c++20 -O2`` build.
 * ``oracle/_ref/libplx_ref.so`` — the reference itself: its headers
-  compiled from the reference tree (``/root/reference/include``) together with
+  compiled from the reference tree (``$PLX_REFERENCE_ROOT/include``, by
+  default ``../reference`` beside this repository) together with
   ``oracle/ref_harness.cpp``, ``oracle/ref_mlp.cpp`` and ``oracle/ref_ipc.cpp``,
   which compile the reference's ``examples/swifttd/swifttd.cpp``,
   ``examples/mlp-xor/mlp_xor.cpp`` and ``examples/ipc-multilayer/ipc_multilayer.cpp``
@@ -26,7 +27,9 @@ import tempfile
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("PLX_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: PLX_REFERENCE_ROOT, else a `reference` directory
+# beside this repository's root.
+REF_ROOT = Path(os.environ.get("PLX_REFERENCE_ROOT", HERE.parents[1] / "reference"))
 ORACLE_SO = HERE / "libplx_oracle.so"
 REF_DIR = HERE / "_ref"
 REF_SO = REF_DIR / "libplx_ref.so"

@@ -109,7 +109,8 @@ _SIGNATURES = {
     "plx_sweep_forward_hebbian_gather": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p,
                                                  c_void_p, c_uint32, c_void_p, c_void_p,
                                                  c_void_p, c_void_p, c_float, c_float,
-                                                 c_void_p, c_void_p, c_uint32, c_uint32]),
+                                                 c_void_p, c_void_p, c_uint32, c_uint32,
+                                                 c_uint32]),
     "plx_peer_alloc": (c_int, [c_void_p, ctypes.c_size_t, POINTER(c_void_p), c_void_p]),
     "plx_peer_free": (c_int, [c_void_p, c_void_p]),
     "plx_peer_open": (c_int, [c_void_p, c_void_p, POINTER(c_void_p)]),
@@ -120,10 +121,6 @@ _SIGNATURES = {
     "plx_recompute_levels": (c_int, [c_void_p, c_uint32, c_uint32, c_uint64, c_void_p, c_void_p,
                                      c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
     "plx_src_levels": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32, c_void_p]),
-    "plx_probe_gather": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_void_p, c_void_p]),
-    "plx_probe_sweep_nofold": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_uint32,
-                                       c_void_p, c_void_p, ctypes.c_float, ctypes.c_float,
-                                       c_void_p, c_void_p]),
     "plx_sort_unique_u64_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_sort_unique_u64": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
                                     ctypes.c_size_t]),

@@ -19,6 +19,10 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OBJ = PKG / "_build"
 LIB = PKG / "libplastix_b200.so"
+# Measurement-only kernels (the benchmark's sweep-ceiling probes) live in a
+# library of their own so that the product library carries none of them.
+PROBE_SRC = PKG / "probe" / "probe.cu"
+PROBE_LIB = PKG / "libplastix_probe.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -61,7 +65,21 @@ def build(verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_probe(verbose)
     return LIB
+
+
+def build_probe(verbose: bool = False) -> Path:
+    """libplastix_probe.so: the sweep-ceiling measurement kernels, linked
+    against the product library (it uses its context and error reporting)."""
+    obj = _compile(PROBE_SRC, verbose)
+    if _stale(PROBE_LIB, [obj, LIB]):
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(PROBE_LIB), str(obj), f"-L{PKG}",
+               "-lplastix_b200", "-Xlinker", "-rpath=$ORIGIN", "-lcudart"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"probe link failed:\n{r.stdout}\n{r.stderr}")
+    return PROBE_LIB
 
 
 if __name__ == "__main__":

@@ -1185,16 +1185,6 @@ int launch_tiles(plx_ctx* ctx, const SweepArgs& args) {
   return PLX_OK;
 }
 
-// Tile configurations (S, NSTAGE, consumer warps). PLX_SWEEP_CFG selects one
-// for tuning; the default is entry 0.
-static int sweep_cfg() {
-  static int cfg = [] {
-    const char* e = getenv("PLX_SWEEP_CFG");
-    return e ? atoi(e) : 0;
-  }();
-  return cfg;
-}
-
 template <class C, int APPLY, bool UPD, bool DEAD>
 int launch_wtile(plx_ctx* ctx, const SweepArgs& args) {
   auto kern = k_sweep_wtile<C, APPLY, UPD, DEAD>;
@@ -1223,22 +1213,14 @@ int launch_wtile(plx_ctx* ctx, const SweepArgs& args) {
   return PLX_OK;
 }
 
-static int sweep_cfg();
+// The warp-tile configuration: 4 plan blocks per tile, 4 four-wide steps in
+// flight per lane, 8 warps per CTA (the fastest of the tile sizes, step
+// depths and CTA shapes measured on the 64M-connection sweep).
+using WTileDefault = WTileCfg<4, 4, 8>;
 
 template <int APPLY, bool UPD, bool DEAD>
-int launch_warp(plx_ctx* ctx, const SweepArgs& args, uint32_t max_row) {
-  (void)max_row;
-  switch (sweep_cfg()) {
-    case 1: return launch_wtile<WTileCfg<4, 6, 8>, APPLY, UPD, DEAD>(ctx, args);
-    case 2: return launch_wtile<WTileCfg<4, 8, 8>, APPLY, UPD, DEAD>(ctx, args);
-    case 3: return launch_wtile<WTileCfg<4, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
-    case 4: return launch_wtile<WTileCfg<8, 4, 8>, APPLY, UPD, DEAD>(ctx, args);
-    case 5: return launch_wtile<WTileCfg<2, 4, 8, 3>, APPLY, UPD, DEAD>(ctx, args);
-    case 6: return launch_wtile<WTileCfg<2, 3, 8, 3>, APPLY, UPD, DEAD>(ctx, args);
-    case 7: return launch_wtile<WTileCfg<1, 4, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
-    case 8: return launch_wtile<WTileCfg<1, 2, 8, 4>, APPLY, UPD, DEAD>(ctx, args);
-    default: return launch_wtile<WTileCfg<4, 4, 8>, APPLY, UPD, DEAD>(ctx, args);
-  }
+int launch_warp(plx_ctx* ctx, const SweepArgs& args) {
+  return launch_wtile<WTileDefault, APPLY, UPD, DEAD>(ctx, args);
 }
 
 template <bool FOLD, int APPLY, int UPD, bool TRACE, bool DEAD>
@@ -1266,25 +1248,16 @@ int launch_sweep(plx_ctx* ctx, const SweepArgs& args, const plx_csr* csr) {
   const bool all_short = !unknown && csr->n_wide == 0 && csr->n_long == 0;
   if (args.to_id && (all_short || unknown) &&
       (UPD == kUpdNone || UPD == kUpdHebbTrace)) {
-    if (int rc = launch_warp<APPLY, UPD == kUpdHebbTrace, DEAD>(ctx, args, csr->max_row))
+    if (int rc = launch_warp<APPLY, UPD == kUpdHebbTrace, DEAD>(ctx, args))
       return rc;
     if (all_short) return PLX_OK;
     // unknown counts: the tile kernel below runs only if the plan has wide rows
   }
   SweepArgs targs = args;
   if (!(args.to_id && unknown && (UPD == kUpdNone || UPD == kUpdHebbTrace))) targs.to_id = nullptr;
-  switch (sweep_cfg()) {
-    case 1:
-      return launch_tiles<SweepLayout<1024, 4, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
-    case 2:
-      return launch_tiles<SweepLayout<2048, 3, 8, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
-    case 3:
-      return launch_tiles<SweepLayout<512, 3, 2, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
-    case 4:
-      return launch_tiles<SweepLayout<512, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
-    default:
-      return launch_tiles<SweepLayout<1024, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE, DEAD>(ctx, targs);
-  }
+  // Tile kernel: 1024-connection tiles, 4 bulk-copy stages, 4 consumer warps.
+  return launch_tiles<SweepLayout<1024, 4, 4, FOLD, U, TRACE, DEAD>, FOLD, APPLY, UPD, TRACE,
+                      DEAD>(ctx, targs);
 }
 
 static int validate_csr(const plx_csr* csr) {
@@ -1512,12 +1485,18 @@ extern "C" int plx_sweep_forward_hebbian_gather(
     plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id, const uint8_t* dead,
     const float* act_src, uint32_t act_src_len, const float* w_in, float* w_out,
     const float* trace_in, float* trace_out, float decay, float rate, float* act_dst,
-    float* const* peer_out, uint32_t n_peers, uint32_t peer_offset) {
+    float* const* peer_out, uint32_t n_peers, uint32_t peer_offset, uint32_t peer_len) {
   PLX_CHECK_ARG(n_peers <= PLX_MAX_PEERS, "at most %d peers", PLX_MAX_PEERS);
   PLX_CHECK_ARG(n_peers == 0 || peer_out, "peer_out is required");
   for (uint32_t p = 0; p < n_peers; ++p) PLX_CHECK_ARG(peer_out[p], "peer_out[%u] is NULL", p);
   PLX_CHECK_ARG(ctx, "ctx is required");
   if (int rc = validate_csr(csr)) return rc;
+  // Every destination row r is stored to peer_out[p][peer_offset + r]: the
+  // whole slice must lie inside the peer buffers (checked before any device
+  // work, so a bad offset never reaches another GPU's memory).
+  PLX_CHECK_ARG(n_peers == 0 || (uint64_t)peer_offset + csr->n_rows <= peer_len,
+                "peer slice [%u, %llu) exceeds the peer buffers of %u floats", peer_offset,
+                (unsigned long long)peer_offset + csr->n_rows, peer_len);
   PLX_CHECK_ARG(act_dst, "act_dst is required");
   PLX_CHECK_ARG(csr->n_edges == 0 ||
                     (from_id && act_src && w_in && w_out && trace_in && trace_out),

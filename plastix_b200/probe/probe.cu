@@ -1,7 +1,19 @@
-// Measurement kernels for the memory ceiling of the connection sweep. They
-// are not part of any reference path: they time the two pieces of the sweep's
-// traffic that no fold order can remove, so that the sweep's own time can be
-// read against them.
+// Measurement kernels for the memory ceiling of the connection sweep, built
+// into their own library (libplastix_probe.so, loaded by the benchmark's
+// `ceiling` workload only). They are not part of any reference path: they
+// time the two pieces of the sweep's traffic that no fold order can remove,
+// so that the sweep's own time can be read against them.
+//
+//   int plx_probe_gather(plx_ctx* ctx, const float* x, uint32_t n_x,
+//                        uint64_t n_gathers, float* sink, uint64_t* done);
+//     about n_gathers random 4-byte loads from x (n_x a power of two) with
+//     the sweep's L2 policy; the exact count goes to *done (host) and the
+//     loaded values are summed into *sink (device).
+//   int plx_probe_sweep_nofold(plx_ctx* ctx, uint64_t n, const uint32_t* from_id,
+//                              const float* act, uint32_t n_act, const float* w_in,
+//                              const float* e_in, float decay, float rate,
+//                              float* w_out, float* e_out);
+//     n a multiple of 4, arrays 16-byte aligned.
 //   plx_probe_gather        random 4-byte gathers from an L2-resident array
 //                           (the act[FromId] loads), nothing else;
 //   plx_probe_sweep_nofold  the sweep's streams and gathers without the row

@@ -222,13 +222,18 @@ class HebbianSweepLayer:
 
     def step_gather(self, act_src: torch.Tensor, peer, offset: int) -> torch.Tensor:
         """``step`` whose destination values also land in every rank's
-        all-gather buffer (``peer``: sharding.PeerGather) at ``offset``, as
-        stores of the sweep itself; call ``peer.barrier()`` before reading."""
+        all-gather buffer of the next epoch (``peer``: sharding.PeerGather)
+        at ``offset``, as stores of the sweep itself; call ``peer.barrier()``
+        before reading."""
+        if offset < 0 or offset + self.n_dst > peer.n_total:
+            raise ValueError(f"slice [{offset}, {offset + self.n_dst}) does not fit the "
+                             f"hand-off buffers of {peer.n_total} floats")
         c, o = self._cur, 1 - self._cur
         call("plx_sweep_forward_hebbian_gather", self.ctx.handle, byref(self.csr.struct),
              _ptr(self.from_id), _ptr(self.dead), _ptr(act_src), int(act_src.numel()),
              _ptr(self._w[c]), _ptr(self._w[o]), _ptr(self._e[c]), _ptr(self._e[o]),
-             self.decay, self.rate, _ptr(self.act_dst), peer.peer_out, peer.world, offset)
+             self.decay, self.rate, _ptr(self.act_dst), peer.out_for_next(), peer.world,
+             offset, peer.n_total)
         self._cur = o
         return self.act_dst
 

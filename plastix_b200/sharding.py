@@ -274,11 +274,25 @@ class ShardedPCNet:
 # every rank's sweep writes into directly over NVLink.
 # ---------------------------------------------------------------------------
 class PeerGather:
-    """A buffer of n_total floats on every rank, mapped into every other rank
-    through CUDA IPC, plus a flag array per rank for plx_peer_barrier. A
-    producer passes ``peer_out`` (all ranks' buffers) to
-    plx_sweep_forward_hebbian_gather with its slice offset; ``barrier()``
-    then guarantees every rank's slice has landed in every buffer."""
+    """All-gather buffers over peer memory, double-buffered by epoch.
+
+    Every rank holds two buffers of n_total floats, mapped into every other
+    rank through CUDA IPC, and a flag array for plx_peer_barrier. Epoch k
+    (counted from 1) hands off into buffer k & 1: a producer passes
+    ``out_for_next()`` (all ranks' buffers of the next epoch) to
+    plx_sweep_forward_hebbian_gather with its slice offset and
+    ``n_total`` as the buffer length, then calls ``barrier()``, after which
+    every rank's slice of that epoch has landed in every buffer and
+    ``gathered_ptr()`` / ``copy_to()`` read it.
+
+    Why two buffers: a rank that has passed barrier k may start the sweep of
+    epoch k + 1 and store into the other ranks' buffers while a slower rank
+    is still reading epoch k (a copy, or a next layer gathering from it).
+    Those stores go to the other buffer. They can only come back to epoch
+    k's buffer at epoch k + 2, which needs every rank's barrier k + 1, and
+    each rank's barrier is queued on its stream after its own reads of
+    epoch k. The contract for consumers: enqueue every read of epoch k's
+    buffer on the context's stream before the barrier of epoch k + 1."""
 
     def __init__(self, ctx, n_total: int, rank: int, world: int, group=None):
         import ctypes
@@ -294,7 +308,7 @@ class PeerGather:
         self.ctx, self.rank, self.world, self.n_total = ctx, rank, world, n_total
         self._own = []
         handles = []
-        for nbytes in (4 * n_total, 8 * world):
+        for nbytes in (4 * n_total, 4 * n_total, 8 * world):
             ptr = c_void_p()
             h = ctypes.create_string_buffer(_abi.IPC_HANDLE_BYTES)
             call("plx_peer_alloc", ctx.handle, nbytes, ctypes.byref(ptr), h)
@@ -303,25 +317,53 @@ class PeerGather:
         everyone = [None] * world
         dist.all_gather_object(everyone, handles, group=group)
         self._opened = []
-        bufs, flags = [], []
+        bufs, flags = ([], []), []
         for q in range(world):
             if q == rank:
-                bufs.append(self._own[0])
-                flags.append(self._own[1])
-                continue
-            got = []
-            for h in everyone[q]:
-                ptr = c_void_p()
-                call("plx_peer_open", ctx.handle, ctypes.create_string_buffer(h, len(h)),
-                     ctypes.byref(ptr))
-                self._opened.append(ptr.value)
-                got.append(ptr.value)
-            bufs.append(got[0])
-            flags.append(got[1])
-        self.peer_out = (c_void_p * world)(*bufs)
+                got = self._own
+            else:
+                got = []
+                for h in everyone[q]:
+                    ptr = c_void_p()
+                    call("plx_peer_open", ctx.handle, ctypes.create_string_buffer(h, len(h)),
+                         ctypes.byref(ptr))
+                    self._opened.append(ptr.value)
+                    got.append(ptr.value)
+            bufs[0].append(got[0])
+            bufs[1].append(got[1])
+            flags.append(got[2])
+        self._peer_out = tuple((c_void_p * world)(*b) for b in bufs)
         self.flags = (c_void_p * world)(*flags)
-        self.local = self._own[0]
+        self._local = (self._own[0], self._own[1])
         self.epoch = 0
+
+    @property
+    def peer_out(self):
+        """Every rank's buffer of the next epoch (what the sweep stores into)."""
+        return self._peer_out[(self.epoch + 1) & 1]
+
+    def out_for_next(self):
+        return self.peer_out
+
+    def gathered_ptr(self) -> int:
+        """This rank's buffer of the last completed epoch (device address)."""
+        if self.epoch == 0:
+            raise RuntimeError("no hand-off has completed yet")
+        return self._local[self.epoch & 1]
+
+    def gathered(self):
+        """This rank's buffer of the last completed epoch as a float32 CUDA
+        tensor (a view, no copy). It holds that epoch's values until the
+        barrier of epoch + 2: read it (e.g. as the next sweep's sources) on
+        the context's stream before the next barrier."""
+        import torch
+
+        class _View:  # zero-copy export of the peer-memory buffer to torch
+            __cuda_array_interface__ = {"shape": (self.n_total,), "typestr": "<f4",
+                                        "data": (self.gathered_ptr(), False), "version": 3,
+                                        "strides": None}
+
+        return torch.as_tensor(_View(), device=self.ctx.device)
 
     def barrier(self) -> None:
         from .runtime import call
@@ -331,10 +373,12 @@ class PeerGather:
              self.epoch)
 
     def copy_to(self, out) -> None:
-        """Copies this rank's gathered buffer into a float32 CUDA tensor."""
+        """Copies this rank's buffer of the last completed epoch into a
+        float32 CUDA tensor (on the context's stream)."""
         from .runtime import _ptr, call
 
-        call("plx_copy_device", self.ctx.handle, _ptr(out), self.local, 4 * self.n_total)
+        call("plx_copy_device", self.ctx.handle, _ptr(out), self.gathered_ptr(),
+             4 * self.n_total)
 
     def close(self) -> None:
         from .runtime import call

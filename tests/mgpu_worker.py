@@ -1,6 +1,8 @@
 """Worker for tests/test_multigpu.py (one process per GPU, launched with
-torch.distributed.run): the sharded multilayer iPC network against the same
-network on one GPU, bit for bit. Not collected by pytest."""
+torch.distributed.run, any number of ranks up to 8): the sharded multilayer
+iPC network against the same network on one GPU, the fused sweep + peer
+hand-off against an NCCL all-gather, and a recurrent chain of hand-offs
+against one GPU, all bit for bit. Not collected by pytest."""
 import os
 import sys
 from datetime import timedelta
@@ -36,6 +38,49 @@ def check_peer_handoff(ctx, rank, world, dev):
         ctx.sync()
         if not torch.equal(got, want):
             bad.append(f"peer hand-off step {step}")
+    torch.cuda.synchronize()
+    dist.barrier()
+    peer.close()
+    dist.barrier()
+    return bad
+
+
+def check_peer_chain(ctx, rank, world, dev, steps=6):
+    """A recurrent layer whose sources are the previous step's gathered
+    destination values, sharded by destination rows: each step's sweep reads
+    the last epoch's hand-off buffer while faster ranks may already store the
+    next epoch into the other buffer. Steps run back to back with no host
+    synchronisation; the final activations and weights must equal the same
+    layer stepped unsharded on one GPU, bit for bit."""
+    m, per_rank = 16384, 1_000_000
+    n = m * world  # sources = all ranks' destinations
+    shards = [workloads.sparse_layer_device(n, m, per_rank, 300 + q, dev) for q in range(world)]
+    act0 = torch.rand(n, generator=torch.Generator(device=dev).manual_seed(77), device=dev)
+    f, t, w, _ = shards[rank]
+    mine = HebbianSweepLayer(ctx, n, m, f, t, w.clone())
+    peer = PeerGather(ctx, n, rank, world)
+    x = act0
+    for _ in range(steps):
+        mine.step_gather(x, peer, rank * m)
+        peer.barrier()
+        x = peer.gathered()
+    # the same layer on one GPU: rank q's rows are rows [q*m, (q+1)*m)
+    full = HebbianSweepLayer(
+        ctx, n, n, torch.cat([s[0] for s in shards]),
+        torch.cat([s[1] + q * m for q, s in enumerate(shards)]),
+        torch.cat([s[2] for s in shards]).clone())
+    y = act0
+    for _ in range(steps):
+        y = full.step(y).clone()
+    ctx.sync()
+    bad = []
+    if not torch.equal(x, y):
+        bad.append("peer chain: gathered activations")
+    lo = rank * per_rank
+    if not torch.equal(mine.weight, full.weight[lo:lo + per_rank]):
+        bad.append("peer chain: weights")
+    if not torch.equal(mine.trace, full.trace[lo:lo + per_rank]):
+        bad.append("peer chain: traces")
     torch.cuda.synchronize()
     dist.barrier()
     peer.close()
@@ -89,6 +134,7 @@ def main():
             if not torch.equal(ch.weight[valid], full[ch.perm[valid].long()]):
                 bad.append(f"source-major weights block {l}")
     bad += check_peer_handoff(ctx, rank, world, dev)
+    bad += check_peer_chain(ctx, rank, world, dev)
     flag = torch.tensor([len(bad)], device=dev)
     dist.all_reduce(flag)
     if bad:
