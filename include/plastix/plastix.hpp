@@ -1,43 +1,42 @@
-// plastix/plastix.hpp -- the Plastix network API (Network<Traits>, SoA field
-// accessors, traits, layer builders) on the B200: the same names and policy
-// signatures as the reference header library (include/plastix/*.hpp of
-// DhanrajHira/plastix), with the state in device memory and every Do* step a
-// kernel that calls the user's policies on the GPU.
+// plastix/plastix.hpp -- the Plastix network API (Network<Traits>) on the
+// B200: the reference header library's names, policy signatures and step
+// order (include/plastix/*.hpp of DhanrajHira/plastix), with the state in
+// device memory and every Do* step run by kernels that call the user's
+// policies on the GPU. The sub-headers (alloc.hpp, soa.hpp, conn.hpp,
+// unit_state.hpp, layers.hpp, traits.hpp) are the reference's too.
 //
 // Differences a user sees:
-//   * Policy functions run on the device, so they carry PLASTIX_HD
+//   * Policy member functions run on the device, so they carry PLASTIX_HD
 //     (__host__ __device__ under nvcc, nothing otherwise):
 //       struct MyMap { PLASTIX_HD static float Map(auto &U, ...) {...} };
 //     The translation unit is compiled by nvcc (-std=c++20
-//     --expt-relaxed-constexpr -arch=sm_100a).
-//   * DoForwardPass / DoBackwardPass fold each unit's connections in the
-//     reference's order (Pipeline: connection index order, backward in
-//     descending order; Topological: by level, then index), one thread per
-//     unit, so Map/Combine/Apply see the same sequence of values.
-//   * DoUpdateConnectionState runs UpdateIncomingConnection over all
-//     connections in parallel, then UpdateOutgoingConnection. Policies that
-//     mutate the global state from those hooks (a reduction into a global, as
-//     SwiftTD does) set `static constexpr bool SequentialConnectionUpdate =
-//     true` in their traits to keep the reference's sequential semantics.
-//   * Structural policies: PruneUnit and PruneConn run per unit / per
-//     connection on the device; AddConn's proposals are enumerated on the
-//     device in the reference's order (level window, unit pairs, the four
-//     checks), then sorted, de-duplicated and committed through the C ABI
-//     (libplastix_b200: link with -lplastix_b200), and Topological networks
-//     re-sort by source level on the device (RecomputeLevels included), as
-//     the reference's constructor and DoStep do. The predicates run in
-//     parallel, so they must not change the global state -- traits with
-//     `static constexpr bool SequentialStructure = true` run them in one
-//     thread in the reference's order instead. AddUnit is not supported.
-//   * Topological passes follow the reference level by level: level L folds
-//     the connections whose SrcLevel is L - 1 into their targets' forward
-//     accumulators (one thread per unit, stored order), then applies the
-//     units of level L.
+//     --expt-relaxed-constexpr, sm_100a) and linked with -lplastix_b200.
+//   * Passes fold each unit's connections in the reference's order
+//     (Pipeline: connection index order, backward in descending order;
+//     Topological: level by level, index order within a level), so every
+//     Map/Combine/Apply sees the same sequence of values. Units run in
+//     parallel; traits whose global state may be written by the hooks (see
+//     ReadOnlyGlobalState in traits.hpp) run every hook that receives it in
+//     one device thread, in the reference's order.
+//   * Pipeline networks whose connections are stored destination-major (as
+//     FullyConnected builds them) take a warp-tiled sweep: coalesced reads of
+//     the connection fields, one warp per tile of rows, each row still folded
+//     strictly left to right.
+//   * GetUnitAlloc()/GetConnAlloc() return the network's host copies, kept
+//     coherent with the device: a field the device has changed is downloaded
+//     when the host reads it, and fields the host touched are uploaded before
+//     the next Do* step. References obtained from them stay valid across
+//     steps, as with the reference.
+//   * AddUnit runs on the host (unit growth is host-orchestrated); the new
+//     units are uploaded before the next device step. Structural decisions
+//     (PruneUnit, AddConn's predicates) run on the host copy by default and
+//     on the device with `DeviceStructure` (traits.hpp); proposals are sorted
+//     and deduplicated on the device either way, and Topological networks
+//     recompute levels and re-sort connections on the device.
 //   * No fixed capacity: networks of any size that fit the GPU.
-//   * GetUnitAlloc()/GetConnAlloc() return host copies (downloaded on call;
-//     edits made through them are uploaded before the next Do* call).
-//     GetGlobals()/SetGlobals() and Save(path)/Load(path) (checkpoints of
-//     every field plus the global state) are additions.
+//   * Additions: GetGlobals()/SetGlobals(), Save(path)/Load(path)
+//     (checkpoints of every field and the global state), SetStream(),
+//     SetProposalCapacity().
 #pragma once
 
 #include <cuda_runtime.h>
@@ -51,8 +50,8 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <optional>
 #include <random>
-#include <ranges>
 #include <span>
 #include <stdexcept>
 #include <string>
@@ -61,11 +60,11 @@
 #include <utility>
 #include <vector>
 
-#if defined(__CUDACC__)
-#define PLASTIX_HD __host__ __device__
-#else
-#define PLASTIX_HD
-#endif
+#include "plastix/alloc.hpp"
+#include "plastix/conn.hpp"
+#include "plastix/layers.hpp"
+#include "plastix/traits.hpp"
+#include "plastix/unit_state.hpp"
 
 namespace plastix {
 
@@ -75,321 +74,59 @@ inline void cuda_check(cudaError_t e, const char *what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// ---------------------------------------------------------------------------
-// Structure-of-arrays storage
-// ---------------------------------------------------------------------------
-namespace alloc {
+// Highest unit level + 1 (AddUnit clamps new levels to [1, MaxLevels - 1]).
+static constexpr uint16_t MaxLevels = 1024;
 
-template <typename Tag, typename T> struct SOAField {
-  using tag = Tag;
-  using type = T;
+struct LevelRange {
+  uint32_t Begin;
+  uint32_t End;
 };
 
-template <typename Tag, typename... Fs> struct FieldIndex;
-template <typename Tag, typename F, typename... Fs> struct FieldIndex<Tag, F, Fs...> {
-  static constexpr size_t value =
-      std::is_same_v<Tag, typename F::tag> ? 0 : 1 + FieldIndex<Tag, Fs...>::value;
+// A proposed connection packed as From | To << 32 (sorted and deduplicated
+// by these bits in DoAddConnections).
+struct CompactEdge {
+  uint64_t Bits;
+  PLASTIX_HD CompactEdge() : Bits(0) {}
+  PLASTIX_HD CompactEdge(uint32_t From, uint32_t To)
+      : Bits(static_cast<uint64_t>(From) | (static_cast<uint64_t>(To) << 32)) {}
+  PLASTIX_HD uint32_t From() const { return static_cast<uint32_t>(Bits); }
+  PLASTIX_HD uint32_t To() const { return static_cast<uint32_t>(Bits >> 32); }
 };
-template <typename Tag> struct FieldIndex<Tag> {
-  static constexpr size_t value = 0;  // not found: index == number of fields
-};
-
-// Pointers to one array per field; what device code (and host code on a host
-// copy) reads and writes through Get<Tag>(Id).
-template <typename... Fs> struct SOAView {
-  void *ptr[sizeof...(Fs) > 0 ? sizeof...(Fs) : 1];
-  size_t size;
-
-  template <typename Tag> PLASTIX_HD auto &Get(size_t Id) const {
-    constexpr size_t I = FieldIndex<Tag, Fs...>::value;
-    static_assert(I < sizeof...(Fs), "no such field");
-    using T = typename std::tuple_element_t<I, std::tuple<Fs...>>::type;
-    return static_cast<T *>(ptr[I])[Id];
-  }
-  PLASTIX_HD size_t Size() const { return size; }
-};
-
-// Host storage of the same fields (construction, host copies): one vector
-// per field, addressed by field position.
-template <typename Entity, typename... Fs> class SOAAllocator {
- public:
-  using View = SOAView<Fs...>;
-  static constexpr size_t NumFields = sizeof...(Fs);
-
-  size_t Allocate() {
-    push(std::index_sequence_for<Fs...>{});
-    return n_++;
-  }
-  std::pair<size_t, size_t> AllocateMany(size_t Count) {
-    const size_t B = n_;
-    for (size_t I = 0; I < Count; ++I) Allocate();
-    return {B, n_};
-  }
-  size_t Size() const { return n_; }
-  // Sets the number of entities (new ones value-initialised).
-  void Resize(size_t N) {
-    resize(N, std::index_sequence_for<Fs...>{});
-    n_ = N;
-  }
-  template <typename Tag> auto &Get(size_t Id) {
-    return std::get<FieldIndex<Tag, Fs...>::value>(store_)[Id];
-  }
-  template <typename Tag> const auto &Get(size_t Id) const {
-    return std::get<FieldIndex<Tag, Fs...>::value>(store_)[Id];
-  }
-  template <typename Tag> auto *GetArrayFor() {
-    return std::get<FieldIndex<Tag, Fs...>::value>(store_).data();
-  }
-  void *field_data(size_t I) { return data_ptr(I, std::index_sequence_for<Fs...>{}); }
-  static constexpr size_t field_bytes(size_t I) {
-    constexpr size_t B[] = {sizeof(typename Fs::type)...};
-    return B[I];
-  }
-  // dst[i] = src[perm[i]] for every field (SOAAllocator::Gather semantics).
-  void Gather(const std::vector<size_t> &Perm) { gather(Perm, std::index_sequence_for<Fs...>{}); }
-
- private:
-  template <size_t... Is> void resize(size_t N, std::index_sequence<Is...>) {
-    (std::get<Is>(store_).resize(N), ...);
-  }
-  template <size_t... Is> void push(std::index_sequence<Is...>) {
-    (std::get<Is>(store_).emplace_back(), ...);
-  }
-  template <size_t... Is> void *data_ptr(size_t I, std::index_sequence<Is...>) {
-    void *p = nullptr;
-    ((I == Is ? (p = static_cast<void *>(std::get<Is>(store_).data()), 0) : 0), ...);
-    return p;
-  }
-  template <size_t... Is> void gather(const std::vector<size_t> &Perm, std::index_sequence<Is...>) {
-    (gather_one(std::get<Is>(store_), Perm), ...);
-  }
-  template <typename V> static void gather_one(V &v, const std::vector<size_t> &Perm) {
-    V out(Perm.size());
-    for (size_t i = 0; i < Perm.size(); ++i) out[i] = v[Perm[i]];
-    v.swap(out);
-  }
-
-  std::tuple<std::vector<typename Fs::type>...> store_;
-  size_t n_ = 0;
-};
-
-}  // namespace alloc
-
-// ---------------------------------------------------------------------------
-// Unit and connection schemas, accessors
-// ---------------------------------------------------------------------------
-struct UnitState {};
-struct ConnectionState {};
-struct ActivationTag {};
-struct ForwardAccTag {};
-struct BackwardAccTag {};
-struct PrunedTag {};
-struct LevelTag {};
-struct FromIdTag {};
-struct ToIdTag {};
-struct DeadTag {};
-struct SrcLevelTag {};
-struct WeightTag {};
-
-// Accessors work on the device views and on the host allocators (host-only
-// Get): the execution-space check is lifted for these templates, each
-// instantiation is only ever called where its Get exists.
-#if defined(__CUDACC__)
-#define PLASTIX_NO_EXEC_CHECK _Pragma("nv_exec_check_disable")
-#else
-#define PLASTIX_NO_EXEC_CHECK
-#endif
-PLASTIX_NO_EXEC_CHECK
-template <typename Tag> PLASTIX_HD constexpr auto &GetField(auto &Alloc, size_t Id) {
-  return Alloc.template Get<Tag>(Id);
-}
-PLASTIX_NO_EXEC_CHECK
-PLASTIX_HD constexpr auto &GetWeight(auto &Alloc, size_t Id) {
-  return GetField<WeightTag>(Alloc, Id);
-}
-PLASTIX_NO_EXEC_CHECK
-PLASTIX_HD constexpr auto &GetActivation(auto &Alloc, size_t Id) {
-  return GetField<ActivationTag>(Alloc, Id);
-}
-PLASTIX_NO_EXEC_CHECK
-PLASTIX_HD constexpr auto &GetForwardAcc(auto &Alloc, size_t Id) {
-  return GetField<ForwardAccTag>(Alloc, Id);
-}
-PLASTIX_NO_EXEC_CHECK
-PLASTIX_HD constexpr auto &GetBackwardAcc(auto &Alloc, size_t Id) {
-  return GetField<BackwardAccTag>(Alloc, Id);
-}
-PLASTIX_NO_EXEC_CHECK
-PLASTIX_HD constexpr auto &GetLevel(auto &Alloc, size_t Id) {
-  return GetField<LevelTag>(Alloc, Id);
-}
-
-template <typename... Fields> struct UnitFieldList {};
-template <typename... Fields> struct ConnFieldList {};
-
-// ---------------------------------------------------------------------------
-// Traits
-// ---------------------------------------------------------------------------
-enum class Propagation { Topological, Pipeline };
-
-struct UnitRange {
-  size_t Begin = 0;
-  size_t End = 0;
-  UnitRange() = default;
-  PLASTIX_HD UnitRange(size_t B, size_t E) : Begin(B), End(E) {}
-  UnitRange(std::pair<size_t, size_t> P) : Begin(P.first), End(P.second) {}
-  PLASTIX_HD size_t Size() const { return End - Begin; }
-  auto Ids() const { return std::views::iota(Begin, End); }
-};
-
-struct EmptyGlobalState {};
-
-struct DefaultForwardPass {
-  using Accumulator = float;
-  PLASTIX_HD static float Map(auto &U, size_t, size_t SrcId, auto &C, size_t ConnId, auto &) {
-    return GetWeight(C, ConnId) * GetActivation(U, SrcId);
-  }
-  PLASTIX_HD static float Combine(float A, float B) { return A + B; }
-  PLASTIX_HD static void Apply(auto &U, size_t Id, auto &, float Acc) {
-    GetActivation(U, Id) = Acc;
-  }
-};
-struct NoBackwardPass {
-  using Accumulator = float;
-};
-struct NoLoss {};
-struct NoUpdateUnit {};
-struct NoUpdateConn {};
-struct NoPruneUnit {};
-struct NoPruneConn {};
-struct NoAddUnit {};
-struct NoAddConn {};
-struct NoResetGlobalState {};
-
-// Mean squared error: BackwardAcc of each output = prediction - target.
-struct MSELoss {
-  PLASTIX_HD static void CalculateLoss(auto &U, UnitRange Outputs, std::span<const float> Targets,
-                                       auto &) {
-    size_t I = 0;
-    for (size_t Id = Outputs.Begin; Id < Outputs.End; ++Id)
-      GetBackwardAcc(U, Id) = GetActivation(U, Id) - Targets[I++];
-  }
-};
-
-template <typename Global = EmptyGlobalState> struct DefaultNetworkTraits {
-  using GlobalState = Global;
-  using ForwardPass = DefaultForwardPass;
-  using BackwardPass = NoBackwardPass;
-  using Loss = NoLoss;
-  using UpdateUnit = NoUpdateUnit;
-  using UpdateConn = NoUpdateConn;
-  using PruneUnit = NoPruneUnit;
-  using PruneConn = NoPruneConn;
-  using AddUnit = NoAddUnit;
-  using AddConn = NoAddConn;
-  using ResetGlobal = NoResetGlobalState;
-  using ExtraUnitFields = UnitFieldList<>;
-  using ExtraConnFields = ConnFieldList<alloc::SOAField<WeightTag, float>>;
-  static constexpr uint16_t Neighbourhood = 1;
-  static constexpr Propagation Model = Propagation::Topological;
-};
-
-// ---------------------------------------------------------------------------
-// Layer builders (host side, at construction)
-// ---------------------------------------------------------------------------
-struct NoUnitInit {
-  void operator()(auto &, auto) const {}
-};
-struct NoConnInit {
-  void operator()(auto &, auto) const {}
-};
-
-struct RandomUniformWeight {
-  RandomUniformWeight(uint32_t Seed = 0, float Min = -1.0f, float Max = 1.0f)
-      : Rng(Seed), Dist(Min, Max) {}
-  void operator()(auto &CA, auto Id) const { GetWeight(CA, Id) = Dist(Rng); }
-
- private:
-  mutable std::mt19937 Rng;
-  mutable std::uniform_real_distribution<float> Dist;
-};
-
-// NumUnits new units one level above the previous layer, each fed by every
-// unit of the previous layer (destination-major connection order).
-template <typename ConnInit = NoConnInit, typename UnitInit = NoUnitInit> struct FullyConnected {
-  size_t NumUnits;
-  ConnInit InitConn = {};
-  UnitInit InitUnit = {};
-
-  template <typename UA, typename CA> UnitRange operator()(UA &U, CA &C, UnitRange Prev) const {
-    const uint16_t Lvl = GetLevel(U, Prev.Begin) + 1;
-    UnitRange Units = U.AllocateMany(NumUnits);
-    for (size_t Id = Units.Begin; Id < Units.End; ++Id) {
-      GetLevel(U, Id) = Lvl;
-      InitUnit(U, Id);
-    }
-    const uint16_t SrcLvl = GetLevel(U, Prev.Begin);
-    for (size_t Dst = Units.Begin; Dst < Units.End; ++Dst)
-      for (size_t Src = Prev.Begin; Src < Prev.End; ++Src) {
-        const size_t Id = C.Allocate();
-        GetField<ToIdTag>(C, Id) = static_cast<uint32_t>(Dst);
-        GetField<FromIdTag>(C, Id) = static_cast<uint32_t>(Src);
-        GetField<SrcLevelTag>(C, Id) = SrcLvl;
-        InitConn(C, Id);
-      }
-    return Units;
-  }
-};
-template <typename CI> FullyConnected(size_t, CI) -> FullyConnected<CI, NoUnitInit>;
-template <typename CI, typename UI>
-FullyConnected(size_t, CI, UI) -> FullyConnected<CI, UI>;
 
 // ---------------------------------------------------------------------------
 // Device kernels (templated on the traits; instantiated in the user's TU)
 // ---------------------------------------------------------------------------
 namespace detail {
 
-template <class Entity, class FwdAcc, class BwdAcc, class... Extra>
-using UnitAllocT = alloc::SOAAllocator<Entity, alloc::SOAField<ActivationTag, float>,
-                                       alloc::SOAField<ForwardAccTag, FwdAcc>,
-                                       alloc::SOAField<BackwardAccTag, BwdAcc>,
-                                       alloc::SOAField<PrunedTag, uint8_t>,
-                                       alloc::SOAField<LevelTag, uint16_t>, Extra...>;
-template <class Entity, class... Extra>
-using ConnAllocT = alloc::SOAAllocator<Entity, alloc::SOAField<FromIdTag, uint32_t>,
-                                       alloc::SOAField<ToIdTag, uint32_t>,
-                                       alloc::SOAField<DeadTag, uint8_t>,
-                                       alloc::SOAField<SrcLevelTag, uint16_t>, Extra...>;
-
-template <class Fwd, class Bwd, class L> struct UnitAllocFromList;
-template <class Fwd, class Bwd, class... E> struct UnitAllocFromList<Fwd, Bwd, UnitFieldList<E...>> {
-  using type = UnitAllocT<UnitState, Fwd, Bwd, E...>;
-};
-template <class L> struct ConnAllocFromList;
-template <class... E> struct ConnAllocFromList<ConnFieldList<E...>> {
-  using type = ConnAllocT<ConnectionState, E...>;
-};
-
-template <class T> struct SequentialUpdate {
-  static constexpr bool value = false;
-};
-template <class T>
-  requires requires { T::SequentialConnectionUpdate; }
-struct SequentialUpdate<T> {
-  static constexpr bool value = T::SequentialConnectionUpdate;
-};
+template <class T> constexpr bool read_only_globals() {
+  if constexpr (requires { T::ReadOnlyGlobalState; }) return T::ReadOnlyGlobalState;
+  else return std::is_empty_v<typename T::GlobalState>;
+}
+template <class T> constexpr bool sequential_conn_update() {
+  if constexpr (requires { T::SequentialConnectionUpdate; }) return T::SequentialConnectionUpdate;
+  else return !read_only_globals<T>();
+}
+template <class T> constexpr bool device_structure() {
+  if constexpr (requires { T::DeviceStructure; }) return T::DeviceStructure;
+  else return false;
+}
+template <class T> constexpr bool sequential_structure() {
+  if constexpr (requires { T::SequentialStructure; }) return T::SequentialStructure;
+  else return !read_only_globals<T>();
+}
 
 inline unsigned blocks(size_t n) { return (unsigned)std::max<size_t>(1, (n + 255) / 256); }
 
-// Forward accumulation: unit I (in [lo, hi), optionally only level `lvl`)
-// folds its incoming connections in the stored order.
+// ---- passes, one thread per unit ------------------------------------------
+
+// Pipeline forward accumulation: unit I folds its incoming connections in
+// index order (in_conn lists them per destination, ascending).
 template <class Tr, class UV, class CV, class G>
 __global__ void k_fwd_acc(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
-                          size_t lo, size_t hi, int lvl) {
+                          size_t n) {
   using FP = typename Tr::ForwardPass;
-  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= hi) return;
-  if (lvl >= 0 && GetLevel(U, I) != lvl) return;
+  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I >= n) return;
   auto acc = GetForwardAcc(U, I);
   for (uint32_t k = in_ptr[I]; k < in_ptr[I + 1]; ++k) {
     const uint32_t c = in_conn[k];
@@ -399,93 +136,10 @@ __global__ void k_fwd_acc(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32
   GetForwardAcc(U, I) = acc;
 }
 
-template <class Tr, class UV, class G>
-__global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
-  using FP = typename Tr::ForwardPass;
-  using Acc = typename FP::Accumulator;
-  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= hi) return;
-  if (lvl >= 0 && GetLevel(U, I) != lvl) return;
-  FP::Apply(U, I, *g, GetForwardAcc(U, I));
-  GetForwardAcc(U, I) = Acc{};
-}
-
-// Backward accumulation: unit I folds its outgoing connections, descending
-// index order (Pipeline) or ascending (Topological), starting from its current
-// BackwardAcc (which a loss may have set).
-template <class Tr, class UV, class CV, class G>
-__global__ void k_bwd_acc(UV U, CV C, G *g, const uint32_t *out_ptr, const uint32_t *out_conn,
-                          size_t n, int lvl, bool descending) {
-  using BP = typename Tr::BackwardPass;
-  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= n) return;
-  if (lvl >= 0 && GetLevel(U, I) != lvl) return;
-  auto acc = GetBackwardAcc(U, I);
-  const uint32_t b = out_ptr[I], e = out_ptr[I + 1];
-  for (uint32_t j = 0; j < e - b; ++j) {
-    const uint32_t c = out_conn[descending ? e - 1 - j : b + j];
-    if (GetField<DeadTag>(C, c)) continue;
-    acc = BP::Combine(acc, BP::Map(U, I, GetField<ToIdTag>(C, c), C, c, *g));
-  }
-  GetBackwardAcc(U, I) = acc;
-}
-
-template <class Tr, class UV, class G>
-__global__ void k_bwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
-  using BP = typename Tr::BackwardPass;
-  using Acc = typename BP::Accumulator;
-  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= hi) return;
-  if (lvl >= 0 && GetLevel(U, I) != lvl) return;
-  BP::Apply(U, I, *g, GetBackwardAcc(U, I));
-  GetBackwardAcc(U, I) = Acc{};
-}
-
-template <class Tr, class UV, class G>
-__global__ void k_loss(UV U, G *g, UnitRange out, const float *t, size_t nt) {
-  Tr::Loss::CalculateLoss(U, out, std::span<const float>(t, nt), *g);
-}
-
-template <class Tr, class UV, class G> __global__ void k_update_unit(UV U, G *g, size_t n) {
-  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I < n) Tr::UpdateUnit::Update(U, I, *g);
-}
-
-// Per-connection update: parallel over connections, or one thread in index
-// order when the traits ask for sequential semantics.
-template <class Tr, bool Incoming, class UV, class CV, class G>
-__global__ void k_update_conn(UV U, CV C, G *g, size_t n, bool sequential) {
-  using UP = typename Tr::UpdateConn;
-  const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  const size_t step = sequential ? 1 : (size_t)gridDim.x * blockDim.x;
-  if (sequential && first != 0) return;
-  for (size_t c = first; c < n; c += step) {
-    if (GetField<DeadTag>(C, c)) continue;
-    const size_t to = GetField<ToIdTag>(C, c), from = GetField<FromIdTag>(C, c);
-    if constexpr (Incoming) UP::UpdateIncomingConnection(U, to, from, C, c, *g);
-    else UP::UpdateOutgoingConnection(U, from, to, C, c, *g);
-  }
-}
-
-template <class Tr, class G> __global__ void k_reset(G *g) { Tr::ResetGlobal::Reset(*g); }
-
-// Traits flag for structural policies that mutate the global state (an RNG
-// drawn inside a predicate): prune, proposal and commit hooks then run in one
-// thread, in the reference's order.
-template <class T> struct SequentialStructure {
-  static constexpr bool value = false;
-};
-template <class T>
-  requires requires { T::SequentialStructure; }
-struct SequentialStructure<T> {
-  static constexpr bool value = T::SequentialStructure;
-};
-
-// Topological forward accumulation of level L (plastix.hpp:111-119 of the
-// reference): every unit folds, in stored order, those incoming connections
-// whose SrcLevel is L - 1 -- whatever the unit's own level. Connections are
-// kept sorted by SrcLevel, so each unit's incoming list is too; `cur` is the
-// unit's position in it, advanced level by level.
+// Topological forward accumulation of level L (reference plastix.hpp:111-119):
+// every unit folds, in stored order, those incoming connections whose
+// SrcLevel is L - 1. Connections are sorted by SrcLevel, so each unit's
+// incoming list is too; `cur` is the unit's position in it.
 template <class Tr, class UV, class CV, class G>
 __global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
                                 uint32_t *cur, size_t n, int L) {
@@ -510,13 +164,153 @@ __global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const 
   if (any) GetForwardAcc(U, I) = acc;
 }
 
+// Apply of the units in [lo, hi) (only those at level `lvl` when lvl >= 0),
+// then the accumulator is reset.
+template <class Tr, class UV, class G>
+__global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
+  using FP = typename Tr::ForwardPass;
+  using Acc = typename FP::Accumulator;
+  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I >= hi) return;
+  if (lvl >= 0 && GetLevel(U, I) != lvl) return;
+  FP::Apply(U, I, *g, GetForwardAcc(U, I));
+  GetForwardAcc(U, I) = Acc{};
+}
+
+// Backward accumulation: unit I folds its outgoing connections into its
+// BackwardAcc -- descending index order (Pipeline, plastix.hpp:193), or, for
+// Topological level L, ascending over those whose SrcLevel is L
+// (plastix.hpp:170-181).
+template <class Tr, class UV, class CV, class G>
+__global__ void k_bwd_acc(UV U, CV C, G *g, const uint32_t *out_ptr, const uint32_t *out_conn,
+                          size_t n, int L) {
+  using BP = typename Tr::BackwardPass;
+  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I >= n) return;
+  const uint32_t b = out_ptr[I], e = out_ptr[I + 1];
+  if (b == e) return;
+  auto acc = GetBackwardAcc(U, I);
+  for (uint32_t j = 0; j < e - b; ++j) {
+    const uint32_t c = out_conn[L < 0 ? e - 1 - j : b + j];
+    if (GetField<DeadTag>(C, c)) continue;
+    if (L >= 0 && GetField<SrcLevelTag>(C, c) != (uint16_t)L) continue;
+    acc = BP::Combine(acc, BP::Map(U, I, GetField<ToIdTag>(C, c), C, c, *g));
+  }
+  GetBackwardAcc(U, I) = acc;
+}
+
+template <class Tr, class UV, class G>
+__global__ void k_bwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
+  using BP = typename Tr::BackwardPass;
+  using Acc = typename BP::Accumulator;
+  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I >= hi) return;
+  if (lvl >= 0 && GetLevel(U, I) != lvl) return;
+  BP::Apply(U, I, *g, GetBackwardAcc(U, I));
+  GetBackwardAcc(U, I) = Acc{};
+}
+
+// ---- passes in one thread: the reference's loops verbatim in order ---------
+// (hooks that may write the global state). `ranges[L]` is the first
+// connection whose SrcLevel is >= L (Topological, after the level sort).
+template <class Tr, class UV, class CV, class G>
+__global__ void k_fwd_seq(UV U, CV C, G *g, size_t n_input, size_t n, size_t m,
+                          const uint32_t *ranges, int levels, bool topo) {
+  using FP = typename Tr::ForwardPass;
+  using Acc = typename FP::Accumulator;
+  auto fold = [&](size_t c) {
+    if (GetField<DeadTag>(C, c)) return;
+    const size_t To = GetField<ToIdTag>(C, c), From = GetField<FromIdTag>(C, c);
+    auto &A = GetForwardAcc(U, To);
+    A = FP::Combine(A, FP::Map(U, To, From, C, c, *g));
+  };
+  if (topo) {
+    for (int L = 1; L <= levels; ++L) {
+      for (size_t c = ranges[L - 1]; c < ranges[L]; ++c) fold(c);
+      for (size_t I = n_input; I < n; ++I)
+        if (GetLevel(U, I) == L) {
+          FP::Apply(U, I, *g, GetForwardAcc(U, I));
+          GetForwardAcc(U, I) = Acc{};
+        }
+    }
+  } else {
+    for (size_t c = 0; c < m; ++c) fold(c);
+    for (size_t I = n_input; I < n; ++I) {
+      FP::Apply(U, I, *g, GetForwardAcc(U, I));
+      GetForwardAcc(U, I) = Acc{};
+    }
+  }
+}
+
+template <class Tr, class UV, class CV, class G>
+__global__ void k_bwd_seq(UV U, CV C, G *g, size_t n_input, size_t n, size_t m,
+                          const uint32_t *ranges, int levels, bool topo) {
+  using BP = typename Tr::BackwardPass;
+  using Acc = typename BP::Accumulator;
+  auto fold = [&](size_t c) {
+    if (GetField<DeadTag>(C, c)) return;
+    const size_t To = GetField<ToIdTag>(C, c), From = GetField<FromIdTag>(C, c);
+    auto &A = GetBackwardAcc(U, From);
+    A = BP::Combine(A, BP::Map(U, From, To, C, c, *g));
+  };
+  if (topo) {
+    for (int L = levels; L >= 1; --L) {
+      for (size_t c = ranges[L]; c < ranges[L + 1]; ++c) fold(c);
+      for (size_t I = n_input; I < n; ++I)
+        if (GetLevel(U, I) == L) {
+          BP::Apply(U, I, *g, GetBackwardAcc(U, I));
+          GetBackwardAcc(U, I) = Acc{};
+        }
+    }
+  } else {
+    for (size_t c = m; c-- > 0;) fold(c);
+    for (size_t I = 0; I < n; ++I) {
+      BP::Apply(U, I, *g, GetBackwardAcc(U, I));
+      GetBackwardAcc(U, I) = Acc{};
+    }
+  }
+}
+
+template <class Tr, class UV, class G>
+__global__ void k_loss(UV U, G *g, UnitRange out, const float *t, size_t nt) {
+  Tr::Loss::CalculateLoss(U, out, std::span<const float>(t, nt), *g);
+}
+
+template <class Tr, class UV, class G>
+__global__ void k_update_unit(UV U, G *g, size_t n, bool seq) {
+  const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t step = seq ? 1 : (size_t)gridDim.x * blockDim.x;
+  if (seq && first != 0) return;
+  for (size_t I = first; I < n; I += step) Tr::UpdateUnit::Update(U, I, *g);
+}
+
+// Per-connection update: parallel over connections, or one thread in index
+// order for sequential semantics.
+template <class Tr, bool Incoming, class UV, class CV, class G>
+__global__ void k_update_conn(UV U, CV C, G *g, size_t n, bool sequential) {
+  using UP = typename Tr::UpdateConn;
+  const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t step = sequential ? 1 : (size_t)gridDim.x * blockDim.x;
+  if (sequential && first != 0) return;
+  for (size_t c = first; c < n; c += step) {
+    if (GetField<DeadTag>(C, c)) continue;
+    const size_t to = GetField<ToIdTag>(C, c), from = GetField<FromIdTag>(C, c);
+    if constexpr (Incoming) UP::UpdateIncomingConnection(U, to, from, C, c, *g);
+    else UP::UpdateOutgoingConnection(U, from, to, C, c, *g);
+  }
+}
+
+template <class Tr, class G> __global__ void k_reset(G *g) { Tr::ResetGlobal::Reset(*g); }
+
+// ---- structure --------------------------------------------------------------
+
 // DoPruneUnits (reference plastix.hpp:257-267): Pruned = ShouldPrune.
 template <class Tr, class UV, class G> __global__ void k_prune_units(UV U, G *g, size_t n, bool seq) {
   const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t step = seq ? 1 : (size_t)gridDim.x * blockDim.x;
   if (seq && first != 0) return;
   for (size_t I = first; I < n; I += step)
-    GetField<PrunedTag>(U, I) = Tr::PruneUnit::ShouldPrune(U, I, *g) ? 1 : 0;
+    GetField<PrunedTag>(U, I) = Tr::PruneUnit::ShouldPrune(U, I, *g) ? true : false;
 }
 
 // DoPruneConnections (reference plastix.hpp:269-299): a live connection dies
@@ -535,7 +329,7 @@ __global__ void k_prune_conns(UV U, CV C, G *g, size_t m, bool seq) {
     if constexpr (HasUnit) rm = GetField<PrunedTag>(U, to) || GetField<PrunedTag>(U, from);
     if constexpr (HasConn)
       if (!rm) rm = Tr::PruneConn::ShouldPrune(U, to, from, C, c, *g);
-    if (rm) GetField<DeadTag>(C, c) = 1;
+    if (rm) GetField<DeadTag>(C, c) = true;
   }
 }
 
@@ -548,10 +342,6 @@ struct LevelPair {
 };
 constexpr int kPropItems = 4;                      // slots per thread
 constexpr uint64_t kPropChunk = 256 * kPropItems;  // slots per block and chunk
-
-PLASTIX_HD inline uint64_t compact_edge(size_t from, size_t to) {  // CompactEdge::Bits
-  return (uint64_t)(uint32_t)from | ((uint64_t)(uint32_t)to << 32);
-}
 
 __device__ inline uint32_t find_pair(const LevelPair *p, uint32_t n, uint64_t s) {
   uint32_t lo = 0, hi = n;
@@ -573,11 +363,11 @@ __device__ uint32_t propose_slot(UV &U, G *g, const LevelPair *pairs, uint32_t n
   const size_t A = ubl[P.a0 + r / P.nb], B = ubl[P.b0 + r % P.nb];
   if (A == B) return 0;
   uint32_t k = 0;
-  if (AC::ShouldAddIncomingConnection(U, A, B, *g)) out[k++] = compact_edge(B, A);
-  if (AC::ShouldAddOutgoingConnection(U, A, B, *g)) out[k++] = compact_edge(A, B);
+  if (AC::ShouldAddIncomingConnection(U, A, B, *g)) out[k++] = CompactEdge(B, A).Bits;
+  if (AC::ShouldAddOutgoingConnection(U, A, B, *g)) out[k++] = CompactEdge(A, B).Bits;
   if (!P.same) {
-    if (AC::ShouldAddIncomingConnection(U, B, A, *g)) out[k++] = compact_edge(A, B);
-    if (AC::ShouldAddOutgoingConnection(U, B, A, *g)) out[k++] = compact_edge(B, A);
+    if (AC::ShouldAddIncomingConnection(U, B, A, *g)) out[k++] = CompactEdge(A, B).Bits;
+    if (AC::ShouldAddOutgoingConnection(U, B, A, *g)) out[k++] = CompactEdge(B, A).Bits;
   }
   return k;
 }
@@ -629,13 +419,15 @@ __global__ void k_propose_seq(UV U, G *g, const LevelPair *pairs, uint32_t np, c
       for (uint32_t bi = 0; bi < P.nb; ++bi) {
         const size_t B = ubl[P.b0 + bi];
         if (A == B) continue;
-        if (n < cap && AC::ShouldAddIncomingConnection(U, A, B, *g)) props[n++] = compact_edge(B, A);
-        if (n < cap && AC::ShouldAddOutgoingConnection(U, A, B, *g)) props[n++] = compact_edge(A, B);
+        if (n < cap && AC::ShouldAddIncomingConnection(U, A, B, *g))
+          props[n++] = CompactEdge(B, A).Bits;
+        if (n < cap && AC::ShouldAddOutgoingConnection(U, A, B, *g))
+          props[n++] = CompactEdge(A, B).Bits;
         if (!P.same) {
           if (n < cap && AC::ShouldAddIncomingConnection(U, B, A, *g))
-            props[n++] = compact_edge(A, B);
+            props[n++] = CompactEdge(A, B).Bits;
           if (n < cap && AC::ShouldAddOutgoingConnection(U, B, A, *g))
-            props[n++] = compact_edge(B, A);
+            props[n++] = CompactEdge(B, A).Bits;
         }
       }
     }
@@ -662,16 +454,37 @@ __global__ void k_commit_conns(UV U, CV C, G *g, const uint64_t *edges, size_t k
   }
 }
 
-__global__ inline void k_widen_u16(const uint16_t *in, size_t n, uint32_t *out) {
+static __global__ void k_widen_u16(const uint16_t *in, size_t n, uint32_t *out) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     out[i] = in[i];
 }
 
-__global__ inline void k_level_hist(const uint16_t *level, size_t n, uint32_t *hist) {
+static __global__ void k_level_hist(const uint16_t *level, size_t n, uint32_t *hist) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     atomicAdd(hist + level[i], 1u);
+}
+
+// ranges[L] = first index whose (sorted) key is >= L, for L in [0, nr).
+static __global__ void k_level_ranges(const uint32_t *keys, size_t m, uint32_t *ranges, int nr) {
+  const int L = blockIdx.x * blockDim.x + threadIdx.x;
+  if (L >= nr) return;
+  size_t lo = 0, hi = m;
+  while (lo < hi) {
+    const size_t mid = (lo + hi) / 2;
+    if ((keys[mid] & 0xFFFFu) < (uint32_t)L) lo = mid + 1;
+    else hi = mid;
+  }
+  ranges[L] = (uint32_t)lo;
+}
+
+// 1 when the connections are stored destination-major (ToId non-decreasing
+// over all connections), else 0 (flag initialised to 1 by the caller).
+static __global__ void k_check_dst_major(const uint32_t *to, size_t m, uint32_t *flag) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i + 1 < m;
+       i += (size_t)gridDim.x * blockDim.x)
+    if (to[i + 1] < to[i]) *flag = 0;
 }
 
 }  // namespace detail
@@ -684,33 +497,37 @@ template <typename Traits> class Network {
   using GlobalState = typename Traits::GlobalState;
   using FP = typename Traits::ForwardPass;
   using BP = typename Traits::BackwardPass;
-  using UnitAllocator = typename detail::UnitAllocFromList<
-      typename FP::Accumulator, typename BP::Accumulator, typename Traits::ExtraUnitFields>::type;
-  using ConnAllocator = typename detail::ConnAllocFromList<typename Traits::ExtraConnFields>::type;
+  using UnitAllocator = UnitAllocFor<Traits>;
+  using ConnAllocator = ConnAllocFor<Traits>;
   using UView = typename UnitAllocator::View;
   using CView = typename ConnAllocator::View;
 
-  static_assert(std::is_same_v<typename Traits::AddUnit, NoAddUnit>,
-                "AddUnit policies are not supported on the device");
   static_assert(std::is_trivially_copyable_v<GlobalState>, "global state is copied to the GPU");
 
   template <typename... Builders>
-    requires(sizeof...(Builders) > 0)
+    requires(sizeof...(Builders) > 0 &&
+             (LayerBuilder<Builders, UnitAllocator, ConnAllocator> && ...))
   Network(size_t InputDim, Builders... Layers) : Network(InputDim, NoUnitInit{}, Layers...) {}
 
   template <typename InputInit, typename... Builders>
-    requires(std::is_invocable_v<InputInit, UnitAllocator &, size_t> && sizeof...(Builders) > 0)
-  Network(size_t InputDim, InputInit Init, Builders... Layers) : NumInput(InputDim) {
+    requires(std::is_invocable_v<InputInit, UnitAllocator &, size_t> && sizeof...(Builders) > 0 &&
+             (LayerBuilder<Builders, UnitAllocator, ConnAllocator> && ...))
+  Network(size_t InputDim, InputInit Init, Builders... Layers)
+      : NumInput(InputDim), UA(kCapacity), CA(kCapacity) {
     for (size_t I = 0; I < InputDim; ++I) Init(UA, UA.Allocate());
     UnitRange Prev{0, InputDim};
     ((Prev = Layers(UA, CA, Prev)), ...);
     OutputRange = Prev;
     cuda_check(cudaGetDevice(&Device), "device");
-    Upload();
+    UA.Link({&Network::FetchUnitField, this});
+    CA.Link({&Network::FetchConnField, this});
+    cuda_check(cudaMalloc(&d_g, sizeof(GlobalState) > 0 ? sizeof(GlobalState) : 1), "globals");
+    cuda_check(cudaMemcpy(d_g, &HostG, sizeof(GlobalState), cudaMemcpyHostToDevice), "globals");
+    BeginDevice();
     // As the reference's constructor: Topological networks recompute the
     // unit levels and sort the connections by source level.
     if constexpr (Traits::Model == Propagation::Topological) SortConnectionsByLevel();
-    RebuildIndex();
+    EndDevice(true, true);
   }
 
   Network(size_t InputDim, size_t OutputDim = 1) : Network(InputDim, FullyConnected<>{OutputDim}) {}
@@ -722,15 +539,22 @@ template <typename Traits> class Network {
   size_t GetStep() const { return Step; }
 
   void DoForwardPass(std::span<const float> Inputs) {
-    SyncToDevice();
-    if (NumInput)
-      cuda_check(cudaMemcpyAsync(d_uf[0], Inputs.data(), NumInput * sizeof(float),
+    BeginDevice();
+    const size_t k = std::min(Inputs.size(), NumInput);
+    if (k)
+      cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], Inputs.data(), k * sizeof(float),
                                  cudaMemcpyHostToDevice, Stream),
                  "inputs");
-    const size_t n = UA.Size();
-    if constexpr (Traits::Model == Propagation::Topological) {
+    const size_t n = UA.Size(), m = CA.Size();
+    constexpr bool topo = Traits::Model == Propagation::Topological;
+    if constexpr (topo) {
       if (NeedsResort) SortConnectionsByLevel();
-      if (IndexStale) RebuildIndex();
+    }
+    if (IndexStale) RebuildIndex();
+    if constexpr (!detail::read_only_globals<Traits>()) {
+      detail::k_fwd_seq<Traits><<<1, 1, 0, Stream>>>(UV(), CV(), d_g, NumInput, n, m, d_ranges,
+                                                      NumLevels, topo);
+    } else if constexpr (topo) {
       if (n)
         cuda_check(cudaMemcpyAsync(d_cursor, d_in_ptr, n * sizeof(uint32_t),
                                    cudaMemcpyDeviceToDevice, Stream),
@@ -741,20 +565,21 @@ template <typename Traits> class Network {
         detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, L);
       }
     } else {
-      if (IndexStale) RebuildIndex();
       detail::k_fwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), CV(), d_g, d_in_ptr,
-                                                                        d_in_conn, 0, n, -1);
+                                                                        d_in_conn, n);
       detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, -1);
     }
     cuda_check(cudaGetLastError(), "forward pass");
+    EndDevice(true, true);
     ++Step;
   }
 
   void DoCalculateLoss(std::span<const float> Targets) {
     if constexpr (!std::is_same_v<typename Traits::Loss, NoLoss>) {
       if (Targets.empty()) return;
-      SyncToDevice();
+      BeginDevice();
       if (Targets.size() > TargetCap) {
+        cuda_check(cudaStreamSynchronize(Stream), "targets");
         if (d_targets) cudaFree(d_targets);
         cuda_check(cudaMalloc(&d_targets, Targets.size() * sizeof(float)), "targets");
         TargetCap = Targets.size();
@@ -765,33 +590,39 @@ template <typename Traits> class Network {
       detail::k_loss<Traits><<<1, 1, 0, Stream>>>(UV(), d_g, OutputRange, d_targets,
                                                   Targets.size());
       cuda_check(cudaGetLastError(), "loss");
+      EndDevice(true, false);
     }
   }
 
   void DoBackwardPass() {
     if constexpr (!std::is_same_v<BP, NoBackwardPass>) {
-      SyncToDevice();
+      BeginDevice();
       if (IndexStale) RebuildIndex();
-      const size_t n = UA.Size();
-      if constexpr (Traits::Model == Propagation::Topological) {
+      const size_t n = UA.Size(), m = CA.Size();
+      constexpr bool topo = Traits::Model == Propagation::Topological;
+      if constexpr (!detail::read_only_globals<Traits>()) {
+        detail::k_bwd_seq<Traits><<<1, 1, 0, Stream>>>(UV(), CV(), d_g, NumInput, n, m, d_ranges,
+                                                        NumLevels, topo);
+      } else if constexpr (topo) {
         for (int L = NumLevels; L >= 1; --L) {
           detail::k_bwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
-              UV(), CV(), d_g, d_out_ptr, d_out_conn, n, L, false);
+              UV(), CV(), d_g, d_out_ptr, d_out_conn, n, L);
           detail::k_bwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput,
                                                                              n, L);
         }
       } else {
         detail::k_bwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
-            UV(), CV(), d_g, d_out_ptr, d_out_conn, n, -1, true);
+            UV(), CV(), d_g, d_out_ptr, d_out_conn, n, -1);
         detail::k_bwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, 0, n, -1);
       }
       cuda_check(cudaGetLastError(), "backward pass");
+      EndDevice(true, true);
     }
   }
 
   void DoResetGlobalState() {
     if constexpr (!std::is_same_v<typename Traits::ResetGlobal, NoResetGlobalState>) {
-      SyncToDevice();
+      BeginDevice();
       detail::k_reset<Traits><<<1, 1, 0, Stream>>>(d_g);
       cuda_check(cudaGetLastError(), "reset");
     }
@@ -799,146 +630,92 @@ template <typename Traits> class Network {
 
   void DoUpdateUnitState() {
     if constexpr (!std::is_same_v<typename Traits::UpdateUnit, NoUpdateUnit>) {
-      SyncToDevice();
-      detail::k_update_unit<Traits><<<detail::blocks(UA.Size()), 256, 0, Stream>>>(UV(), d_g,
-                                                                                  UA.Size());
+      BeginDevice();
+      constexpr bool seq = !detail::read_only_globals<Traits>();
+      const size_t n = UA.Size();
+      detail::k_update_unit<Traits><<<seq ? 1 : detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, n,
+                                                                                    seq);
       cuda_check(cudaGetLastError(), "unit update");
+      EndDevice(true, false);
     }
   }
 
   void DoUpdateConnectionState() {
     if constexpr (!std::is_same_v<typename Traits::UpdateConn, NoUpdateConn>) {
-      SyncToDevice();
-      constexpr bool seq = detail::SequentialUpdate<Traits>::value;
+      BeginDevice();
+      constexpr bool seq = detail::sequential_conn_update<Traits>();
       const size_t n = CA.Size();
       const unsigned grid = seq ? 1 : std::min<unsigned>(detail::blocks(n), 4096);
       detail::k_update_conn<Traits, true><<<grid, 256, 0, Stream>>>(UV(), CV(), d_g, n, seq);
       detail::k_update_conn<Traits, false><<<grid, 256, 0, Stream>>>(UV(), CV(), d_g, n, seq);
       cuda_check(cudaGetLastError(), "connection update");
+      EndDevice(true, true);
     }
   }
 
   void DoPruneUnits() {
     if constexpr (!std::is_same_v<typename Traits::PruneUnit, NoPruneUnit>) {
-      SyncToDevice();
       const size_t n = UA.Size();
-      detail::k_prune_units<Traits><<<kSeq ? 1 : detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, n,
-                                                                                     kSeq);
-      cuda_check(cudaGetLastError(), "prune units");
+      if constexpr (detail::device_structure<Traits>()) {
+        BeginDevice();
+        detail::k_prune_units<Traits><<<kSeq ? 1 : detail::blocks(n), 256, 0, Stream>>>(
+            UV(), d_g, n, kSeq);
+        cuda_check(cudaGetLastError(), "prune units");
+        EndDevice(true, false);
+      } else {
+        // The reference's loop (plastix.hpp:257-267) on the host copy.
+        PullGlobals();
+        for (size_t I = 0; I < n; ++I)
+          GetField<PrunedTag>(UA, I) = Traits::PruneUnit::ShouldPrune(UA, I, HostG);
+        PushGlobals();
+      }
     }
   }
 
   void DoPruneConnections() {
     if constexpr (!std::is_same_v<typename Traits::PruneUnit, NoPruneUnit> ||
                   !std::is_same_v<typename Traits::PruneConn, NoPruneConn>) {
-      SyncToDevice();
+      BeginDevice();
       const size_t m = CA.Size();
       const unsigned grid = kSeq ? 1 : std::min<unsigned>(detail::blocks(m), 4096);
       detail::k_prune_conns<Traits><<<grid, 256, 0, Stream>>>(UV(), CV(), d_g, m, kSeq);
       cuda_check(cudaGetLastError(), "prune connections");
+      EndDevice(false, true);
     }
   }
 
-  void DoAddUnits() {}
+  // DoAddUnits (reference plastix.hpp:300-319) on the host copy: units are
+  // allocated and initialised by the policy there, then uploaded (with every
+  // unit field) before the next device step.
+  void DoAddUnits() {
+    if constexpr (!std::is_same_v<typename Traits::AddUnit, NoAddUnit>) {
+      using AP = typename Traits::AddUnit;
+      PullGlobals();
+      const size_t N = UA.Size();
+      for (size_t I = 0; I < N; ++I) {
+        const std::optional<int16_t> Offset = AP::AddUnit(UA, I, HostG);
+        if (!Offset.has_value()) continue;
+        const int32_t Base = GetLevel(UA, I);
+        const int32_t NewLevel = std::clamp(Base + static_cast<int32_t>(*Offset), int32_t{1},
+                                            static_cast<int32_t>(MaxLevels - 1));
+        const size_t NewId = UA.Allocate();
+        if (NewId == static_cast<size_t>(-1)) break;
+        GetLevel(UA, NewId) = static_cast<uint16_t>(NewLevel);
+        AP::InitUnit(UA, NewId, I, HostG);
+      }
+      PushGlobals();
+    }
+  }
 
   // DoAddConnections (reference plastix.hpp:320-435): units bucketed by level
-  // (phase 0), the level-pair window enumerated on the device in the
-  // reference's order (phase 1), sort + unique commit (phases 2-3) through the
-  // C ABI, new connections appended and initialised by InitConnection.
+  // (phase 0), the level-pair window enumerated in the reference's order
+  // (phase 1) -- on the device with DeviceStructure, else on the host copy --,
+  // then the proposals sorted and deduplicated on the device (phases 2-3) and
+  // committed in that order through InitConnection.
   void DoAddConnections() {
     if constexpr (!std::is_same_v<typename Traits::AddConn, NoAddConn>) {
-      SyncToDevice();
-      const size_t n = UA.Size();
-      if (n == 0) return;
-      plx_ctx *ctx = PlxCtx();
-      // phase 0: units by level (stable by id), level offsets
-      uint32_t *hist = Buf<uint32_t>(0, 65536);
-      cuda_check(cudaMemsetAsync(hist, 0, 65536 * sizeof(uint32_t), Stream), "histogram");
-      detail::k_level_hist<<<detail::blocks(n), 256, 0, Stream>>>(LevelPtr(), n, hist);
-      std::vector<uint32_t> h(65536);
-      cuda_check(cudaMemcpyAsync(h.data(), hist, h.size() * 4, cudaMemcpyDeviceToHost, Stream),
-                 "histogram");
-      cuda_check(cudaStreamSynchronize(Stream), "histogram");
-      uint32_t highest = 0;
-      for (uint32_t L = 0; L < 65536; ++L)
-        if (h[L]) highest = L;
-      std::vector<uint32_t> off(highest + 2, 0);
-      for (uint32_t L = 0; L <= highest; ++L) off[L + 1] = off[L] + h[L];
-      uint32_t *keys = Buf<uint32_t>(1, n), *keys_out = Buf<uint32_t>(2, n);
-      uint32_t *ubl = Buf<uint32_t>(3, n);
-      detail::k_widen_u16<<<detail::blocks(n), 256, 0, Stream>>>(LevelPtr(), n, keys);
-      RadixSort(n, keys, keys_out, ubl, 16);
-      // phase 1: the level pairs of the window, in the reference's order
-      std::vector<detail::LevelPair> pairs;
-      uint64_t total = 0;
-      auto add = [&](uint32_t La, uint32_t Lb) {
-        const uint32_t na = off[La + 1] - off[La], nb = off[Lb + 1] - off[Lb];
-        if (!na || !nb) return;
-        pairs.push_back({total, off[La], na, off[Lb], nb, La == Lb ? 1u : 0u});
-        total += (uint64_t)na * nb;
-      };
-      constexpr uint32_t N = Traits::Neighbourhood;
-      const uint32_t init_right = std::min<uint32_t>(N, highest);
-      for (uint32_t La = 0; La <= init_right; ++La)
-        for (uint32_t Lb = La; Lb <= init_right; ++Lb) add(La, Lb);
-      for (uint32_t R = N + 1; R <= highest; ++R)
-        for (uint32_t W = R - N; W <= R; ++W) add(W, R);
-      if (total == 0) return;
-      auto *d_pairs = Buf<detail::LevelPair>(4, pairs.size());
-      cuda_check(cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(detail::LevelPair),
-                                 cudaMemcpyHostToDevice, Stream),
-                 "level pairs");
-      const uint32_t np = (uint32_t)pairs.size();
-      uint64_t n_props = 0;
-      uint64_t *props = nullptr;
-      if constexpr (kSeq) {
-        const uint64_t cap = std::min<uint64_t>(ProposalCap, 4 * total);
-        props = Buf<uint64_t>(5, cap);
-        uint64_t *cnt = Buf<uint64_t>(6, 1);
-        detail::k_propose_seq<Traits><<<1, 1, 0, Stream>>>(UV(), d_g, d_pairs, np, ubl, cap, props,
-                                                           cnt);
-        cuda_check(cudaMemcpyAsync(&n_props, cnt, 8, cudaMemcpyDeviceToHost, Stream), "count");
-        cuda_check(cudaStreamSynchronize(Stream), "proposals");
-      } else {
-        const uint64_t n_chunks = (total + detail::kPropChunk - 1) / detail::kPropChunk;
-        uint64_t *counts = Buf<uint64_t>(6, n_chunks + 1), *coff = Buf<uint64_t>(7, n_chunks + 1);
-        const unsigned grid = (unsigned)std::min<uint64_t>(n_chunks, 8192);
-        detail::k_propose<Traits, false><<<grid, 256, 0, Stream>>>(
-            UV(), d_g, d_pairs, np, ubl, total, n_chunks, counts, nullptr, 0, nullptr);
-        cuda_check(cudaMemsetAsync(counts + n_chunks, 0, 8, Stream), "counts");
-        size_t tb = 0;
-        cuda_check(cub::DeviceScan::ExclusiveSum(nullptr, tb, counts, coff, n_chunks + 1, Stream),
-                   "scan");
-        void *tmp = Buf<uint8_t>(8, tb);
-        cuda_check(cub::DeviceScan::ExclusiveSum(tmp, tb, counts, coff, n_chunks + 1, Stream),
-                   "scan");
-        cuda_check(cudaMemcpyAsync(&n_props, coff + n_chunks, 8, cudaMemcpyDeviceToHost, Stream),
-                   "count");
-        cuda_check(cudaStreamSynchronize(Stream), "proposals");
-        n_props = std::min<uint64_t>(n_props, ProposalCap);
-        if (n_props == 0) return;
-        props = Buf<uint64_t>(5, n_props);
-        detail::k_propose<Traits, true><<<grid, 256, 0, Stream>>>(
-            UV(), d_g, d_pairs, np, ubl, total, n_chunks, nullptr, coff, n_props, props);
-      }
-      cuda_check(cudaGetLastError(), "proposals");
-      if (n_props == 0) return;
-      // phases 2-3: sorted unique proposals, committed in that order
-      uint64_t *uniq = Buf<uint64_t>(9, n_props), *ucnt = Buf<uint64_t>(10, 1);
-      const size_t sb = plx_sort_unique_u64_scratch_bytes(n_props);
-      plx_check(plx_sort_unique_u64(ctx, n_props, props, uniq, ucnt, Buf<uint8_t>(11, sb), sb),
-                "plx_sort_unique_u64");
-      uint64_t k = 0;
-      cuda_check(cudaMemcpyAsync(&k, ucnt, 8, cudaMemcpyDeviceToHost, Stream), "unique");
-      cuda_check(cudaStreamSynchronize(Stream), "unique");
-      if (k == 0) return;
-      const size_t m0 = CA.Size();
-      GrowConnections(k);
-      detail::k_commit_conns<Traits><<<kSeq ? 1 : detail::blocks(k), 256, 0, Stream>>>(
-          UV(), CV(), d_g, uniq, k, m0, kSeq);
-      cuda_check(cudaGetLastError(), "commit");
-      NeedsResort = Traits::Model == Propagation::Topological;
-      IndexStale = true;
+      if constexpr (detail::device_structure<Traits>()) AddConnectionsOnDevice();
+      else AddConnectionsOnHost();
     }
   }
 
@@ -953,44 +730,46 @@ template <typename Traits> class Network {
     DoAddUnits();
     DoAddConnections();
     if constexpr (Traits::Model == Propagation::Topological)
-      if (NeedsResort) SortConnectionsByLevel();
+      if (NeedsResort) {
+        BeginDevice();
+        SortConnectionsByLevel();
+        EndDevice(true, true);
+      }
     DoResetGlobalState();
   }
 
   // Activations of the output units (waits for the device).
-  std::span<const float> GetOutput() {
+  std::span<const float> GetOutput() const {
+    const uint64_t act = uint64_t(1) << core::kActivation;
+    if (!(UA.StaleMask() & act)) {  // the host copy is current
+      const float *p = static_cast<const float *>(UA.field_data(core::kActivation));
+      return {p + OutputRange.Begin, OutputRange.Size()};
+    }
     Output.resize(OutputRange.Size());
-    cuda_check(cudaMemcpyAsync(Output.data(), static_cast<float *>(d_uf[0]) + OutputRange.Begin,
-                               Output.size() * sizeof(float), cudaMemcpyDeviceToHost, Stream),
-               "output");
+    if (!Output.empty())
+      cuda_check(cudaMemcpyAsync(Output.data(),
+                                 static_cast<const float *>(d_uf[core::kActivation]) +
+                                     OutputRange.Begin,
+                                 Output.size() * sizeof(float), cudaMemcpyDeviceToHost, Stream),
+                 "output");
     cuda_check(cudaStreamSynchronize(Stream), "output");
     return {Output.data(), Output.size()};
   }
 
-  // Host copies: downloaded unless the host copy already holds edits not yet
-  // uploaded (no Do* call since the last access); edits are uploaded before
-  // the next Do* call.
-  UnitAllocator &GetUnitAlloc() {
-    if (!UnitDirty) Download(UA, d_uf);
-    UnitDirty = true;
-    return UA;
-  }
-  ConnAllocator &GetConnAlloc() {
-    if (!ConnDirty) Download(CA, d_cf);
-    ConnDirty = true;
-    return CA;
-  }
+  // The coherent host copies (see the header comment).
+  UnitAllocator &GetUnitAlloc() { return UA; }
+  ConnAllocator &GetConnAlloc() { return CA; }
+
   GlobalState GetGlobals() {
-    GlobalState g;
-    cuda_check(cudaMemcpyAsync(&g, d_g, sizeof(g), cudaMemcpyDeviceToHost, Stream), "globals");
-    cuda_check(cudaStreamSynchronize(Stream), "globals");
-    return g;
+    PullGlobals();
+    return HostG;
   }
   void SetGlobals(const GlobalState &g) {
-    cuda_check(cudaMemcpyAsync(d_g, &g, sizeof(g), cudaMemcpyHostToDevice, Stream), "globals");
-    cuda_check(cudaStreamSynchronize(Stream), "globals");
+    HostG = g;
+    PushGlobals();
   }
   void SetStream(cudaStream_t s) {
+    cuda_check(cudaStreamSynchronize(Stream), "stream");
     Stream = s;
     if (Ctx) plx_check(plx_ctx_set_stream(Ctx, s), "plx_ctx_set_stream");
   }
@@ -1005,10 +784,9 @@ template <typename Traits> class Network {
   // state. Load replaces this network's state with the file's; the traits
   // (field schema and global state) must be the ones that wrote it.
   void Save(const std::string &Path) {
-    SyncToDevice();
-    Download(UA, d_uf);
-    Download(CA, d_cf);
-    const GlobalState G = GetGlobals();
+    UA.FetchAll();
+    CA.FetchAll();
+    PullGlobals();
     CheckpointHeader H = Header();
     FILE *F = std::fopen(Path.c_str(), "wb");
     if (!F) throw std::runtime_error("cannot write " + Path);
@@ -1018,7 +796,7 @@ template <typename Traits> class Network {
       ok = WriteAll(F, UA.field_data(i), UA.Size() * UnitAllocator::field_bytes(i));
     for (size_t i = 0; ok && i < ConnAllocator::NumFields; ++i)
       ok = WriteAll(F, CA.field_data(i), CA.Size() * ConnAllocator::field_bytes(i));
-    ok = ok && WriteAll(F, &G, sizeof(G));
+    ok = ok && WriteAll(F, &HostG, sizeof(HostG));
     ok = (std::fclose(F) == 0) && ok;
     if (!ok) throw std::runtime_error("short write to " + Path);
   }
@@ -1050,22 +828,24 @@ template <typename Traits> class Network {
     GlobalState G{};
     if (!ReadAll(F, &G, sizeof(G))) fail("truncated global state");
     std::fclose(F);
-    for (void *p : d_uf) cudaFree(p);
-    for (void *p : d_cf) cudaFree(p);
-    UploadAlloc(UA, d_uf, true);
-    UploadAlloc(CA, d_cf, true);
+    // The host copies now hold the whole state: nothing is stale, everything
+    // goes to the device (re-allocated at the loaded sizes).
+    UA.ClearAllStale();
+    CA.ClearAllStale();
+    ForceUpload();
     SetGlobals(G);
     NumInput = H.NumInput;
     OutputRange = UnitRange(H.OutBegin, H.OutEnd);
     Step = H.Step;
     NumLevels = H.NumLevels;
     NeedsResort = (H.Flags & 1u) != 0;
-    UnitDirty = ConnDirty = false;
-    RebuildIndex();
+    BeginDevice();
+    if constexpr (Traits::Model == Propagation::Topological) ComputeLevelRanges();
   }
 
  private:
-  static constexpr bool kSeq = detail::SequentialStructure<Traits>::value;
+  static constexpr bool kSeq = detail::sequential_structure<Traits>();
+  static constexpr size_t kCapacity = size_t(1) << 40;
 
   struct CheckpointHeader {
     char Magic[8];
@@ -1076,7 +856,7 @@ template <typename Traits> class Network {
   };
   CheckpointHeader Header() const {
     CheckpointHeader H{};
-    std::memcpy(H.Magic, "PLXCKPT1", 8);
+    std::memcpy(H.Magic, "PLXCKPT2", 8);
     H.NumInput = NumInput;
     H.Step = Step;
     H.Units = UA.Size();
@@ -1151,19 +931,108 @@ template <typename Traits> class Network {
     v.size = CA.Size();
     return v;
   }
-  // Field positions of the core schema (detail::UnitAllocT / ConnAllocT).
-  uint16_t *LevelPtr() const { return static_cast<uint16_t *>(d_uf[4]); }
-  uint32_t *FromPtr() const { return static_cast<uint32_t *>(d_cf[0]); }
-  uint32_t *ToPtr() const { return static_cast<uint32_t *>(d_cf[1]); }
-  uint8_t *DeadPtr() const { return static_cast<uint8_t *>(d_cf[2]); }
-  uint16_t *SrcLevelPtr() const { return static_cast<uint16_t *>(d_cf[3]); }
+  uint16_t *LevelPtr() const { return static_cast<uint16_t *>(d_uf[core::kLevel]); }
+  uint32_t *FromPtr() const { return static_cast<uint32_t *>(d_cf[core::kFromId]); }
+  uint32_t *ToPtr() const { return static_cast<uint32_t *>(d_cf[core::kToId]); }
+  uint8_t *DeadPtr() const { return static_cast<uint8_t *>(d_cf[core::kDead]); }
+  uint16_t *SrcLevelPtr() const { return static_cast<uint16_t *>(d_cf[core::kSrcLevel]); }
+
+  // ---- coherence of the host copies ---------------------------------------
+  static void FetchUnitField(void *owner, size_t I) {
+    auto *N = static_cast<Network *>(owner);
+    N->DownloadField(N->UA, N->d_uf, N->DevUnits, I);
+  }
+  static void FetchConnField(void *owner, size_t I) {
+    auto *N = static_cast<Network *>(owner);
+    N->DownloadField(N->CA, N->d_cf, N->DevConns, I);
+  }
+  template <class A>
+  void DownloadField(A &a, const std::vector<void *> &d, size_t dev_count, size_t I) {
+    cuda_check(cudaStreamSynchronize(Stream), "download");
+    if (dev_count == static_cast<size_t>(-1)) return;  // no device copy yet
+    const size_t k = std::min(a.Size(), dev_count);
+    if (k)
+      cuda_check(cudaMemcpy(a.field_data(I), d[I], k * A::field_bytes(I), cudaMemcpyDeviceToHost),
+                 "field download");
+  }
+  // Brings the device copies up to date with the host: fields the host
+  // touched are uploaded; when the host changed the number of entities
+  // (AddUnit, host-side AddConn, Load) the device arrays are re-made from
+  // the (completed) host copy.
+  template <class A>
+  bool SyncAlloc(A &a, std::vector<void *> &d, size_t &dev_count) {
+    const size_t n = a.Size();
+    bool changed = false;
+    if (n != dev_count || d.empty()) {
+      a.FetchAll();
+      cuda_check(cudaStreamSynchronize(Stream), "resize");
+      for (void *p : d) cudaFree(p);
+      d.assign(A::NumFields, nullptr);
+      for (size_t i = 0; i < A::NumFields; ++i) {
+        cuda_check(cudaMalloc(&d[i], std::max<size_t>(1, n) * A::field_bytes(i)), "field");
+        if (n)
+          cuda_check(cudaMemcpy(d[i], a.field_data(i), n * A::field_bytes(i),
+                                cudaMemcpyHostToDevice),
+                     "field upload");
+      }
+      dev_count = n;
+      a.ClearDirty();
+      return true;
+    }
+    const uint64_t dirty = a.DirtyMask();
+    if (dirty) {
+      for (size_t i = 0; i < A::NumFields; ++i)
+        if (((dirty >> i) & 1u) && n)
+          cuda_check(cudaMemcpyAsync(d[i], a.field_data(i), n * A::field_bytes(i),
+                                     cudaMemcpyHostToDevice, Stream),
+                     "field upload");
+      // pageable host memory: the copies are staged before the calls return
+      a.ClearDirty();
+      changed = true;
+    }
+    return changed;
+  }
+  // Called before device work: host edits reach the device, and an edit of
+  // the connection topology invalidates the connection index.
+  void BeginDevice() {
+    const uint64_t cdirty = CA.DirtyMask();
+    const bool units_resized = UA.Size() != DevUnits;
+    const bool conns_resized = CA.Size() != DevConns;
+    SyncAlloc(UA, d_uf, DevUnits);
+    SyncAlloc(CA, d_cf, DevConns);
+    constexpr uint64_t topo_fields = (uint64_t(1) << core::kFromId) | (uint64_t(1) << core::kToId) |
+                                     (uint64_t(1) << core::kDead) |
+                                     (uint64_t(1) << core::kSrcLevel);
+    if (units_resized || conns_resized || (cdirty & topo_fields)) IndexStale = true;
+  }
+  // Called after device work that may have changed the unit / connection
+  // fields: the host copies of those fields are stale.
+  void EndDevice(bool units, bool conns) {
+    if (units) UA.MarkStale(UnitAllocator::AllFields());
+    if (conns) CA.MarkStale(ConnAllocator::AllFields());
+  }
+  void ForceUpload() {
+    DevUnits = DevConns = static_cast<size_t>(-1);
+    IndexStale = true;
+  }
+  void PullGlobals() {
+    cuda_check(cudaMemcpyAsync(&HostG, d_g, sizeof(GlobalState), cudaMemcpyDeviceToHost, Stream),
+               "globals");
+    cuda_check(cudaStreamSynchronize(Stream), "globals");
+  }
+  void PushGlobals() {
+    cuda_check(cudaMemcpyAsync(d_g, &HostG, sizeof(GlobalState), cudaMemcpyHostToDevice, Stream),
+               "globals");
+    cuda_check(cudaStreamSynchronize(Stream), "globals");
+  }
+
+  // ---- levels, index ---------------------------------------------------------
 
   // SortConnectionsByLevel (reference plastix.hpp:539-579) on the device:
   // RecomputeLevels, SrcLevel = Level[FromId], stable radix sort on the
   // 16-bit key, Gather of every connection field; NumLevels = highest
-  // SrcLevel + 1.
+  // SrcLevel + 1, level ranges for the one-thread passes.
   void SortConnectionsByLevel() {
-    SyncToDevice();
     const size_t n = UA.Size(), m = CA.Size();
     plx_ctx *ctx = PlxCtx();
     const size_t lb = plx_recompute_levels_scratch_bytes(n, m);
@@ -1171,8 +1040,10 @@ template <typename Traits> class Network {
                                    DeadPtr(), LevelPtr(), nullptr, Buf<uint8_t>(13, lb), lb),
               "plx_recompute_levels");
     NeedsResort = false;
+    UA.MarkStale(uint64_t(1) << core::kLevel);
     if (m == 0) {
       NumLevels = 0;
+      ComputeLevelRanges();
       return;
     }
     plx_check(plx_src_levels(ctx, m, FromPtr(), LevelPtr(), (uint32_t)n, SrcLevelPtr()),
@@ -1199,8 +1070,26 @@ template <typename Traits> class Network {
       cudaFree(d_cf[i]);
       d_cf[i] = fresh[i];
     }
+    CA.MarkStale(ConnAllocator::AllFields());
     NumLevels = (int)(last & 0xFFFFu) + 1;
     IndexStale = true;
+    ComputeLevelRanges();
+  }
+
+  // ranges[L] (L in [0, NumLevels + 2)) = first connection whose SrcLevel is
+  // >= L, from the sorted SrcLevel keys (the reference's Ranges table).
+  void ComputeLevelRanges() {
+    const int nr = NumLevels + 2;
+    d_ranges = Buf<uint32_t>(14, nr);
+    const size_t m = CA.Size();
+    if (m == 0 || NumLevels == 0) {
+      cuda_check(cudaMemsetAsync(d_ranges, 0, nr * sizeof(uint32_t), Stream), "ranges");
+      return;
+    }
+    uint32_t *keys = Buf<uint32_t>(1, m);
+    detail::k_widen_u16<<<detail::blocks(m), 256, 0, Stream>>>(SrcLevelPtr(), m, keys);
+    detail::k_level_ranges<<<(nr + 255) / 256, 256, 0, Stream>>>(keys, m, d_ranges, nr);
+    cuda_check(cudaGetLastError(), "ranges");
   }
 
   // Incoming connection lists per destination (stored order) and outgoing per
@@ -1208,6 +1097,7 @@ template <typename Traits> class Network {
   // of ToId and FromId, row offsets from the sorted keys.
   void RebuildIndex() {
     const size_t n = UA.Size(), m = CA.Size();
+    cuda_check(cudaStreamSynchronize(Stream), "index");
     for (uint32_t *p : {d_in_ptr, d_out_ptr, d_in_conn, d_out_conn, d_cursor})
       if (p) cudaFree(p);
     cuda_check(cudaMalloc(&d_in_ptr, (n + 1) * 4), "index");
@@ -1230,7 +1120,186 @@ template <typename Traits> class Network {
     plx_check(plx_csr_row_ptr(ctx, keys_out, m, 0, (uint32_t)n, d_out_ptr), "plx_csr_row_ptr");
   }
 
-  // Appends k zeroed connections (device arrays and the host copy's size).
+  // ---- DoAddConnections ----------------------------------------------------
+
+  // The level-pair window of phase 1 in the reference's order: the initial
+  // window [0, min(N, highest)] as pairs La <= Lb, then each new right level
+  // R with every level of [R - N, R].
+  template <class F> static void ForEachLevelPair(uint32_t highest, F &&f) {
+    constexpr uint32_t N = Traits::Neighbourhood;
+    const uint32_t init_right = std::min<uint32_t>(N, highest);
+    for (uint32_t La = 0; La <= init_right; ++La)
+      for (uint32_t Lb = La; Lb <= init_right; ++Lb) f(La, Lb);
+    for (uint32_t R = N + 1; R <= highest; ++R)
+      for (uint32_t W = R - N; W <= R; ++W) f(W, R);
+  }
+
+  // Sorts and deduplicates `n_props` proposals (device) and returns the
+  // unique ones in ascending CompactEdge order (device, `k` entries).
+  uint64_t *SortUnique(uint64_t *props, uint64_t n_props, uint64_t &k) {
+    uint64_t *uniq = Buf<uint64_t>(9, n_props), *ucnt = Buf<uint64_t>(10, 1);
+    const size_t sb = plx_sort_unique_u64_scratch_bytes(n_props);
+    plx_check(plx_sort_unique_u64(PlxCtx(), n_props, props, uniq, ucnt, Buf<uint8_t>(11, sb), sb),
+              "plx_sort_unique_u64");
+    cuda_check(cudaMemcpyAsync(&k, ucnt, 8, cudaMemcpyDeviceToHost, Stream), "unique");
+    cuda_check(cudaStreamSynchronize(Stream), "unique");
+    return uniq;
+  }
+
+  // Phase 0 and 1 on the host copy with the host global state, exactly the
+  // reference's loops (predicates may use host-only facilities); phases 2-3
+  // sort and deduplicate on the device; the commit runs InitConnection on
+  // the host copy, and the new connections are uploaded before the next
+  // device step.
+  void AddConnectionsOnHost() {
+    using AC = typename Traits::AddConn;
+    const size_t n = UA.Size();
+    if (n == 0) return;
+    PullGlobals();
+    std::vector<uint32_t> off;
+    uint32_t highest = 0;
+    for (size_t I = 0; I < n; ++I) highest = std::max<uint32_t>(highest, GetLevel(UA, I));
+    off.assign(highest + 2, 0);
+    for (size_t I = 0; I < n; ++I) ++off[GetLevel(UA, I) + 1];
+    for (uint32_t L = 0; L <= highest; ++L) off[L + 1] += off[L];
+    std::vector<uint32_t> ubl(n), pos(off.begin(), off.end() - 1);
+    for (size_t I = 0; I < n; ++I) ubl[pos[GetLevel(UA, I)]++] = (uint32_t)I;
+    std::vector<uint64_t> props;
+    const uint64_t cap = ProposalCap;
+    ForEachLevelPair(highest, [&](uint32_t La, uint32_t Lb) {
+      for (uint32_t Ai = off[La]; Ai < off[La + 1]; ++Ai) {
+        const uint32_t U = ubl[Ai];
+        for (uint32_t Bi = off[Lb]; Bi < off[Lb + 1]; ++Bi) {
+          const uint32_t V = ubl[Bi];
+          if (U == V) continue;
+          if (props.size() < cap && AC::ShouldAddIncomingConnection(UA, U, V, HostG))
+            props.push_back(CompactEdge(V, U).Bits);
+          if (props.size() < cap && AC::ShouldAddOutgoingConnection(UA, U, V, HostG))
+            props.push_back(CompactEdge(U, V).Bits);
+          if (La != Lb) {
+            if (props.size() < cap && AC::ShouldAddIncomingConnection(UA, V, U, HostG))
+              props.push_back(CompactEdge(U, V).Bits);
+            if (props.size() < cap && AC::ShouldAddOutgoingConnection(UA, V, U, HostG))
+              props.push_back(CompactEdge(V, U).Bits);
+          }
+        }
+      }
+    });
+    if (props.empty()) {
+      PushGlobals();
+      return;
+    }
+    uint64_t *d_props = Buf<uint64_t>(5, props.size());
+    cuda_check(cudaMemcpyAsync(d_props, props.data(), props.size() * 8, cudaMemcpyHostToDevice,
+                               Stream),
+               "proposals");
+    uint64_t k = 0;
+    const uint64_t *uniq = SortUnique(d_props, props.size(), k);
+    std::vector<uint64_t> edges(k);
+    if (k)
+      cuda_check(cudaMemcpy(edges.data(), uniq, k * 8, cudaMemcpyDeviceToHost), "unique");
+    const size_t before = CA.Size();
+    for (const uint64_t b : edges) {
+      const CompactEdge E{(uint32_t)b, (uint32_t)(b >> 32)};
+      const size_t C = CA.Allocate();
+      if (C == static_cast<size_t>(-1)) break;
+      GetField<FromIdTag>(CA, C) = E.From();
+      GetField<ToIdTag>(CA, C) = E.To();
+      GetField<SrcLevelTag>(CA, C) = GetLevel(UA, E.From());
+      AC::InitConnection(UA, E.From(), E.To(), CA, C, HostG);
+    }
+    PushGlobals();
+    if (CA.Size() > before) {
+      NeedsResort = Traits::Model == Propagation::Topological;
+      IndexStale = true;
+    }
+  }
+
+  // Phases 0-1 on the device: level histogram + stable radix sort (units by
+  // level), the level-pair window, k_propose (count pass, per-chunk scan,
+  // ordered write pass) or k_propose_seq; then sort/unique and k_commit_conns.
+  void AddConnectionsOnDevice() {
+    BeginDevice();
+    const size_t n = UA.Size();
+    if (n == 0) return;
+    uint32_t *hist = Buf<uint32_t>(0, 65536);
+    cuda_check(cudaMemsetAsync(hist, 0, 65536 * sizeof(uint32_t), Stream), "histogram");
+    detail::k_level_hist<<<detail::blocks(n), 256, 0, Stream>>>(LevelPtr(), n, hist);
+    std::vector<uint32_t> h(65536);
+    cuda_check(cudaMemcpyAsync(h.data(), hist, h.size() * 4, cudaMemcpyDeviceToHost, Stream),
+               "histogram");
+    cuda_check(cudaStreamSynchronize(Stream), "histogram");
+    uint32_t highest = 0;
+    for (uint32_t L = 0; L < 65536; ++L)
+      if (h[L]) highest = L;
+    std::vector<uint32_t> off(highest + 2, 0);
+    for (uint32_t L = 0; L <= highest; ++L) off[L + 1] = off[L] + h[L];
+    uint32_t *keys = Buf<uint32_t>(1, n), *keys_out = Buf<uint32_t>(2, n);
+    uint32_t *ubl = Buf<uint32_t>(3, n);
+    detail::k_widen_u16<<<detail::blocks(n), 256, 0, Stream>>>(LevelPtr(), n, keys);
+    RadixSort(n, keys, keys_out, ubl, 16);
+    std::vector<detail::LevelPair> pairs;
+    uint64_t total = 0;
+    ForEachLevelPair(highest, [&](uint32_t La, uint32_t Lb) {
+      const uint32_t na = off[La + 1] - off[La], nb = off[Lb + 1] - off[Lb];
+      if (!na || !nb) return;
+      pairs.push_back({total, off[La], na, off[Lb], nb, La == Lb ? 1u : 0u});
+      total += (uint64_t)na * nb;
+    });
+    if (total == 0) return;
+    auto *d_pairs = Buf<detail::LevelPair>(4, pairs.size());
+    cuda_check(cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(detail::LevelPair),
+                               cudaMemcpyHostToDevice, Stream),
+               "level pairs");
+    const uint32_t np = (uint32_t)pairs.size();
+    uint64_t n_props = 0;
+    uint64_t *props = nullptr;
+    if constexpr (kSeq) {
+      const uint64_t cap = std::min<uint64_t>(ProposalCap, 4 * total);
+      props = Buf<uint64_t>(5, cap);
+      uint64_t *cnt = Buf<uint64_t>(6, 1);
+      detail::k_propose_seq<Traits><<<1, 1, 0, Stream>>>(UV(), d_g, d_pairs, np, ubl, cap, props,
+                                                         cnt);
+      cuda_check(cudaMemcpyAsync(&n_props, cnt, 8, cudaMemcpyDeviceToHost, Stream), "count");
+      cuda_check(cudaStreamSynchronize(Stream), "proposals");
+    } else {
+      const uint64_t n_chunks = (total + detail::kPropChunk - 1) / detail::kPropChunk;
+      uint64_t *counts = Buf<uint64_t>(6, n_chunks + 1), *coff = Buf<uint64_t>(7, n_chunks + 1);
+      const unsigned grid = (unsigned)std::min<uint64_t>(n_chunks, 8192);
+      detail::k_propose<Traits, false><<<grid, 256, 0, Stream>>>(
+          UV(), d_g, d_pairs, np, ubl, total, n_chunks, counts, nullptr, 0, nullptr);
+      cuda_check(cudaMemsetAsync(counts + n_chunks, 0, 8, Stream), "counts");
+      size_t tb = 0;
+      cuda_check(cub::DeviceScan::ExclusiveSum(nullptr, tb, counts, coff, n_chunks + 1, Stream),
+                 "scan");
+      void *tmp = Buf<uint8_t>(8, tb);
+      cuda_check(cub::DeviceScan::ExclusiveSum(tmp, tb, counts, coff, n_chunks + 1, Stream),
+                 "scan");
+      cuda_check(cudaMemcpyAsync(&n_props, coff + n_chunks, 8, cudaMemcpyDeviceToHost, Stream),
+                 "count");
+      cuda_check(cudaStreamSynchronize(Stream), "proposals");
+      n_props = std::min<uint64_t>(n_props, ProposalCap);
+      if (n_props == 0) return;
+      props = Buf<uint64_t>(5, n_props);
+      detail::k_propose<Traits, true><<<grid, 256, 0, Stream>>>(
+          UV(), d_g, d_pairs, np, ubl, total, n_chunks, nullptr, coff, n_props, props);
+    }
+    cuda_check(cudaGetLastError(), "proposals");
+    if (n_props == 0) return;
+    uint64_t k = 0;
+    const uint64_t *uniq = SortUnique(props, n_props, k);
+    if (k == 0) return;
+    const size_t m0 = CA.Size();
+    GrowConnections(k);
+    detail::k_commit_conns<Traits><<<kSeq ? 1 : detail::blocks(k), 256, 0, Stream>>>(
+        UV(), CV(), d_g, uniq, k, m0, kSeq);
+    cuda_check(cudaGetLastError(), "commit");
+    EndDevice(false, true);
+    NeedsResort = Traits::Model == Propagation::Topological;
+    IndexStale = true;
+  }
+
+  // Appends k zeroed connections (device arrays and the host copy's count).
   void GrowConnections(size_t k) {
     const size_t m = CA.Size();
     for (size_t i = 0; i < ConnAllocator::NumFields; ++i) {
@@ -1244,45 +1313,10 @@ template <typename Traits> class Network {
       cudaFree(d_cf[i]);
       d_cf[i] = p;
     }
-    for (size_t i = 0; i < k; ++i) CA.Allocate();
+    CA.AllocateMany(k);
+    DevConns = m + k;
   }
 
-  template <class A> void UploadAlloc(A &a, std::vector<void *> &d, bool alloc) {
-    if (alloc) d.assign(A::NumFields, nullptr);
-    for (size_t i = 0; i < A::NumFields; ++i) {
-      const size_t bytes = std::max<size_t>(1, a.Size()) * A::field_bytes(i);
-      if (alloc) cuda_check(cudaMalloc(&d[i], bytes), "field");
-      if (a.Size())
-        cuda_check(cudaMemcpy(d[i], a.field_data(i), a.Size() * A::field_bytes(i),
-                              cudaMemcpyHostToDevice),
-                   "field upload");
-    }
-  }
-  template <class A> void Download(A &a, std::vector<void *> &d) {
-    cuda_check(cudaStreamSynchronize(Stream), "download");
-    for (size_t i = 0; i < A::NumFields; ++i)
-      if (a.Size())
-        cuda_check(cudaMemcpy(a.field_data(i), d[i], a.Size() * A::field_bytes(i),
-                              cudaMemcpyDeviceToHost),
-                   "field download");
-  }
-  void Upload() {
-    UploadAlloc(UA, d_uf, true);
-    UploadAlloc(CA, d_cf, true);
-    cuda_check(cudaMalloc(&d_g, sizeof(GlobalState) > 0 ? sizeof(GlobalState) : 1), "globals");
-    GlobalState g{};
-    cuda_check(cudaMemcpy(d_g, &g, sizeof(GlobalState), cudaMemcpyHostToDevice), "globals");
-  }
-  void SyncToDevice() {
-    if (UnitDirty) {
-      UploadAlloc(UA, d_uf, false);
-      UnitDirty = false;
-    }
-    if (ConnDirty) {
-      UploadAlloc(CA, d_cf, false);
-      ConnDirty = false;
-    }
-  }
   void Release() {
     if (Stream) cudaStreamSynchronize(Stream);
     else cudaDeviceSynchronize();
@@ -1298,25 +1332,26 @@ template <typename Traits> class Network {
 
   size_t NumInput;
   UnitRange OutputRange;
-  UnitAllocator UA;
-  ConnAllocator CA;
+  mutable UnitAllocator UA;
+  mutable ConnAllocator CA;
+  GlobalState HostG{};
   int NumLevels = 0;
   size_t Step = 0;
   int Device = 0;
   std::vector<void *> d_uf, d_cf;
+  size_t DevUnits = static_cast<size_t>(-1), DevConns = static_cast<size_t>(-1);
   GlobalState *d_g = nullptr;
   uint32_t *d_in_ptr = nullptr, *d_out_ptr = nullptr, *d_in_conn = nullptr, *d_out_conn = nullptr;
-  uint32_t *d_cursor = nullptr;
+  uint32_t *d_cursor = nullptr, *d_ranges = nullptr;
   float *d_targets = nullptr;
   size_t TargetCap = 0;
-  bool UnitDirty = false, ConnDirty = false;
   bool NeedsResort = false, IndexStale = true;
   uint64_t ProposalCap = uint64_t(1) << 26;
   cudaStream_t Stream = nullptr;
   plx_ctx *Ctx = nullptr;
   void *Scratch[16] = {};
   size_t ScratchBytes[16] = {};
-  std::vector<float> Output;
+  mutable std::vector<float> Output;
 };
 
 }  // namespace plastix

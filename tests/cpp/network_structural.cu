@@ -1,8 +1,14 @@
 // Structural parity program: the pure prune / add-connection policies of
 // oracle/structural_policies.hpp on the device Network (Topological), the
 // same network and inputs as the reference run that made the fixture.
-// Usage: network_structural <variant 0|1> <n_in> <h1> <h2> <seed> <steps> <dir>
+// Usage: network_structural <variant> <n_in> <h1> <h2> <seed> <steps> <dir>
 //        [resume_at]
+// Variants 0 (small) and 1 (medium) use the traits as written: the global
+// state is not declared read-only, so the hooks that receive it run in one
+// device thread, and the structural decisions run on the host copy.
+// Variants 2 and 3 are the same networks with DeviceStructure and
+// ReadOnlyGlobalState: parallel passes, and pruning predicates and
+// connection proposals enumerated on the device.
 // Reads <dir>/inputs.bin (steps x n_in floats); writes outputs.bin and the
 // final connections (from, to, dead, src_level, w) and units (level, act).
 // With resume_at, the network is saved before that step and the run goes on
@@ -18,6 +24,11 @@
 #include <vector>
 
 namespace {
+
+template <class Base> struct OnDevice : Base {
+  static constexpr bool DeviceStructure = true;
+  static constexpr bool ReadOnlyGlobalState = true;  // only ResetGlobal writes it
+};
 
 template <class T> void put(const std::string &dir, const char *name, const std::vector<T> &v) {
   FILE *f = std::fopen((dir + "/" + name).c_str(), "wb");
@@ -90,9 +101,14 @@ int main(int argc, char **argv) {
   const uint32_t seed = std::atoi(argv[5]);
   const int steps = std::atoi(argv[6]);
   try {
-    return variant == 0
-               ? run<structural_test::SmallTraits>(n_in, h1, h2, seed, steps, argv[7], resume_at)
-               : run<structural_test::MediumTraits>(n_in, h1, h2, seed, steps, argv[7], resume_at);
+    using namespace structural_test;
+    switch (variant) {
+      case 0: return run<SmallTraits>(n_in, h1, h2, seed, steps, argv[7], resume_at);
+      case 1: return run<MediumTraits>(n_in, h1, h2, seed, steps, argv[7], resume_at);
+      case 2: return run<OnDevice<SmallTraits>>(n_in, h1, h2, seed, steps, argv[7], resume_at);
+      case 3: return run<OnDevice<MediumTraits>>(n_in, h1, h2, seed, steps, argv[7], resume_at);
+      default: return 1;
+    }
   } catch (const std::exception &e) {
     std::fprintf(stderr, "%s\n", e.what());
     return 4;

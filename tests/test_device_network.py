@@ -97,9 +97,10 @@ def test_device_network_swifttd_matches_reference(tmp_path):
     np.testing.assert_allclose(v["b"], z["fields"][9], rtol=1e-5, atol=1e-6)
 
 
-def _run_structural(tmp_path, name, resume_at=None):
+def _run_structural(tmp_path, name, resume_at=None, on_device=False):
     z = np.load(GOLDEN / "structural_net.npz")
     variant, n_in, h1, h2, seed, steps = (int(v) for v in z[f"{name}_params"])
+    variant += 2 if on_device else 0
     np.ascontiguousarray(z[f"{name}_inputs"], np.float32).tofile(tmp_path / "inputs.bin")
     exe = compile_prog("network_structural", tmp_path)
     args = [str(exe), str(variant), str(n_in), str(h1), str(h2), str(seed), str(steps),
@@ -113,13 +114,15 @@ def _run_structural(tmp_path, name, resume_at=None):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("on_device", [False, True], ids=["host-decisions", "device-decisions"])
 @pytest.mark.parametrize("resume_at", [None, 2, 4])
-def test_device_network_structural_small_matches_reference(tmp_path, resume_at):
+def test_device_network_structural_small_matches_reference(tmp_path, resume_at, on_device):
     """Two-way proposals (into input units, cycles), a unit pruned at step 2,
     weights pruned below 0.02: five steps, every array bit for bit -- also
     when the run is checkpointed before step `resume_at` and resumed in a
-    newly built network (Save / Load)."""
-    z, got = _run_structural(tmp_path, "small", resume_at)
+    newly built network (Save / Load); with the structural decisions made on
+    the host copy (the default) and on the device (DeviceStructure)."""
+    z, got = _run_structural(tmp_path, "small", resume_at, on_device)
     for k, v in got.items():
         want = z[f"small_{k}"].reshape(-1)
         assert v.size == want.size, k
@@ -127,13 +130,14 @@ def test_device_network_structural_small_matches_reference(tmp_path, resume_at):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("on_device", [False, True], ids=["host-decisions", "device-decisions"])
 @pytest.mark.parametrize("resume_at", [None, 1])
-def test_device_network_structural_medium_matches_reference(tmp_path, resume_at):
+def test_device_network_structural_medium_matches_reference(tmp_path, resume_at, on_device):
     """32 -> 200 -> 50 with forward proposals over ~60k unit pairs per step
-    (the parallel enumeration runs over many chunks): digests of every array,
-    straight through and resumed from a checkpoint."""
+    (on the device the parallel enumeration runs over many chunks): digests
+    of every array, straight through and resumed from a checkpoint."""
     import hashlib
-    z, got = _run_structural(tmp_path, "medium", resume_at)
+    z, got = _run_structural(tmp_path, "medium", resume_at, on_device)
     for k, v in got.items():
         assert v.size == int(z[f"medium_{k}_size"]), k
         assert hashlib.sha256(v.tobytes()).hexdigest() == str(z[f"medium_{k}_sha256"]), k
