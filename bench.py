@@ -54,17 +54,21 @@ def parse_args():
     p.add_argument("--handoff", choices=["p2p", "nccl"], default="p2p",
                    help="N > 1: hand the destination slices to every GPU with the sweep's "
                         "own stores over NVLink (p2p) or with an NCCL all-gather after it")
+    p.add_argument("--layout", choices=["sliced", "csr"], default="sliced",
+                   help="storage order of the swept layer: warp-sliced rows (one lane per "
+                        "row) or the destination-sorted CSR order")
     p.add_argument("--ipc-units", type=int, default=1 << 18,
                    help="units per layer of the ipc workload (2^18 in the configuration)")
     p.add_argument("--ipc-fan-in", type=int, default=2048)
     p.add_argument("--workload",
-                   choices=["sweep", "swifttd", "ipc", "structural", "ceiling", "levels"],
+                   choices=["sweep", "swifttd", "ipc", "structural", "ceiling", "levels", "api"],
                    default="sweep",
                    help="sweep: the single-layer fwd+Hebbian sweep (default, the headline); "
                         "swifttd: 4M-feature SwiftTD learner; ipc: 5-layer predictive-coding "
                         "net; structural: prune/regrow/re-sort/forward step; ceiling: the sweep "
                         "beside the same traffic without row folds and random gathers alone; "
-                        "levels: RecomputeLevels + SortConnectionsByLevel at 2^24 connections")
+                        "levels: RecomputeLevels + SortConnectionsByLevel at 2^24 connections; "
+                        "api: the sweep through plastix::Network<Traits>::DoStep")
     return p.parse_args()
 
 
@@ -264,7 +268,7 @@ def run_ours(args):
     g.manual_seed(args.seed)
     act_src = torch.rand(n_src_total, generator=g, device=device)  # replicated inputs
     del act_local
-    layer = HebbianSweepLayer(ctx, n_src_total, n_dst, from_id, to_id, w)
+    layer = HebbianSweepLayer(ctx, n_src_total, n_dst, from_id, to_id, w, layout=args.layout)
     del from_id, to_id, w
     gathered = torch.empty(n_dst * world, device=device) if world > 1 else None
     p2p = world > 1 and args.handoff == "p2p"
@@ -433,6 +437,7 @@ def run_ours(args):
         "dtype": "f32", "data": "synthetic (seeded torch generator on device)",
         "config": {"workload": WORKLOAD, "n_src": n_src_total, "n_dst_per_gpu": n_dst,
                    "n_edges_per_gpu": n_edges, "parallelism": f"dst-range shards x{world}",
+                   "layout": args.layout,
                    "l2": "inputs larger than L2: 1.36 GB of connection state streamed "
                          "per sweep vs 126 MB L2",
                    "handoff": ("destination slices stored by the sweep kernel into every "
@@ -441,7 +446,9 @@ def run_ours(args):
                                "sweep") if world > 1 else "none"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS hbm_gbs)",
-                     "traffic": traffic_per_launch("sweep_hebbian_64M"),
+                     "traffic": traffic_per_launch("sweep_hebbian_64M" if args.layout == "csr"
+                                                   else "sweep_hebbian_sliced_64M"),
+                     "kernel": "k_sweep_wtile" if args.layout == "csr" else "k_sweep_sliced",
                      "kernel_ms": kern_ms, "algorithmic_bytes_per_launch": algo_bytes},
         "handoff_ms": handoff_ms if world > 1 else None,
         "cpu_baseline": cpu,
@@ -953,11 +960,45 @@ def bench_levels(args):
     ctx.close()
 
 
+def bench_api(args):
+    """The single-layer sweep through the reference's C++ API: a
+    plastix::Network<Traits> with PLASTIX_HD Hebbian-trace policies
+    (plastix_b200/apps/network_sweep.cu), stepped with DoStep. Device time
+    per DoStep from CUDA events on the network's stream; e2e per step is
+    DoStep from a host input vector + GetOutput (host clock)."""
+    from plastix_b200 import build
+
+    exe = build.app_path("network_sweep")
+    if not exe.exists():
+        exe = build.build_app("network_sweep")
+    sampler = ClockSampler(0)
+    r = subprocess.run([str(exe), "bench", str(args.n_src), str(args.n_dst), str(args.n_edges),
+                        str(args.seed), str(args.steps), str(args.warmup)],
+                       capture_output=True, text=True, timeout=1800)
+    clocks = sampler.stop()
+    if r.returncode != 0:
+        raise SystemExit(f"network_sweep failed:\n{r.stdout}\n{r.stderr}")
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    n = args.n_edges
+    ms = d["device_ms_per_step"]
+    algo = 20 * n + 8 * args.n_dst + 4 * args.n_src
+    config = {"workload": "single sparse layer sweep through plastix::Network<Traits>::DoStep "
+                          "(PLASTIX_HD policies: identity forward, Hebbian trace update)",
+              "n_src": args.n_src, "n_dst": args.n_dst, "n_edges": n,
+              "l2": "inputs larger than L2", "build_s": d["build_s"]}
+    e2e = {"value": n / (d["e2e_ms_per_step"] / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": 4 * args.n_src, "d2h_bytes_per_step": 4 * args.n_dst}
+    _line(args, "api", n / (ms / 1e3), UNIT, ms, config, _roof(algo, ms, None), None, e2e,
+          clocks, None)
+    return 0
+
+
 def run_other(args):
     if args.gpus != 1 and args.workload not in ("ipc", "structural"):
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
     return {"swifttd": bench_swifttd, "ipc": bench_ipc, "structural": bench_structural,
-            "ceiling": bench_ceiling, "levels": bench_levels}[args.workload](args) or 0
+            "ceiling": bench_ceiling, "levels": bench_levels, "api": bench_api}[args.workload](
+                args) or 0
 
 
 def main():

@@ -19,9 +19,10 @@
 //     ReadOnlyGlobalState in traits.hpp) run every hook that receives it in
 //     one device thread, in the reference's order.
 //   * Pipeline networks whose connections are stored destination-major (as
-//     FullyConnected builds them) take a warp-tiled sweep: coalesced reads of
-//     the connection fields, one warp per tile of rows, each row still folded
-//     strictly left to right.
+//     FullyConnected builds them) take a warp-tiled forward accumulation:
+//     Map on consecutive connections per lane (coalesced reads of the
+//     connection fields), each unit's values still combined strictly in
+//     connection order.
 //   * GetUnitAlloc()/GetConnAlloc() return the network's host copies, kept
 //     coherent with the device: a field the device has changed is downloaded
 //     when the host reads it, and fields the host touched are uploaded before
@@ -134,6 +135,49 @@ __global__ void k_fwd_acc(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32
     acc = FP::Combine(acc, FP::Map(U, I, GetField<FromIdTag>(C, c), C, c, *g));
   }
   GetForwardAcc(U, I) = acc;
+}
+
+// Pipeline forward accumulation for connections stored destination-major
+// (ToId non-decreasing, as FullyConnected and destination-sorted builders
+// emit them): units in blocks of 32, one lane per unit; the block's
+// connections are evaluated 32 at a time with Map -- consecutive connections
+// on consecutive lanes, so connection fields are read coalesced --, staged in
+// shared memory, and each lane folds its unit's staged values with Combine
+// strictly in connection order (the same sequence as k_fwd_acc).
+constexpr uint32_t kTileChunk = 256;  // connections per staged chunk
+constexpr uint32_t kTileWarps = 8;
+template <class Tr, class UV, class CV, class G>
+__global__ void __launch_bounds__(kTileWarps * 32)
+    k_fwd_acc_tiled(UV U, CV C, G *g, const uint32_t *in_ptr, size_t n) {
+  using FP = typename Tr::ForwardPass;
+  using Acc = typename FP::Accumulator;
+  __shared__ __align__(16) unsigned char raw[kTileWarps][kTileChunk * sizeof(Acc)];
+  __shared__ bool live[kTileWarps][kTileChunk];
+  const uint32_t lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+  Acc *stage = reinterpret_cast<Acc *>(raw[w]);
+  for (size_t r0 = ((size_t)blockIdx.x * kTileWarps + w) * 32; r0 < n;
+       r0 += (size_t)gridDim.x * kTileWarps * 32) {
+    const size_t r = r0 + lane;
+    const size_t r_end = r0 + 32 < n ? r0 + 32 : n;
+    const uint32_t rs = r < n ? in_ptr[r] : 0u, re = r < n ? in_ptr[r + 1] : 0u;
+    const uint32_t c_lo = in_ptr[r0], c_hi = in_ptr[r_end];
+    Acc acc = r < n ? GetForwardAcc(U, r) : Acc{};
+    for (uint32_t c0 = c_lo; c0 < c_hi; c0 += kTileChunk) {
+      const uint32_t cn = c_hi - c0 < kTileChunk ? c_hi - c0 : kTileChunk;
+      for (uint32_t j = lane; j < cn; j += 32) {
+        const size_t c = (size_t)c0 + j;
+        const bool ok = !GetField<DeadTag>(C, c);
+        live[w][j] = ok;
+        if (ok) stage[j] = FP::Map(U, GetField<ToIdTag>(C, c), GetField<FromIdTag>(C, c), C, c, *g);
+      }
+      __syncwarp();
+      const uint32_t lo = rs > c0 ? rs : c0, hi = re < c0 + cn ? re : c0 + cn;
+      for (uint32_t c = lo; c < hi; ++c)
+        if (live[w][c - c0]) acc = FP::Combine(acc, stage[c - c0]);
+      __syncwarp();
+    }
+    if (r < n) GetForwardAcc(U, r) = acc;
+  }
 }
 
 // Topological forward accumulation of level L (reference plastix.hpp:111-119):
@@ -519,6 +563,7 @@ template <typename Traits> class Network {
     ((Prev = Layers(UA, CA, Prev)), ...);
     OutputRange = Prev;
     cuda_check(cudaGetDevice(&Device), "device");
+    cuda_check(cudaDeviceGetAttribute(&NumSMs, cudaDevAttrMultiProcessorCount, Device), "device");
     UA.Link({&Network::FetchUnitField, this});
     CA.Link({&Network::FetchConnField, this});
     cuda_check(cudaMalloc(&d_g, sizeof(GlobalState) > 0 ? sizeof(GlobalState) : 1), "globals");
@@ -565,8 +610,17 @@ template <typename Traits> class Network {
         detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, L);
       }
     } else {
-      detail::k_fwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), CV(), d_g, d_in_ptr,
-                                                                        d_in_conn, n);
+      using Acc = typename FP::Accumulator;
+      if (DstMajor && std::is_trivially_copyable_v<Acc> && sizeof(Acc) <= 16) {
+        const unsigned grid = (unsigned)std::min<size_t>(
+            std::max<size_t>(1, (n + 32 * detail::kTileWarps - 1) / (32 * detail::kTileWarps)),
+            (size_t)NumSMs * 8);
+        detail::k_fwd_acc_tiled<Traits><<<grid, detail::kTileWarps * 32, 0, Stream>>>(
+            UV(), CV(), d_g, d_in_ptr, n);
+      } else {
+        detail::k_fwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), CV(), d_g,
+                                                                          d_in_ptr, d_in_conn, n);
+      }
       detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, -1);
     }
     cuda_check(cudaGetLastError(), "forward pass");
@@ -1112,6 +1166,17 @@ template <typename Traits> class Network {
       return;
     }
     plx_ctx *ctx = PlxCtx();
+    // Destination-major storage (ToId non-decreasing) enables the tiled
+    // forward accumulation.
+    uint32_t *flag = Buf<uint32_t>(15, 1);
+    const uint32_t one = 1;
+    cuda_check(cudaMemcpyAsync(flag, &one, 4, cudaMemcpyHostToDevice, Stream), "index");
+    detail::k_check_dst_major<<<std::min<unsigned>(detail::blocks(m), 4096), 256, 0, Stream>>>(
+        ToPtr(), m, flag);
+    uint32_t dm = 0;
+    cuda_check(cudaMemcpyAsync(&dm, flag, 4, cudaMemcpyDeviceToHost, Stream), "index");
+    cuda_check(cudaStreamSynchronize(Stream), "index");
+    DstMajor = dm != 0;
     uint32_t *keys_out = Buf<uint32_t>(2, m);
     const uint32_t bits = BitsFor(n);
     RadixSort(m, ToPtr(), keys_out, d_in_conn, bits);
@@ -1345,7 +1410,8 @@ template <typename Traits> class Network {
   uint32_t *d_cursor = nullptr, *d_ranges = nullptr;
   float *d_targets = nullptr;
   size_t TargetCap = 0;
-  bool NeedsResort = false, IndexStale = true;
+  bool NeedsResort = false, IndexStale = true, DstMajor = false;
+  int NumSMs = 148;
   uint64_t ProposalCap = uint64_t(1) << 26;
   cudaStream_t Stream = nullptr;
   plx_ctx *Ctx = nullptr;

@@ -162,6 +162,66 @@ int plx_sweep_forward_hebbian(plx_ctx* ctx, const plx_csr* csr,
                               float* trace_out, float decay, float rate,
                               float* act_dst);
 
+/* ---- warp-sliced row layout (the fused sweep, one lane per row) ---------- */
+
+#define PLX_SLICED_NONE 0xFFFFFFFFu
+
+/* Connections of a destination-sorted CSR re-laid for a sweep in which one
+ * lane owns one row: rows are taken in windows of 512 consecutive rows,
+ * ordered by length inside each window (descending, stable) and dealt 32 at
+ * a time into slices. Slot slice_ptr[s] + 128*g + 4*l + c holds connection
+ * 4g + c of the row of lane l of slice s; shorter rows leave padding slots.
+ * Every connection field of a sliced layer is stored in slot order;
+ * perm[slot] is the slot's reference connection index (PLX_SLICED_NONE for
+ * padding). All arrays are device memory. */
+typedef struct plx_sliced {
+  const uint64_t* slice_ptr; /* [n_slices + 1] first slot of each slice       */
+  const uint32_t* lane_row;  /* [n_slices * 32] row of each lane (or NONE)    */
+  const uint32_t* lane_len;  /* [n_slices * 32] connections of that row       */
+  const uint32_t* perm;      /* [n_slots] reference index of each slot        */
+  uint64_t n_slots;
+  uint64_t n_edges;
+  uint32_t n_rows;
+  uint32_t n_slices; /* ceil(n_rows / 32) */
+} plx_sliced;
+
+uint32_t plx_sliced_n_slices(uint32_t n_rows);
+size_t plx_sliced_plan_scratch_bytes(uint32_t n_rows);
+
+/* Builds the slices of a CSR (row_ptr as from plx_csr_row_ptr) into the
+ * caller's arrays (slice_ptr: n_slices + 1 u64, lane_row / lane_len:
+ * n_slices * 32 u32) and fills *out, including n_slots (this call waits for
+ * the stream to read it back; allocate the slot arrays from it). perm is
+ * left NULL until plx_sliced_perm. Replaces nothing in the reference: it is
+ * the storage order of the sweep below. */
+int plx_sliced_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows, uint64_t n_edges,
+                    plx_sliced* out, uint64_t* slice_ptr, uint32_t* lane_row,
+                    uint32_t* lane_len, void* scratch, size_t scratch_bytes);
+/* perm[slot] (n_slots u32, 16-byte aligned) from the CSR; sets out->perm. */
+int plx_sliced_perm(plx_ctx* ctx, plx_sliced* sl, const uint32_t* row_ptr, uint32_t* perm);
+/* slot[i] = ref[perm[i]] (zero for padding) / ref[perm[i]] = slot[i], for
+ * one field of 1, 2, 4 or 8 bytes per element. */
+int plx_sliced_pack(plx_ctx* ctx, const plx_sliced* sl, const void* ref, void* slot,
+                    uint32_t elem_bytes);
+int plx_sliced_unpack(plx_ctx* ctx, const plx_sliced* sl, const void* slot, void* ref,
+                      uint32_t elem_bytes);
+
+/* plx_sweep_forward_hebbian (DoForwardPass, Pipeline, identity Apply, then
+ * the trace rule of DoUpdateConnectionState, plastix.hpp:133-148 and
+ * :238-245) over a sliced layer: from_id, dead (optional), weight and trace
+ * in slot order; weight and trace are updated in place. Every row is folded
+ * left to right by one lane, so row values, weights and traces equal the
+ * reference's bit for bit, whatever the row lengths. act_dst is indexed by
+ * row. With n_peers > 0 each row value is also stored to
+ * peer_out[p][peer_offset + r], as plx_sweep_forward_hebbian_gather (same
+ * peer_len check). */
+int plx_sweep_forward_hebbian_sliced(plx_ctx* ctx, const plx_sliced* sl, const uint32_t* from_id,
+                                     const uint8_t* dead, const float* act_src,
+                                     uint32_t act_src_len, float* weight, float* trace,
+                                     float decay, float rate, float* act_dst,
+                                     float* const* peer_out, uint32_t n_peers,
+                                     uint32_t peer_offset, uint32_t peer_len);
+
 /* ---- hand-off over peer memory (one process per GPU, NVLink) ------------ */
 
 #define PLX_MAX_PEERS 8

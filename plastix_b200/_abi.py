@@ -53,6 +53,15 @@ class Chunked(ctypes.Structure):
                 ("n_rows", c_uint32), ("n_src", c_uint32), ("n_chunks", c_uint32)]
 
 
+class Sliced(ctypes.Structure):
+    _fields_ = [("slice_ptr", c_void_p), ("lane_row", c_void_p), ("lane_len", c_void_p),
+                ("perm", c_void_p), ("n_slots", c_uint64), ("n_edges", c_uint64),
+                ("n_rows", c_uint32), ("n_slices", c_uint32)]
+
+
+SLICED_NONE = 0xFFFFFFFF
+
+
 class Field(ctypes.Structure):
     _fields_ = [("src", c_void_p), ("dst", c_void_p), ("elem_bytes", c_uint32),
                 ("flags", c_uint32)]
@@ -141,6 +150,17 @@ _SIGNATURES = {
                                           c_void_p, c_void_p, c_float, c_float, c_void_p]),
     "plx_sweep_update": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p, c_void_p,
                                  c_uint32, c_void_p, c_int, c_float, c_void_p, c_void_p]),
+    "plx_sliced_n_slices": (c_uint32, [c_uint32]),
+    "plx_sliced_plan_scratch_bytes": (ctypes.c_size_t, [c_uint32]),
+    "plx_sliced_plan": (c_int, [c_void_p, c_void_p, c_uint32, c_uint64, POINTER(Sliced),
+                                c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t]),
+    "plx_sliced_perm": (c_int, [c_void_p, POINTER(Sliced), c_void_p, c_void_p]),
+    "plx_sliced_pack": (c_int, [c_void_p, POINTER(Sliced), c_void_p, c_void_p, c_uint32]),
+    "plx_sliced_unpack": (c_int, [c_void_p, POINTER(Sliced), c_void_p, c_void_p, c_uint32]),
+    "plx_sweep_forward_hebbian_sliced": (c_int, [c_void_p, POINTER(Sliced), c_void_p, c_void_p,
+                                                 c_void_p, c_uint32, c_void_p, c_void_p,
+                                                 c_float, c_float, c_void_p, c_void_p,
+                                                 c_uint32, c_uint32, c_uint32]),
 }
 
 _lib = None

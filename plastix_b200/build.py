@@ -23,6 +23,14 @@ LIB = PKG / "libplastix_b200.so"
 # library of their own so that the product library carries none of them.
 PROBE_SRC = PKG / "probe" / "probe.cu"
 PROBE_LIB = PKG / "libplastix_probe.so"
+# Programs written against the reference's C++ API (include/plastix/*.hpp).
+APPS = {"network_sweep": PKG / "apps" / "network_sweep.cu"}
+APP_FLAGS = ["-std=c++20", "--expt-relaxed-constexpr", "-O2", "--fmad=false", "-lineinfo",
+             "-diag-suppress=20050", f"-I{ROOT / 'include'}"]
+
+
+def app_path(name: str) -> Path:
+    return OBJ / name
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -66,7 +74,21 @@ def build(verbose: bool = False) -> Path:
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     build_probe(verbose)
+    for name in APPS:
+        build_app(name)
     return LIB
+
+
+def build_app(name: str) -> Path:
+    exe = app_path(name)
+    deps = [APPS[name], LIB] + sorted((ROOT / "include").rglob("*.h*"))
+    if _stale(exe, deps):
+        cmd = [NVCC, *ARCH, *APP_FLAGS, str(APPS[name]), "-o", str(exe), f"-L{PKG}",
+               "-lplastix_b200", "-Xlinker", "-rpath=$ORIGIN/.."]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {name}:\n{r.stdout}\n{r.stderr}")
+    return exe
 
 
 def build_probe(verbose: bool = False) -> Path:

@@ -15,7 +15,7 @@ from typing import Optional
 import torch
 
 from . import _abi
-from ._abi import Chunked, Csr, Field, call
+from ._abi import Chunked, Csr, Field, Sliced, call
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -162,40 +162,109 @@ def sweep_update(ctx: Context, csr: DstCsr, from_id: torch.Tensor, act_src: torc
          _ptr(w_out))
 
 
+class SlicedRows:
+    """The warp-sliced row layout of a destination-sorted CSR (see
+    plx_sliced_plan): rows in windows of 512, ordered by length inside a
+    window and dealt 32 per slice, one row per lane; slot order for every
+    connection field, with ``pack`` / ``unpack`` between reference order and
+    slot order."""
+
+    def __init__(self, ctx: Context, csr: "DstCsr"):
+        dev = ctx.device
+        self.ctx = ctx
+        n_rows, n_edges = csr.n_rows, csr.n_edges
+        lib = _abi.lib()
+        n_slices = int(lib.plx_sliced_n_slices(n_rows))
+        self.slice_ptr = torch.empty(n_slices + 1, dtype=torch.int64, device=dev)
+        self.lane_row = torch.empty(n_slices * 32, dtype=torch.int32, device=dev)
+        self.lane_len = torch.empty(n_slices * 32, dtype=torch.int32, device=dev)
+        nb = int(lib.plx_sliced_plan_scratch_bytes(n_rows))
+        scratch = torch.empty(nb, dtype=torch.uint8, device=dev)
+        self.struct = Sliced()
+        call("plx_sliced_plan", ctx.handle, _ptr(csr.row_ptr), n_rows, n_edges,
+             byref(self.struct), _ptr(self.slice_ptr), _ptr(self.lane_row), _ptr(self.lane_len),
+             _ptr(scratch), nb)
+        del scratch
+        self.n_slots = int(self.struct.n_slots)
+        self.perm = torch.empty(max(self.n_slots, 4), dtype=torch.int32, device=dev)
+        call("plx_sliced_perm", ctx.handle, byref(self.struct), _ptr(csr.row_ptr),
+             _ptr(self.perm))
+        self.n_rows, self.n_edges = n_rows, n_edges
+
+    def pack(self, ref: torch.Tensor) -> torch.Tensor:
+        """A field in slot order (padding slots zero) from reference order."""
+        out = torch.zeros(max(self.n_slots, 4), dtype=ref.dtype, device=ref.device)
+        if self.n_slots:
+            call("plx_sliced_pack", self.ctx.handle, byref(self.struct), _ptr(ref.contiguous()),
+                 _ptr(out), ref.element_size())
+        return out
+
+    def unpack(self, slot: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A field in reference order from slot order."""
+        if out is None:
+            out = torch.empty(self.n_edges, dtype=slot.dtype, device=slot.device)
+        if self.n_slots:
+            call("plx_sliced_unpack", self.ctx.handle, byref(self.struct), _ptr(slot),
+                 _ptr(out), slot.element_size())
+        return out
+
+
 class HebbianSweepLayer:
     """One sparse layer stepped like ``Network::DoStep`` in Pipeline mode with
     the Hebbian trace rule: forward sum (identity Apply) + per-connection
-    trace/weight update, fused into one pass. Weights and traces are
-    double-buffered on the device (the fused sweep reads one copy and writes
-    the other); ``weight``/``trace`` are the current copies."""
+    trace/weight update, fused into one pass. Arguments are in the
+    reference's connection order (sorted by ToId); ``weight``/``trace``
+    return the current values in that order.
+
+    ``layout="csr"``: the connections stay in that order; weights and traces
+    are double-buffered (the fused CSR sweep reads one copy and writes the
+    other). ``layout="sliced"``: they are re-laid once into the warp-sliced
+    row layout (SlicedRows), one lane per row, updated in place; ``weight``
+    and ``trace`` then unpack to reference order on request."""
 
     def __init__(self, ctx: Context, n_src: int, n_dst: int, from_id: torch.Tensor,
                  to_id: torch.Tensor, weight: torch.Tensor,
                  trace: Optional[torch.Tensor] = None, *, decay: float = 0.9,
                  rate: float = 1e-3, dead: Optional[torch.Tensor] = None,
-                 fast: bool = True):
+                 fast: bool = True, layout: str = "csr"):
+        if layout not in ("csr", "sliced"):
+            raise ValueError("layout must be 'csr' or 'sliced'")
         dev = ctx.device
         self.ctx = ctx
+        self.layout = layout
         self.n_src, self.n_dst = n_src, n_dst
         self.decay, self.rate = decay, rate
-        self.from_id = from_id.to(dev, torch.int32).contiguous()
+        from_id = from_id.to(dev, torch.int32).contiguous()
         self.to_id = to_id.to(dev, torch.int32).contiguous()
-        self.dead = None if dead is None else dead.to(dev, torch.uint8).contiguous()
-        n = self.from_id.numel()
-        self._w = [weight.to(dev, torch.float32).contiguous().clone(),
-                   torch.empty(n, dtype=torch.float32, device=dev)]
+        dead = None if dead is None else dead.to(dev, torch.uint8).contiguous()
+        n = from_id.numel()
+        w = weight.to(dev, torch.float32).contiguous()
         tr = torch.zeros(n, dtype=torch.float32, device=dev) if trace is None else \
-            trace.to(dev, torch.float32).contiguous().clone()
-        self._e = [tr, torch.empty(n, dtype=torch.float32, device=dev)]
-        self._cur = 0
+            trace.to(dev, torch.float32).contiguous()
         self.csr = DstCsr(ctx, self.to_id, n_src, n_dst, use_to_id=fast)
         self.act_dst = torch.zeros(n_dst, dtype=torch.float32, device=dev)
+        if layout == "sliced":
+            self.slices = SlicedRows(ctx, self.csr)
+            self.from_id = self.slices.pack(from_id)
+            self.dead = None if dead is None else self.slices.pack(dead)
+            self._w = [self.slices.pack(w)]
+            self._e = [self.slices.pack(tr)]
+        else:
+            self.from_id, self.dead = from_id, dead
+            self._w = [w.clone(), torch.empty(n, dtype=torch.float32, device=dev)]
+            self._e = [tr.clone(), torch.empty(n, dtype=torch.float32, device=dev)]
+        self._cur = 0
 
     @property
     def weight(self) -> torch.Tensor:
+        if self.layout == "sliced":
+            return self.slices.unpack(self._w[0])
         return self._w[self._cur]
 
     def _state_tensors(self):
+        if self.layout == "sliced":  # slot order: a checkpoint of this layout
+            return {"weight_slots": self._w[0], "trace_slots": self._e[0],
+                    "act_dst": self.act_dst}
         return {"weight": self._w[self._cur], "trace": self._e[self._cur],
                 "act_dst": self.act_dst}
 
@@ -210,9 +279,20 @@ class HebbianSweepLayer:
 
     @property
     def trace(self) -> torch.Tensor:
+        if self.layout == "sliced":
+            return self.slices.unpack(self._e[0])
         return self._e[self._cur]
 
+    def _sliced_sweep(self, act_src, peers=None, n_peers=0, offset=0, peer_len=0):
+        call("plx_sweep_forward_hebbian_sliced", self.ctx.handle, byref(self.slices.struct),
+             _ptr(self.from_id), _ptr(self.dead), _ptr(act_src), int(act_src.numel()),
+             _ptr(self._w[0]), _ptr(self._e[0]), self.decay, self.rate, _ptr(self.act_dst),
+             peers, n_peers, offset, peer_len)
+
     def step(self, act_src: torch.Tensor) -> torch.Tensor:
+        if self.layout == "sliced":
+            self._sliced_sweep(act_src)
+            return self.act_dst
         c, o = self._cur, 1 - self._cur
         sweep_forward_hebbian(self.ctx, self.csr, self.from_id, act_src, self._w[c],
                               self._w[o], self._e[c], self._e[o], self.act_dst,
@@ -228,6 +308,9 @@ class HebbianSweepLayer:
         if offset < 0 or offset + self.n_dst > peer.n_total:
             raise ValueError(f"slice [{offset}, {offset + self.n_dst}) does not fit the "
                              f"hand-off buffers of {peer.n_total} floats")
+        if self.layout == "sliced":
+            self._sliced_sweep(act_src, peer.out_for_next(), peer.world, offset, peer.n_total)
+            return self.act_dst
         c, o = self._cur, 1 - self._cur
         call("plx_sweep_forward_hebbian_gather", self.ctx.handle, byref(self.csr.struct),
              _ptr(self.from_id), _ptr(self.dead), _ptr(act_src), int(act_src.numel()),

@@ -1,0 +1,46 @@
+"""The single-layer sweep written against the reference's C++ API
+(plastix::Network<Traits> with PLASTIX_HD policies, stepped with DoStep:
+plastix_b200/apps/network_sweep.cu) against the oracle, bit for bit: the
+destination-major forward accumulation (Map on consecutive connections per
+lane, each unit's values combined in connection order) and the
+per-connection Hebbian trace update, for short, long and empty rows."""
+import subprocess
+
+import numpy as np
+import pytest
+
+from plastix_b200 import build, workloads
+
+
+def _write_layer(path, L):
+    with open(path, "wb") as f:
+        np.array([L.n_src, L.n_dst, L.from_id.size], np.uint64).tofile(f)
+        np.ascontiguousarray(L.from_id, np.uint32).tofile(f)
+        np.ascontiguousarray(L.to_id - L.n_src, np.uint32).tofile(f)
+        np.ascontiguousarray(L.weight, np.float32).tofile(f)
+        np.ascontiguousarray(L.act_in, np.float32).tofile(f)
+
+
+def test_api_program_is_built():
+    exe = build.build_app("network_sweep")
+    assert exe.exists()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["random", "rows"])
+def test_api_sweep_matches_oracle(tmp_path, orc, case):
+    if case == "random":
+        L = workloads.sparse_layer(20000, 3000, 200003, seed=17)
+    else:
+        L = workloads.sparse_layer_rows(900, [0, 5, 300, 0, 1, 2000, 64, 65, 257] * 40, seed=5)
+    _write_layer(tmp_path / "layer.bin", L)
+    exe = build.build_app("network_sweep")
+    r = subprocess.run([str(exe), "check", str(tmp_path), "3"], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    act = np.concatenate([L.act_in, np.zeros(L.n_dst, np.float32)])
+    w, e, a = orc.step_hebbian(L.from_id, L.to_id, L.weight, L.trace, act, L.n_src, 0.9, 1e-3,
+                               sweeps=3)
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "out.bin", np.float32), a[L.n_src:])
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "w.bin", np.float32), w)
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "e.bin", np.float32), e)

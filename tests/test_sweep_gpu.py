@@ -42,10 +42,11 @@ def assert_rows(got, want, row_len, exact_ok=True):
     np.testing.assert_allclose(got[~short], want[~short], rtol=RTOL, atol=ATOL)
 
 
-def run_hebbian(ctx, L, sweeps, decay=0.9, rate=1e-3, dead=None, fast=True):
+def run_hebbian(ctx, L, sweeps, decay=0.9, rate=1e-3, dead=None, fast=True, layout="csr"):
     layer = HebbianSweepLayer(ctx, L.n_src, L.n_dst, ids(L.from_id), ids(L.to_id),
                               dev(L.weight), dev(L.trace), decay=decay, rate=rate,
-                              dead=None if dead is None else dev(dead), fast=fast)
+                              dead=None if dead is None else dev(dead), fast=fast,
+                              layout=layout)
     act = dev(L.act_in)
     for _ in range(sweeps):
         out = layer.step(act)
@@ -245,3 +246,117 @@ def test_row_ptr_equals_searchsorted(ctx, case):
                            side="left")
     want[-1] = to_id.size
     np.testing.assert_array_equal(rp.cpu().numpy().astype(np.int64), want)
+
+
+# ---------------------------------------------------------------------------
+# The warp-sliced row layout (plx_sweep_forward_hebbian_sliced): one lane per
+# row, so every row -- whatever its length -- is folded in the reference's
+# order: bit-exact everywhere.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("n_src,n_dst,n_edges,seed", [
+    (1000, 200, 12345, 1),
+    (4096, 4096, 2048 * 3, 2),
+    (50000, 20000, 300001, 3),
+    (8, 3, 7, 4),
+    (1 << 14, 1 << 10, 1 << 16, 5),
+    (3000, 513, 40000, 6),        # one row past a 512-row window
+])
+def test_sliced_hebbian_bit_exact(ctx, orc, n_src, n_dst, n_edges, seed):
+    L = workloads.sparse_layer(n_src, n_dst, n_edges, seed=seed)
+    got = run_hebbian(ctx, L, sweeps=4, layout="sliced")
+    want = oracle_hebbian(orc, L, sweeps=4)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+
+
+def test_sliced_hebbian_golden_fixture(ctx):
+    from pathlib import Path
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "sweep_hebbian_small.npz")
+    L = workloads.sparse_layer(int(fx["n_src"]), int(fx["n_dst"]), int(fx["n_edges"]),
+                               seed=int(fx["seed"]))
+    w, e, a = run_hebbian(ctx, L, int(fx["sweeps"]), float(fx["decay"]), float(fx["rate"]),
+                          layout="sliced")
+    np.testing.assert_array_equal(w, fx["w"])
+    np.testing.assert_array_equal(e, fx["trace"])
+    np.testing.assert_array_equal(a, fx["act"])
+
+
+def test_sliced_hebbian_dead_connections(ctx, orc):
+    L = workloads.sparse_layer(3000, 500, 40000, seed=11)
+    dead = (np.random.default_rng(3).random(L.from_id.size) < 0.2).astype(np.uint8)
+    got = run_hebbian(ctx, L, 3, dead=dead, layout="sliced")
+    want = oracle_hebbian(orc, L, 3, dead=dead)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+
+
+@pytest.mark.parametrize("lens", [
+    [256] * 30 + [1, 255, 0, 254, 3] * 20,
+    [0] * 50 + [7] * 3000 + [0] * 50,
+    [64, 0, 0, 128, 1] * 4000,
+    [0, 0, 5, 0, 3000, 0, 1, 2047, 2048, 2049, 0],   # rows past the staged 96 re-gather
+    [257] * 40 + [256] * 40,
+    [10000],
+    [0] * 100,
+    [1] * 5000 + [4100] + [3] * 700,
+    [97, 96, 95, 100, 4, 5] * 300,                    # around the staging limit
+])
+def test_sliced_row_shapes(ctx, orc, lens):
+    L = workloads.sparse_layer_rows(777, lens, seed=len(lens))
+    got = run_hebbian(ctx, L, 2, layout="sliced")
+    want = oracle_hebbian(orc, L, 2)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+
+
+def test_sliced_layout_invariants(ctx):
+    """perm lists every connection exactly once, in the documented slot
+    positions (slot slice_ptr[s] + 128 g + 4 lane + c = connection 4g + c of
+    the lane's row), rows sorted by length inside each 512-row window;
+    unpack(pack(x)) == x."""
+    from plastix_b200.runtime import SlicedRows
+    lens = list(np.random.default_rng(1).integers(0, 150, 1300))
+    L = workloads.sparse_layer_rows(500, lens, seed=3)
+    csr = DstCsr(ctx, ids(L.to_id), L.n_src, L.n_dst)
+    sl = SlicedRows(ctx, csr)
+    ctx.sync()
+    perm = host(sl.perm)[:sl.n_slots].view(np.uint32)
+    sp = host(sl.slice_ptr)
+    rows = host(sl.lane_row).view(np.uint32)
+    ln = host(sl.lane_len)
+    rp = host(csr.row_ptr)
+    assert sp[0] == 0 and sp[-1] == sl.n_slots and np.all(np.diff(sp) % 128 == 0)
+    valid = perm != _abi.SLICED_NONE
+    assert np.array_equal(np.sort(perm[valid]), np.arange(L.from_id.size))
+    for s in range(sp.size - 1):
+        for lane in range(32):
+            r = rows[32 * s + lane]
+            if r == _abi.SLICED_NONE:
+                continue
+            assert r // 512 == (32 * s) // 512  # the row belongs to the slice's window
+            j = np.arange(ln[32 * s + lane])
+            slot = sp[s] + 128 * (j // 4) + 4 * lane + j % 4
+            np.testing.assert_array_equal(perm[slot], rp[r] + j)
+        lens_s = ln[32 * s:32 * s + 32]
+        assert np.all(np.diff(lens_s[rows[32 * s:32 * s + 32] != _abi.SLICED_NONE]) <= 0)
+    x = torch.arange(L.from_id.size, dtype=torch.float32, device="cuda")
+    np.testing.assert_array_equal(host(sl.unpack(sl.pack(x))), host(x))
+
+
+def test_sliced_full_size_sweep_matches_oracle(ctx, orc):
+    """The 64M-connection single-layer workload in the sliced layout, two
+    sweeps, compared bit for bit with the oracle over the whole layer."""
+    n_src = n_dst = 1 << 20
+    n = 1 << 26
+    from_id, to_id, w, act = workloads.sparse_layer_device(n_src, n_dst, n, 1234, "cuda")
+    layer = HebbianSweepLayer(ctx, n_src, n_dst, from_id, to_id, w, layout="sliced")
+    layer.step(act)
+    out = layer.step(act)
+    ctx.sync()
+    f, t = host(from_id).view(np.uint32), host(to_id).view(np.uint32)
+    a_full = np.concatenate([host(act), np.zeros(n_dst, np.float32)])
+    ww, ee, aa = orc.step_hebbian(f, t, host(w), np.zeros(n, np.float32), a_full, n_src,
+                                  0.9, 1e-3, sweeps=2)
+    np.testing.assert_array_equal(host(out), aa[n_src:])
+    np.testing.assert_array_equal(host(layer.weight), ww)
+    np.testing.assert_array_equal(host(layer.trace), ee)
