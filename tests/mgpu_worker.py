@@ -18,14 +18,14 @@ from plastix_b200.runtime import Context, HebbianSweepLayer, PredictiveCodingNet
 from plastix_b200.sharding import PeerGather, ShardedPCNet, ipc_block_edges  # noqa: E402
 
 
-def check_peer_handoff(ctx, rank, world, dev):
+def check_peer_handoff(ctx, rank, world, dev, layout):
     """The fused sweep + peer-memory hand-off against the plain sweep and an
     NCCL all-gather, over several steps (epochs)."""
     n_src, n_dst, n = 50_000, 40_000, 2_000_000
     f, t, w, _ = workloads.sparse_layer_device(n_src, n_dst, n, 100 + rank, dev)
     act = torch.rand(n_src, generator=torch.Generator(device=dev).manual_seed(9), device=dev)
-    a = HebbianSweepLayer(ctx, n_src, n_dst, f, t, w.clone())
-    b = HebbianSweepLayer(ctx, n_src, n_dst, f, t, w.clone())
+    a = HebbianSweepLayer(ctx, n_src, n_dst, f, t, w.clone(), layout=layout)
+    b = HebbianSweepLayer(ctx, n_src, n_dst, f, t, w.clone(), layout=layout)
     peer = PeerGather(ctx, n_dst * world, rank, world)
     want = torch.empty(n_dst * world, device=dev)
     got = torch.empty(n_dst * world, device=dev)
@@ -37,7 +37,7 @@ def check_peer_handoff(ctx, rank, world, dev):
         peer.copy_to(got)
         ctx.sync()
         if not torch.equal(got, want):
-            bad.append(f"peer hand-off step {step}")
+            bad.append(f"peer hand-off ({layout}) step {step}")
     torch.cuda.synchronize()
     dist.barrier()
     peer.close()
@@ -45,7 +45,7 @@ def check_peer_handoff(ctx, rank, world, dev):
     return bad
 
 
-def check_peer_chain(ctx, rank, world, dev, steps=6):
+def check_peer_chain(ctx, rank, world, dev, layout, steps=6):
     """A recurrent layer whose sources are the previous step's gathered
     destination values, sharded by destination rows: each step's sweep reads
     the last epoch's hand-off buffer while faster ranks may already store the
@@ -57,7 +57,7 @@ def check_peer_chain(ctx, rank, world, dev, steps=6):
     shards = [workloads.sparse_layer_device(n, m, per_rank, 300 + q, dev) for q in range(world)]
     act0 = torch.rand(n, generator=torch.Generator(device=dev).manual_seed(77), device=dev)
     f, t, w, _ = shards[rank]
-    mine = HebbianSweepLayer(ctx, n, m, f, t, w.clone())
+    mine = HebbianSweepLayer(ctx, n, m, f, t, w.clone(), layout=layout)
     peer = PeerGather(ctx, n, rank, world)
     x = act0
     for _ in range(steps):
@@ -75,12 +75,12 @@ def check_peer_chain(ctx, rank, world, dev, steps=6):
     ctx.sync()
     bad = []
     if not torch.equal(x, y):
-        bad.append("peer chain: gathered activations")
+        bad.append(f"peer chain ({layout}): gathered activations")
     lo = rank * per_rank
     if not torch.equal(mine.weight, full.weight[lo:lo + per_rank]):
-        bad.append("peer chain: weights")
+        bad.append(f"peer chain ({layout}): weights")
     if not torch.equal(mine.trace, full.trace[lo:lo + per_rank]):
-        bad.append("peer chain: traces")
+        bad.append(f"peer chain ({layout}): traces")
     torch.cuda.synchronize()
     dist.barrier()
     peer.close()
@@ -133,8 +133,9 @@ def main():
             full = ref.weights(l, S * F)
             if not torch.equal(ch.weight[valid], full[ch.perm[valid].long()]):
                 bad.append(f"source-major weights block {l}")
-    bad += check_peer_handoff(ctx, rank, world, dev)
-    bad += check_peer_chain(ctx, rank, world, dev)
+    for layout in ("csr", "sliced"):
+        bad += check_peer_handoff(ctx, rank, world, dev, layout)
+        bad += check_peer_chain(ctx, rank, world, dev, layout)
     flag = torch.tensor([len(bad)], device=dev)
     dist.all_reduce(flag)
     if bad:
