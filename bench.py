@@ -971,14 +971,22 @@ def bench_api(args):
     exe = build.app_path("network_sweep")
     if not exe.exists():
         exe = build.build_app("network_sweep")
-    sampler = ClockSampler(0)
-    r = subprocess.run([str(exe), "bench", str(args.n_src), str(args.n_dst), str(args.n_edges),
-                        str(args.seed), str(args.steps), str(args.warmup)],
-                       capture_output=True, text=True, timeout=1800)
-    clocks = sampler.stop()
-    if r.returncode != 0:
-        raise SystemExit(f"network_sweep failed:\n{r.stdout}\n{r.stderr}")
-    d = json.loads(r.stdout.strip().splitlines()[-1])
+    # clocks are sampled over the program's timed loops only (it announces
+    # them on stdout), not over the host-side construction of the network
+    proc = subprocess.Popen([str(exe), "bench", str(args.n_src), str(args.n_dst),
+                             str(args.n_edges), str(args.seed), str(args.steps),
+                             str(args.warmup)], stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                            text=True)
+    sampler, lines = None, []
+    for line in proc.stdout:
+        lines.append(line)
+        if line.startswith("timed-region-begins"):
+            sampler = ClockSampler(0)
+    rc = proc.wait(timeout=1800)
+    clocks = sampler.stop() if sampler else None
+    if rc != 0:
+        raise SystemExit(f"network_sweep failed:\n{''.join(lines)}\n{proc.stderr.read()}")
+    d = json.loads(lines[-1])
     n = args.n_edges
     ms = d["device_ms_per_step"]
     algo = 20 * n + 8 * args.n_dst + 4 * args.n_src
