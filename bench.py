@@ -851,10 +851,11 @@ def _probe_lib():
 
 
 def bench_ceiling(args):
-    """The sweep against the two pieces of its traffic no fold order removes:
-    the same connections swept without the row folds (FromId/Weight/Trace
-    loads, act[FromId] gathers, Weight/Trace stores) and as many random
-    gathers alone. Prints per-launch times (CUDA events, inputs > L2)."""
+    """The sweep (CSR order and warp-sliced rows) against the two pieces of its
+    traffic no fold order removes: the same connections swept without the row
+    folds (FromId/Weight/Trace loads, act[FromId] gathers, Weight/Trace
+    stores) and as many random gathers alone; and the shared-memory
+    source-chunk route. Prints per-launch times (CUDA events, inputs > L2)."""
     import torch
 
     from plastix_b200 import _abi, workloads
@@ -884,20 +885,43 @@ def bench_ceiling(args):
         probe_call("plx_probe_gather", ctx.handle, act.data_ptr(), n_src, n, sink.data_ptr(),
                    ctypes.byref(done))
 
+    sliced = HebbianSweepLayer(ctx, n_src, n_dst, from_id, to_id, w.clone(), layout="sliced")
     out = {}
-    for name, fn in (("sweep", lambda i: layer.step(act)), ("nofold", nofold), ("gather", gather)):
+    for name, fn in (("sweep", lambda i: layer.step(act)), ("sliced", lambda i: sliced.step(act)),
+                     ("nofold", nofold), ("gather", gather)):
         ms, clocks = _timed_loop(ctx.stream, fn, args.steps, args.warmup)
         out[name] = ms / args.steps
     ctx.sync()
     gathers = int(done.value)
+    # The shared-memory source-chunk route for the same layer (the layout the
+    # multilayer iPC uses): rows' connections grouped by 16384-source chunk,
+    # chunk partials added per row, then an update pass. Timed with the
+    # trace-free Hebbian update, so both times are lower bounds for the
+    # fused rule.
+    from plastix_b200.runtime import ChunkedRows
+    del layer, sliced, e, w2, e2
+    torch.cuda.empty_cache()
+    ch = ChunkedRows(ctx, from_id, to_id, w, 0, n_src, n_src, n_dst)
+    post = torch.empty(n_dst, device=device)
+    ms_f, _ = _timed_loop(ctx.stream, lambda i: ch.fold(act, post, _abi.APPLY_IDENTITY),
+                          args.steps, args.warmup)
+    ms_u, _ = _timed_loop(ctx.stream, lambda i: ch.update(act, post, _abi.UPDATE_HEBBIAN, 1e-3),
+                          args.steps, args.warmup)
+    ctx.sync()
+    out["chunked_fold"], out["chunked_update"] = ms_f / args.steps, ms_u / args.steps
+    chunk_slots = int(ch.seg_ptr[-1].item())
+    del ch
     line = {"metric": "ms per launch (sweep memory ceiling probes)", "unit": "ms",
             "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "dtype": "f32", "data": "synthetic (seeded generators)",
             "config": {"workload": "sweep ceiling probes", "n_src": n_src, "n_dst": n_dst,
                        "connections": n, "l2": "inputs larger than L2"},
-            "sweep_ms": out["sweep"], "nofold_ms": out["nofold"], "gather_ms": out["gather"],
+            "sweep_ms": out["sweep"], "sliced_sweep_ms": out["sliced"],
+            "nofold_ms": out["nofold"], "gather_ms": out["gather"],
             "gathers": gathers, "gathers_per_s": gathers / (out["gather"] / 1e3),
-            "sweep_over_nofold": out["sweep"] / out["nofold"], "clocks": clocks}
+            "sweep_over_nofold": out["sweep"] / out["nofold"],
+            "chunked_fold_ms": out["chunked_fold"], "chunked_update_ms": out["chunked_update"],
+            "chunked_slots_per_connection": chunk_slots / n, "clocks": clocks}
     print(json.dumps(line), flush=True)
     ctx.close()
 
