@@ -81,3 +81,20 @@ def test_noalloc_rejects_sizes_above_its_limit():
                                  0, None, c_void_p(16))
     assert rc == _abi.PLX_ERR_ARG
     assert b"limit" in lib.plx_last_error()
+
+
+def test_noalloc_empty_input_counts_zero():
+    # n = 0 after a non-empty call: the count must come back 0, as from the
+    # regular entry point, not the previous call's count.
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ctx = Context(0)
+    stream = torch.cuda.current_stream()
+    w, f, age = _inputs(10_000, 3)
+    _run_noalloc(stream, 10_000, w, f, age)
+    empty = [t[:0] for t in (w, f, age)]
+    got = _run_noalloc(stream, 0, *empty)
+    want = _run_regular(ctx, 0, *empty)
+    ctx.sync()
+    assert int(got[2].item()) == int(want[2].item()) == 0
+    ctx.close()
