@@ -57,6 +57,10 @@ def parse_args():
     p.add_argument("--layout", choices=["sliced", "csr"], default="sliced",
                    help="storage order of the swept layer: warp-sliced rows (one lane per "
                         "row) or the destination-sorted CSR order")
+    p.add_argument("--api-traits", choices=["fused", "generic"], default="fused",
+                   help="api workload: the rule as the library's HebbianTraceUpdate policy "
+                        "(DoStep runs one fused sliced sweep) or as a user hook (the generic "
+                        "device passes)")
     p.add_argument("--ipc-units", type=int, default=1 << 18,
                    help="units per layer of the ipc workload (2^18 in the configuration)")
     p.add_argument("--ipc-fan-in", type=int, default=2048)
@@ -987,7 +991,8 @@ def bench_levels(args):
 def bench_api(args):
     """The single-layer sweep through the reference's C++ API: a
     plastix::Network<Traits> with PLASTIX_HD Hebbian-trace policies
-    (plastix_b200/apps/network_sweep.cu), stepped with DoStep. Device time
+    (plastix_b200/apps/network_sweep.cu), stepped with DoStep; --api-traits
+    picks the library policy (fused route) or the user-hook spelling. Device time
     per DoStep from CUDA events on the network's stream; e2e per step is
     DoStep from a host input vector + GetOutput (host clock)."""
     from plastix_b200 import build
@@ -999,8 +1004,8 @@ def bench_api(args):
     # them on stdout), not over the host-side construction of the network
     proc = subprocess.Popen([str(exe), "bench", str(args.n_src), str(args.n_dst),
                              str(args.n_edges), str(args.seed), str(args.steps),
-                             str(args.warmup)], stdout=subprocess.PIPE, stderr=subprocess.PIPE,
-                            text=True)
+                             str(args.warmup), args.api_traits], stdout=subprocess.PIPE,
+                            stderr=subprocess.PIPE, text=True)
     sampler, lines = None, []
     for line in proc.stdout:
         lines.append(line)
@@ -1014,9 +1019,12 @@ def bench_api(args):
     n = args.n_edges
     ms = d["device_ms_per_step"]
     algo = 20 * n + 8 * args.n_dst + 4 * args.n_src
+    route = ("HebbianTraceUpdate policy: one fused sliced sweep per DoStep"
+             if args.api_traits == "fused" else
+             "user hook: generic passes (tiled forward, per-connection update)")
     config = {"workload": "single sparse layer sweep through plastix::Network<Traits>::DoStep "
                           "(PLASTIX_HD policies: identity forward, Hebbian trace update)",
-              "n_src": args.n_src, "n_dst": args.n_dst, "n_edges": n,
+              "traits": route, "n_src": args.n_src, "n_dst": args.n_dst, "n_edges": n,
               "l2": "inputs larger than L2", "build_s": d["build_s"]}
     e2e = {"value": n / (d["e2e_ms_per_step"] / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": 4 * args.n_src, "d2h_bytes_per_step": 4 * args.n_dst}

@@ -144,6 +144,7 @@ template <typename T, typename... Fields> class SOAAllocator {
   using Entity = T;
   using View = SOAView<Fields...>;
   static constexpr size_t NumFields = sizeof...(Fields);
+  template <size_t I> using FieldTypeAt = FieldType<I, Fields...>;
 
   explicit SOAAllocator(size_t NumElements) : Capacity(NumElements) {}
   SOAAllocator(const SOAAllocator &) = delete;

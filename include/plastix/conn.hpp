@@ -19,6 +19,8 @@ struct ToIdTag {};
 struct DeadTag {};
 struct SrcLevelTag {};
 struct WeightTag {};
+// The eligibility trace of HebbianTraceUpdate (traits.hpp); not a core field.
+struct TraceTag {};
 
 PLASTIX_NO_EXEC_CHECK
 PLASTIX_HD constexpr auto &GetWeight(auto &Alloc, size_t Id) {

@@ -523,6 +523,53 @@ static __global__ void k_level_ranges(const uint32_t *keys, size_t m, uint32_t *
   ranges[L] = (uint32_t)lo;
 }
 
+// Traits the fused single-layer sweep serves: Pipeline, DefaultForwardPass
+// with HebbianTraceUpdate, no other hook, float Weight and Trace fields.
+template <class T> struct IsHebbianTrace : std::false_type {};
+template <float D, float R> struct IsHebbianTrace<HebbianTraceUpdate<D, R>> : std::true_type {};
+template <class T> constexpr bool fused_hebbian_traits() {
+  using CA = ConnAllocFor<T>;
+  constexpr size_t w = CA::template IndexOf<WeightTag>(), e = CA::template IndexOf<TraceTag>();
+  if constexpr (w >= CA::NumFields || e >= CA::NumFields) {
+    return false;
+  } else {
+    return T::Model == Propagation::Pipeline &&
+           std::is_same_v<typename T::ForwardPass, DefaultForwardPass> &&
+           IsHebbianTrace<typename T::UpdateConn>::value &&
+           std::is_same_v<typename T::BackwardPass, NoBackwardPass> &&
+           std::is_same_v<typename T::Loss, NoLoss> &&
+           std::is_same_v<typename T::UpdateUnit, NoUpdateUnit> &&
+           std::is_same_v<typename T::PruneUnit, NoPruneUnit> &&
+           std::is_same_v<typename T::PruneConn, NoPruneConn> &&
+           std::is_same_v<typename T::AddUnit, NoAddUnit> &&
+           std::is_same_v<typename T::AddConn, NoAddConn> &&
+           std::is_same_v<typename T::ResetGlobal, NoResetGlobalState> &&
+           std::is_same_v<typename CA::template FieldTypeAt<w>, float> &&
+           std::is_same_v<typename CA::template FieldTypeAt<e>, float>;
+  }
+}
+
+// mm[0] = min over ToId, mm[1] = max over FromId (caller initialises
+// mm = {UINT32_MAX, 0}).
+static __global__ void k_any_set(const uint8_t *v, size_t m, uint32_t *flag) {
+  uint32_t any = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < m; i += (size_t)gridDim.x * blockDim.x)
+    any |= v[i];
+  if (__syncthreads_or(any != 0) && threadIdx.x == 0) atomicOr(flag, 1u);
+}
+
+static __global__ void k_to_min_from_max(const uint32_t *to, const uint32_t *from, size_t m,
+                                         uint32_t *mm) {
+  uint32_t lo = 0xFFFFFFFFu, hi = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < m;
+       i += (size_t)gridDim.x * blockDim.x) {
+    lo = min(lo, to[i]);
+    hi = max(hi, from[i]);
+  }
+  atomicMin(mm, lo);
+  atomicMax(mm + 1, hi);
+}
+
 // 1 when the connections are stored destination-major (ToId non-decreasing
 // over all connections), else 0 (flag initialised to 1 by the caller).
 static __global__ void k_check_dst_major(const uint32_t *to, size_t m, uint32_t *flag) {
@@ -585,11 +632,7 @@ template <typename Traits> class Network {
 
   void DoForwardPass(std::span<const float> Inputs) {
     BeginDevice();
-    const size_t k = std::min(Inputs.size(), NumInput);
-    if (k)
-      cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], Inputs.data(), k * sizeof(float),
-                                 cudaMemcpyHostToDevice, Stream),
-                 "inputs");
+    UploadInputs(Inputs);
     const size_t n = UA.Size(), m = CA.Size();
     constexpr bool topo = Traits::Model == Propagation::Topological;
     if constexpr (topo) {
@@ -774,6 +817,9 @@ template <typename Traits> class Network {
   }
 
   void DoStep(std::span<const float> Inputs, std::span<const float> Targets = {}) {
+    if constexpr (detail::fused_hebbian_traits<Traits>()) {
+      if (FusedStep(Inputs)) return;
+    }
     DoForwardPass(Inputs);
     DoCalculateLoss(Targets);
     DoBackwardPass();
@@ -799,15 +845,23 @@ template <typename Traits> class Network {
       const float *p = static_cast<const float *>(UA.field_data(core::kActivation));
       return {p + OutputRange.Begin, OutputRange.Size()};
     }
-    Output.resize(OutputRange.Size());
-    if (!Output.empty())
-      cuda_check(cudaMemcpyAsync(Output.data(),
+    // into a pinned buffer owned by the network (valid until the next call)
+    const size_t k = OutputRange.Size();
+    if (OutCap < k) {
+      cuda_check(cudaStreamSynchronize(Stream), "output");
+      if (OutHost) cudaFreeHost(OutHost);
+      OutHost = nullptr;
+      cuda_check(cudaMallocHost(reinterpret_cast<void **>(&OutHost), k * sizeof(float)), "output");
+      OutCap = k;
+    }
+    if (k)
+      cuda_check(cudaMemcpyAsync(OutHost,
                                  static_cast<const float *>(d_uf[core::kActivation]) +
                                      OutputRange.Begin,
-                                 Output.size() * sizeof(float), cudaMemcpyDeviceToHost, Stream),
+                                 k * sizeof(float), cudaMemcpyDeviceToHost, Stream),
                  "output");
     cuda_check(cudaStreamSynchronize(Stream), "output");
-    return {Output.data(), Output.size()};
+    return {OutHost, k};
   }
 
   // The coherent host copies (see the header comment).
@@ -998,6 +1052,7 @@ template <typename Traits> class Network {
   }
   static void FetchConnField(void *owner, size_t I) {
     auto *N = static_cast<Network *>(owner);
+    N->FieldsFromSlots();
     N->DownloadField(N->CA, N->d_cf, N->DevConns, I);
   }
   template <class A>
@@ -1048,8 +1103,10 @@ template <typename Traits> class Network {
   }
   // Called before device work: host edits reach the device, and an edit of
   // the connection topology invalidates the connection index.
-  void BeginDevice() {
+  void BeginDevice(bool fused_step = false) {
+    if (!fused_step) FieldsFromSlots();
     const uint64_t cdirty = CA.DirtyMask();
+    if (cdirty) Fused.Ready = false;  // the slot copies no longer match
     const bool units_resized = UA.Size() != DevUnits;
     const bool conns_resized = CA.Size() != DevConns;
     SyncAlloc(UA, d_uf, DevUnits);
@@ -1063,7 +1120,10 @@ template <typename Traits> class Network {
   // fields: the host copies of those fields are stale.
   void EndDevice(bool units, bool conns) {
     if (units) UA.MarkStale(UnitAllocator::AllFields());
-    if (conns) CA.MarkStale(ConnAllocator::AllFields());
+    if (conns) {
+      CA.MarkStale(ConnAllocator::AllFields());
+      Fused.Ready = false;  // the reference-order fields may now be newer
+    }
   }
   void ForceUpload() {
     DevUnits = DevConns = static_cast<size_t>(-1);
@@ -1177,6 +1237,20 @@ template <typename Traits> class Network {
     cuda_check(cudaMemcpyAsync(&dm, flag, 4, cudaMemcpyDeviceToHost, Stream), "index");
     cuda_check(cudaStreamSynchronize(Stream), "index");
     DstMajor = dm != 0;
+    Fused.Ready = false;
+    Fused.Eligible = false;
+    if constexpr (detail::fused_hebbian_traits<Traits>()) {
+      // one layer: every source an input unit, every destination not
+      uint32_t *mm = Buf<uint32_t>(15, 2);
+      const uint32_t init[2] = {0xFFFFFFFFu, 0u};
+      cuda_check(cudaMemcpyAsync(mm, init, 8, cudaMemcpyHostToDevice, Stream), "index");
+      detail::k_to_min_from_max<<<std::min<unsigned>(detail::blocks(m), 1024), 256, 0, Stream>>>(
+          ToPtr(), FromPtr(), m, mm);
+      uint32_t got[2] = {0, 0};
+      cuda_check(cudaMemcpyAsync(got, mm, 8, cudaMemcpyDeviceToHost, Stream), "index");
+      cuda_check(cudaStreamSynchronize(Stream), "index");
+      Fused.Eligible = DstMajor && got[0] >= NumInput && got[1] < NumInput && n > NumInput;
+    }
     uint32_t *keys_out = Buf<uint32_t>(2, m);
     const uint32_t bits = BitsFor(n);
     RadixSort(m, ToPtr(), keys_out, d_in_conn, bits);
@@ -1382,9 +1456,164 @@ template <typename Traits> class Network {
     DevConns = m + k;
   }
 
+  // Input activations to the device. Large inputs go through two pinned
+  // staging buffers, so the host copy of step k + 1 overlaps the device work
+  // of step k and the transfer runs at pinned-memory speed; each buffer is
+  // reused only after the transfer that read it has completed.
+  void UploadInputs(std::span<const float> Inputs) {
+    const size_t k = std::min(Inputs.size(), NumInput);
+    if (!k) return;
+    const size_t bytes = k * sizeof(float);
+    if (bytes < (size_t(256) << 10)) {
+      cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], Inputs.data(), bytes,
+                                 cudaMemcpyHostToDevice, Stream),
+                 "inputs");
+      return;
+    }
+    Staging &b = Stage[StageNext];
+    StageNext ^= 1;
+    if (b.Bytes < bytes) {
+      if (b.Host) {
+        cuda_check(cudaEventSynchronize(b.Done), "inputs");
+        cudaFreeHost(b.Host);
+      }
+      cuda_check(cudaMallocHost(&b.Host, bytes), "inputs");
+      b.Bytes = bytes;
+      if (!b.Done) cuda_check(cudaEventCreateWithFlags(&b.Done, cudaEventDisableTiming), "inputs");
+    } else {
+      cuda_check(cudaEventSynchronize(b.Done), "inputs");
+    }
+    std::memcpy(b.Host, Inputs.data(), bytes);
+    cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], b.Host, bytes, cudaMemcpyHostToDevice,
+                               Stream),
+               "inputs");
+    cuda_check(cudaEventRecord(b.Done, Stream), "inputs");
+  }
+  struct Staging {
+    void *Host = nullptr;
+    size_t Bytes = 0;
+    cudaEvent_t Done = nullptr;
+  };
+  Staging Stage[2];
+  int StageNext = 0;
+
+  // ---- the fused single-layer step (HebbianTraceUpdate traits) -------------
+  // The layer is re-laid once into warp-sliced rows (plx_sliced_*); each
+  // DoStep is then one plx_sweep_forward_hebbian_sliced launch, bit-exact
+  // with the generic passes. Weight and Trace live in slot order while
+  // steps run; they are unpacked into the reference-order fields when
+  // anything else -- a host read, another Do* step -- needs them, and host
+  // edits or other steps invalidate the slot copies (re-packed on the next
+  // fused step).
+  struct FusedState {
+    bool Eligible = false, Ready = false, SlotsNewer = false, AnyDead = true;
+    plx_sliced Sl{};
+    // slot-order FromId, Dead, Weight, Trace; lane lengths, row offsets,
+    // slice offsets, lane rows, slot -> connection permutation
+    void *Mem[9] = {};
+    size_t Bytes[9] = {};
+  };
+  template <class T> T *FusedBuf(int slot, size_t count) {
+    const size_t bytes = std::max<size_t>(count, 4) * sizeof(T);
+    if (Fused.Bytes[slot] < bytes) {
+      cuda_check(cudaStreamSynchronize(Stream), "fused");
+      if (Fused.Mem[slot]) cudaFree(Fused.Mem[slot]);
+      cuda_check(cudaMalloc(&Fused.Mem[slot], bytes), "fused");
+      Fused.Bytes[slot] = bytes;
+    }
+    return static_cast<T *>(Fused.Mem[slot]);
+  }
+  static constexpr size_t kW = ConnAllocator::template IndexOf<WeightTag>();
+  static constexpr size_t kE = ConnAllocator::template IndexOf<TraceTag>();
+
+  void FieldsFromSlots() {
+    if constexpr (detail::fused_hebbian_traits<Traits>()) {
+      if (!Fused.SlotsNewer) return;
+      Fused.SlotsNewer = false;
+      plx_ctx *ctx = PlxCtx();
+      plx_check(plx_sliced_unpack(ctx, &Fused.Sl, Fused.Mem[2], d_cf[kW], 4), "plx_sliced_unpack");
+      plx_check(plx_sliced_unpack(ctx, &Fused.Sl, Fused.Mem[3], d_cf[kE], 4), "plx_sliced_unpack");
+    }
+  }
+
+  void BuildFused() {
+    const size_t n = UA.Size(), m = CA.Size();
+    const uint32_t rows = (uint32_t)(n - NumInput);
+    plx_ctx *ctx = PlxCtx();
+    uint32_t *row_ptr = FusedBuf<uint32_t>(5, rows + 1);
+    plx_check(plx_csr_row_ptr(ctx, ToPtr(), m, (uint32_t)NumInput, rows, row_ptr),
+              "plx_csr_row_ptr");
+    const uint32_t ns = plx_sliced_n_slices(rows);
+    const size_t sb = plx_sliced_plan_scratch_bytes(rows);
+    plx_check(plx_sliced_plan(ctx, row_ptr, rows, m, &Fused.Sl, FusedBuf<uint64_t>(6, ns + 1),
+                              FusedBuf<uint32_t>(7, (size_t)ns * 32),
+                              FusedBuf<uint32_t>(4, (size_t)ns * 32), Buf<uint8_t>(8, sb), sb),
+              "plx_sliced_plan");
+    const size_t slots = Fused.Sl.n_slots;
+    plx_check(plx_sliced_perm(ctx, &Fused.Sl, row_ptr, FusedBuf<uint32_t>(8, slots)),
+              "plx_sliced_perm");
+    uint32_t *from = FusedBuf<uint32_t>(0, slots);
+    uint8_t *dead = FusedBuf<uint8_t>(1, slots);
+    float *w = FusedBuf<float>(2, slots), *e = FusedBuf<float>(3, slots);
+    if (slots) {
+      plx_check(plx_sliced_pack(ctx, &Fused.Sl, FromPtr(), from, 4), "plx_sliced_pack");
+      plx_check(plx_sliced_pack(ctx, &Fused.Sl, DeadPtr(), dead, 1), "plx_sliced_pack");
+      plx_check(plx_sliced_pack(ctx, &Fused.Sl, d_cf[kW], w, 4), "plx_sliced_pack");
+      plx_check(plx_sliced_pack(ctx, &Fused.Sl, d_cf[kE], e, 4), "plx_sliced_pack");
+    }
+    // the dead-aware kernel only while some connection is dead
+    uint32_t *flag = Buf<uint32_t>(15, 2);
+    cuda_check(cudaMemsetAsync(flag, 0, 4, Stream), "fused");
+    detail::k_any_set<<<std::min<unsigned>(detail::blocks(m), 1024), 256, 0, Stream>>>(DeadPtr(),
+                                                                                       m, flag);
+    uint32_t any = 0;
+    cuda_check(cudaMemcpyAsync(&any, flag, 4, cudaMemcpyDeviceToHost, Stream), "fused");
+    cuda_check(cudaStreamSynchronize(Stream), "fused");
+    Fused.AnyDead = any != 0;
+    Fused.Ready = true;
+    Fused.SlotsNewer = false;
+  }
+
+  // One DoStep as a single fused sweep; false when the network is not (or no
+  // longer) a single destination-major layer fed by input units.
+  bool FusedStep(std::span<const float> Inputs) {
+    if (!Fused.SlotsNewer) BeginDevice(true);
+    else if (UA.DirtyMask() || CA.DirtyMask() || UA.Size() != DevUnits || CA.Size() != DevConns) {
+      FieldsFromSlots();  // host edits since the last step: go through the fields
+      BeginDevice(true);
+    }
+    if (IndexStale) RebuildIndex();
+    if (!Fused.Eligible) return false;
+    if (!Fused.Ready) BuildFused();
+    UploadInputs(Inputs);
+    using U = typename Traits::UpdateConn;
+    float *act = static_cast<float *>(d_uf[core::kActivation]);
+    plx_check(plx_sweep_forward_hebbian_sliced(
+                  PlxCtx(), &Fused.Sl, static_cast<uint32_t *>(Fused.Mem[0]),
+                  Fused.AnyDead ? static_cast<uint8_t *>(Fused.Mem[1]) : nullptr, act,
+                  (uint32_t)NumInput, static_cast<float *>(Fused.Mem[2]),
+                  static_cast<float *>(Fused.Mem[3]), U::kDecay, U::kRate, act + NumInput,
+                  nullptr, 0, 0, 0),
+              "plx_sweep_forward_hebbian_sliced");
+    Fused.SlotsNewer = true;
+    UA.MarkStale(UnitAllocator::AllFields());
+    CA.MarkStale(ConnAllocator::AllFields());
+    ++Step;
+    return true;
+  }
+
   void Release() {
     if (Stream) cudaStreamSynchronize(Stream);
     else cudaDeviceSynchronize();
+    for (void *p : Fused.Mem)
+      if (p) cudaFree(p);
+    if (OutHost) cudaFreeHost(OutHost);
+    OutHost = nullptr;
+    for (Staging &b : Stage) {
+      if (b.Host) cudaFreeHost(b.Host);
+      if (b.Done) cudaEventDestroy(b.Done);
+      b = Staging{};
+    }
     for (void *p : d_uf) cudaFree(p);
     for (void *p : d_cf) cudaFree(p);
     for (void *p : {(void *)d_g, (void *)d_in_ptr, (void *)d_out_ptr, (void *)d_in_conn,
@@ -1411,13 +1640,15 @@ template <typename Traits> class Network {
   float *d_targets = nullptr;
   size_t TargetCap = 0;
   bool NeedsResort = false, IndexStale = true, DstMajor = false;
+  FusedState Fused;
   int NumSMs = 148;
   uint64_t ProposalCap = uint64_t(1) << 26;
   cudaStream_t Stream = nullptr;
   plx_ctx *Ctx = nullptr;
   void *Scratch[16] = {};
   size_t ScratchBytes[16] = {};
-  mutable std::vector<float> Output;
+  mutable float *OutHost = nullptr;
+  mutable size_t OutCap = 0;
 };
 
 }  // namespace plastix

@@ -160,6 +160,25 @@ struct NoResetGlobalState {
   PLASTIX_HD static void Reset(auto &) {}
 };
 
+// A Hebbian connection rule with a decaying eligibility trace (an addition;
+// the reference ships no plasticity rule): per live connection, with pre =
+// Activation[Src] and post = Activation[Dst] after the forward pass,
+//   trace' = Decay * trace + pre * post,   weight' = weight + Rate * trace'
+// (each product and sum rounded separately). Needs WeightTag and TraceTag
+// among the connection fields. A single Pipeline layer whose traits use
+// DefaultForwardPass with this rule (and no other hook) steps through one
+// fused device sweep per DoStep.
+template <float Decay, float Rate> struct HebbianTraceUpdate {
+  static constexpr float kDecay = Decay, kRate = Rate;
+  PLASTIX_HD static void UpdateIncomingConnection(auto &U, size_t DstId, size_t SrcId, auto &C,
+                                                  size_t ConnId, auto &) {
+    float &E = GetField<TraceTag>(C, ConnId);
+    E = Decay * E + GetActivation(U, SrcId) * GetActivation(U, DstId);
+    GetWeight(C, ConnId) += Rate * E;
+  }
+  PLASTIX_HD static void UpdateOutgoingConnection(auto &, size_t, size_t, auto &, size_t, auto &) {}
+};
+
 // Losses stage dL/dActivation of each output unit into its BackwardAcc.
 struct NoLoss {
   PLASTIX_HD static void CalculateLoss(auto &, UnitRange, std::span<const float>, auto &) {}

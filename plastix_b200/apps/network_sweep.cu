@@ -6,15 +6,21 @@
 // parity test (small layers against the oracle).
 //
 // Usage:
-//   network_sweep bench <n_src> <n_dst> <n_edges> <seed> <steps> <warmup>
+//   network_sweep bench <n_src> <n_dst> <n_edges> <seed> <steps> <warmup> [generic|fused]
 //     prints one JSON object: device ms per DoStep (CUDA events on the
 //     network's stream) and end-to-end ms per step (DoStep from a host
 //     input vector + GetOutput, host clock), construction time.
-//   network_sweep check <dir> <steps>
+//   network_sweep check <dir> <steps> [generic|fused]
 //     reads n_src n_dst n_edges (u64 x3), from, to (u32), weight, act (f32)
 //     from <dir>/layer.bin, runs <steps> DoSteps, writes out.bin (final
 //     destination activations), w.bin and e.bin (weights and traces in the
 //     given connection order).
+//   network_sweep check-edit <dir> <steps> [generic|fused]
+//     as check, and after the first step reads trace n/3 on the host and
+//     adds 0.25 to weight 0 and -0.5 to weight n/2 through GetConnAlloc().
+// The last argument picks the traits: "generic" (default) spells the rule
+// out as a user hook; "fused" uses plastix::HebbianTraceUpdate, which DoStep
+// runs as one fused sliced sweep.
 #include <plastix/plastix.hpp>
 
 #include <chrono>
@@ -22,6 +28,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 namespace {
@@ -41,6 +48,8 @@ struct HebbianTrace {
                                                   auto &) {}
 };
 
+// Policies written out by the user: DoStep runs the generic device passes
+// (tiled forward accumulation, then the per-connection update hook).
 struct SweepTraits : plastix::DefaultNetworkTraits<> {
   using UpdateConn = HebbianTrace;
   using ExtraConnFields =
@@ -48,6 +57,21 @@ struct SweepTraits : plastix::DefaultNetworkTraits<> {
                              plastix::alloc::SOAField<TraceTag, float>>;
   static constexpr plastix::Propagation Model = plastix::Propagation::Pipeline;
 };
+
+// The same rule through the library's HebbianTraceUpdate policy: DoStep
+// recognises it and runs the single fused sliced sweep.
+struct FusedSweepTraits : plastix::DefaultNetworkTraits<> {
+  using UpdateConn = plastix::HebbianTraceUpdate<0.9f, 1e-3f>;
+  using ExtraConnFields =
+      plastix::ConnFieldList<plastix::alloc::SOAField<plastix::WeightTag, float>,
+                             plastix::alloc::SOAField<plastix::TraceTag, float>>;
+  static constexpr plastix::Propagation Model = plastix::Propagation::Pipeline;
+};
+static_assert(plastix::detail::fused_hebbian_traits<FusedSweepTraits>());
+static_assert(!plastix::detail::fused_hebbian_traits<SweepTraits>());
+
+template <class Traits> using TraceOf =
+    std::conditional_t<std::is_same_v<Traits, FusedSweepTraits>, plastix::TraceTag, TraceTag>;
 
 // A LayerBuilder that appends n_dst units and the given destination-sorted
 // connections (from: source unit ids, to: destination index in [0, n_dst)).
@@ -123,7 +147,7 @@ template <class T> void write_vec(const std::string &path, const std::vector<T> 
   std::fclose(f);
 }
 
-int check(const std::string &dir, int steps) {
+template <class Traits> int check(const std::string &dir, int steps, bool edit) {
   FILE *f = std::fopen((dir + "/layer.bin").c_str(), "rb");
   if (!f) return 2;
   uint64_t hdr[3];
@@ -134,18 +158,26 @@ int check(const std::string &dir, int steps) {
   if (!read_vec(f, from, n) || !read_vec(f, to, n) || !read_vec(f, w, n) || !read_vec(f, act, n_src))
     return 2;
   std::fclose(f);
-  plastix::Network<SweepTraits> Net(n_src, GivenConnections{&from, &to, &w, n_dst});
+  plastix::Network<Traits> Net(n_src, GivenConnections{&from, &to, &w, n_dst});
   std::span<const float> out;
   for (int s = 0; s < steps; ++s) {
     Net.DoStep(act);
     out = Net.GetOutput();
+    if (edit && s == 0 && n) {
+      // host edits between steps: read a trace, bump two weights
+      auto &C = Net.GetConnAlloc();
+      volatile float probe = plastix::GetField<TraceOf<Traits>>(C, n / 3);
+      (void)probe;
+      plastix::GetWeight(C, 0) += 0.25f;
+      plastix::GetWeight(C, n / 2) -= 0.5f;
+    }
   }
   std::vector<float> o(out.begin(), out.end());
   auto &C = Net.GetConnAlloc();
   std::vector<float> wo(n), eo(n);
   for (uint64_t i = 0; i < n; ++i) {
     wo[i] = plastix::GetWeight(C, i);
-    eo[i] = plastix::GetField<TraceTag>(C, i);
+    eo[i] = plastix::GetField<TraceOf<Traits>>(C, i);
   }
   write_vec(dir + "/out.bin", o);
   write_vec(dir + "/w.bin", wo);
@@ -153,12 +185,13 @@ int check(const std::string &dir, int steps) {
   return 0;
 }
 
+template <class Traits>
 int bench(uint64_t n_src, uint64_t n_dst, uint64_t n, uint64_t seed, int steps, int warmup) {
   std::vector<uint32_t> from, to;
   std::vector<float> w, act;
   make_layer(n_src, n_dst, n, seed, from, to, w, act);
   const auto t0 = std::chrono::steady_clock::now();
-  plastix::Network<SweepTraits> Net(n_src, GivenConnections{&from, &to, &w, n_dst});
+  plastix::Network<Traits> Net(n_src, GivenConnections{&from, &to, &w, n_dst});
   cudaStream_t stream;
   plastix::cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
   Net.SetStream(stream);
@@ -201,11 +234,20 @@ int bench(uint64_t n_src, uint64_t n_dst, uint64_t n, uint64_t seed, int steps, 
 
 int main(int argc, char **argv) {
   try {
-    if (argc == 8 && std::string(argv[1]) == "bench")
-      return bench(std::strtoull(argv[2], nullptr, 10), std::strtoull(argv[3], nullptr, 10),
-                   std::strtoull(argv[4], nullptr, 10), std::strtoull(argv[5], nullptr, 10),
-                   std::atoi(argv[6]), std::atoi(argv[7]));
-    if (argc == 4 && std::string(argv[1]) == "check") return check(argv[2], std::atoi(argv[3]));
+    const std::string mode = argc > 1 ? argv[1] : "";
+    const bool fused = std::string(argv[argc - 1]) == "fused";
+    const int args = argc - (fused || std::string(argv[argc - 1]) == "generic");
+    if (args == 8 && mode == "bench") {
+      const uint64_t a = std::strtoull(argv[2], nullptr, 10), b = std::strtoull(argv[3], nullptr, 10),
+                     c = std::strtoull(argv[4], nullptr, 10), d = std::strtoull(argv[5], nullptr, 10);
+      return fused ? bench<FusedSweepTraits>(a, b, c, d, std::atoi(argv[6]), std::atoi(argv[7]))
+                   : bench<SweepTraits>(a, b, c, d, std::atoi(argv[6]), std::atoi(argv[7]));
+    }
+    if (args == 4 && (mode == "check" || mode == "check-edit")) {
+      const bool edit = mode == "check-edit";
+      return fused ? check<FusedSweepTraits>(argv[2], std::atoi(argv[3]), edit)
+                   : check<SweepTraits>(argv[2], std::atoi(argv[3]), edit);
+    }
   } catch (const std::exception &e) {
     std::fprintf(stderr, "%s\n", e.what());
     return 4;
