@@ -1001,18 +1001,24 @@ def bench_api(args):
     if not exe.exists():
         exe = build.build_app("network_sweep")
     # clocks are sampled over the program's timed loops only (it announces
-    # them on stdout), not over the host-side construction of the network
+    # them on stdout), not over the host-side construction of the network;
+    # the sampler is started first, so that its set-up does not eat into a
+    # short timed region, and its samples are cleared at the announcement
+    sampler = ClockSampler(0)
     proc = subprocess.Popen([str(exe), "bench", str(args.n_src), str(args.n_dst),
                              str(args.n_edges), str(args.seed), str(args.steps),
                              str(args.warmup), args.api_traits], stdout=subprocess.PIPE,
                             stderr=subprocess.PIPE, text=True)
-    sampler, lines = None, []
+    lines, began = [], False
     for line in proc.stdout:
         lines.append(line)
         if line.startswith("timed-region-begins"):
-            sampler = ClockSampler(0)
+            sampler.samples.clear()
+            began = True
     rc = proc.wait(timeout=1800)
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop()
+    if not began:
+        clocks = None
     if rc != 0:
         raise SystemExit(f"network_sweep failed:\n{''.join(lines)}\n{proc.stderr.read()}")
     d = json.loads(lines[-1])

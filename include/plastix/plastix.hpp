@@ -1458,8 +1458,9 @@ template <typename Traits> class Network {
 
   // Input activations to the device. Large inputs go through two pinned
   // staging buffers, so the host copy of step k + 1 overlaps the device work
-  // of step k and the transfer runs at pinned-memory speed; each buffer is
-  // reused only after the transfer that read it has completed.
+  // of step k and the transfer runs at pinned-memory speed, piece by piece
+  // behind the host copy; each buffer is reused only after the transfers
+  // that read it have completed.
   void UploadInputs(std::span<const float> Inputs) {
     const size_t k = std::min(Inputs.size(), NumInput);
     if (!k) return;
@@ -1483,10 +1484,18 @@ template <typename Traits> class Network {
     } else {
       cuda_check(cudaEventSynchronize(b.Done), "inputs");
     }
-    std::memcpy(b.Host, Inputs.data(), bytes);
-    cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], b.Host, bytes, cudaMemcpyHostToDevice,
-                               Stream),
-               "inputs");
+    // in 1 MiB pieces: the transfer of piece i runs while piece i + 1 is
+    // copied into the staging buffer
+    constexpr size_t piece = size_t(1) << 20;
+    auto *src = reinterpret_cast<const char *>(Inputs.data());
+    auto *host = static_cast<char *>(b.Host);
+    auto *dev = static_cast<char *>(d_uf[core::kActivation]);
+    for (size_t off = 0; off < bytes; off += piece) {
+      const size_t len = std::min(piece, bytes - off);
+      std::memcpy(host + off, src + off, len);
+      cuda_check(cudaMemcpyAsync(dev + off, host + off, len, cudaMemcpyHostToDevice, Stream),
+                 "inputs");
+    }
     cuda_check(cudaEventRecord(b.Done, Stream), "inputs");
   }
   struct Staging {

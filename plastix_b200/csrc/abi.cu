@@ -60,9 +60,23 @@ extern "C" int plx_ctx_create(int device, void* stream, plx_ctx** out) {
   return PLX_OK;
 }
 
+int ctx_counters(plx_ctx* ctx, size_t n, uint32_t** out) {
+  if (ctx->counters_cap < n) {
+    PLX_TRY_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (ctx->d_counters) PLX_TRY_CUDA(cudaFree(ctx->d_counters));
+    ctx->d_counters = nullptr;
+    ctx->counters_cap = 0;
+    PLX_TRY_CUDA(cudaMalloc(&ctx->d_counters, n * sizeof(uint32_t)));
+    ctx->counters_cap = n;
+  }
+  *out = ctx->d_counters;
+  return PLX_OK;
+}
+
 extern "C" int plx_ctx_destroy(plx_ctx* ctx) {
   if (!ctx) return PLX_OK;
   cudaSetDevice(ctx->device);
+  if (ctx->d_counters) cudaFree(ctx->d_counters);
   cudaError_t e = cudaFree(ctx->d_status);
   delete ctx;
   if (e != cudaSuccess) return check_cuda(e, "cudaFree(status)");

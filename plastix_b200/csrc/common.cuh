@@ -246,4 +246,9 @@ struct plx_ctx {
   int32_t* d_status = nullptr;  // device word written by bounded waits
   uint32_t* d_queue = nullptr;  // work counter of the warp sweeps (same allocation)
   uint64_t timeout_ns = 2000000000ull;
+  uint32_t* d_counters = nullptr;  // per-window counters of the sliced hand-off
+  size_t counters_cap = 0;
 };
+
+// The context's counter array, grown (never shrunk) to at least n words.
+int ctx_counters(plx_ctx* ctx, size_t n, uint32_t** out);

@@ -66,6 +66,7 @@ struct SlicedArgs {
   float* act_dst;
   uint32_t* queue;
   int32_t* status;
+  uint32_t* win_done;  // [n_slices / 16 rounded up] slices finished per window
   uint32_t n_peers;
   uint32_t peer_offset;
   float* peer_out[PLX_MAX_PEERS];
@@ -179,6 +180,30 @@ __device__ __forceinline__ void load_sid(const SlicedArgs& a, uint64_t base, uin
   }
 }
 
+// The hand-off to the other GPUs. A window's rows are contiguous
+// ([512 w, 512 w + 512)) but its lanes' rows are permuted, so row values are
+// not stored to the peers one lane at a time (scattered 4-byte NVLink
+// writes); the warp that finishes a window's last slice instead copies the
+// whole window from act_dst to every peer buffer with coalesced stores.
+// Every warp makes its row values visible (fence) before it counts its slice.
+__device__ __forceinline__ void push_window(const SlicedArgs& a, uint32_t s, uint32_t lane) {
+  __threadfence();
+  __syncwarp();
+  const uint32_t win = s / kSlSlicesPerWin;
+  uint32_t last = 0;
+  if (lane == 0) {
+    const uint32_t in_win = min(kSlSlicesPerWin, a.n_slices - win * kSlSlicesPerWin);
+    last = atomicAdd(a.win_done + win, 1u) == in_win - 1;
+  }
+  if (!__shfl_sync(kFullMask, last, 0)) return;
+  __threadfence();
+  const uint32_t lo = win * kSlWin, hi = min(a.n_rows, lo + kSlWin);
+  for (uint32_t r = lo + lane; r < hi; r += kSlLanes) {
+    const float v = __ldcg(a.act_dst + r);
+    for (uint32_t p = 0; p < a.n_peers; ++p) a.peer_out[p][a.peer_offset + r] = v;
+  }
+}
+
 // Each warp takes slices one at a time from an atomic queue: no CTA-level
 // barrier, so a warp never waits for the others (measured: the same passes
 // inside a CTA that swept a window of slices together ran at half this rate).
@@ -263,10 +288,8 @@ __global__ void __launch_bounds__(kSlWarps * 32, 4) k_sweep_sliced(SlicedArgs a)
     }
     // Apply (identity): the row's value, written by its lane
     const float post = acc;
-    if (row != kSlNone) {
-      a.act_dst[row] = post;
-      for (uint32_t p = 0; p < a.n_peers; ++p) a.peer_out[p][a.peer_offset + row] = post;
-    }
+    if (row != kSlNone) a.act_dst[row] = post;
+    if (a.n_peers) push_window(a, s, lane);
     __syncwarp();
     // ---- pass 2: trace and weight update in place ----------------------------
     for (uint32_t g0 = 0; g0 < my_groups; g0 += kSlStep) {
@@ -512,6 +535,11 @@ extern "C" int plx_sweep_forward_hebbian_sliced(plx_ctx* ctx, const plx_sliced* 
   if (per_sm < 1) per_sm = 1;
   const uint32_t n_blocks = (sl->n_slices + kSlWarps - 1) / kSlWarps;
   const uint32_t grid = std::min<uint32_t>(n_blocks, (uint32_t)ctx->num_sms * per_sm);
+  if (n_peers) {
+    const size_t n_win = (sl->n_slices + kSlSlicesPerWin - 1) / kSlSlicesPerWin;
+    if (int rc = ctx_counters(ctx, n_win, &a.win_done)) return rc;
+    PLX_TRY_CUDA(cudaMemsetAsync(a.win_done, 0, n_win * sizeof(uint32_t), ctx->stream));
+  }
   PLX_TRY_CUDA(cudaMemsetAsync(ctx->d_queue, 0, sizeof(uint32_t), ctx->stream));
   kern<<<std::max(grid, 1u), kSlWarps * 32, kSlSmemBytes, ctx->stream>>>(a);
   PLX_LAUNCH_CHECK("k_sweep_sliced");

@@ -360,3 +360,37 @@ def test_sliced_full_size_sweep_matches_oracle(ctx, orc):
     np.testing.assert_array_equal(host(out), aa[n_src:])
     np.testing.assert_array_equal(host(layer.weight), ww)
     np.testing.assert_array_equal(host(layer.trace), ee)
+
+
+@pytest.mark.parametrize("n_dst,offset", [(1300, 3), (512, 0), (31, 1001), (4097, 2)])
+def test_sliced_hand_off_stores_every_window(ctx, orc, n_dst, offset):
+    """The sliced sweep's hand-off: the warp that finishes a 512-row window
+    copies it to every peer buffer. Here the peers are three buffers of this
+    GPU: after each of three sweeps every buffer holds exactly the layer's
+    row values at [offset, offset + n_dst) and nothing else changed, for
+    layers whose last window is partial, and with the per-window counters
+    reused across sweeps and layers of another size."""
+    from ctypes import c_void_p
+    lens = list(np.random.default_rng(n_dst).integers(0, 120, n_dst))
+    L = workloads.sparse_layer_rows(900, lens, seed=offset)
+    layer = HebbianSweepLayer(ctx, L.n_src, L.n_dst, ids(L.from_id), ids(L.to_id),
+                              dev(L.weight), dev(L.trace), layout="sliced")
+    peer_len = offset + n_dst + 77
+    bufs = [torch.full((peer_len,), float("nan"), device="cuda") for _ in range(3)]
+    arr = (c_void_p * 3)(*[b.data_ptr() for b in bufs])
+    act = dev(L.act_in)
+    want_a = np.concatenate([L.act_in, np.zeros(L.n_dst, np.float32)])
+    w_ref, e_ref = L.weight, L.trace
+    for _ in range(3):
+        for b in bufs:
+            b.fill_(float("nan"))
+        layer._sliced_sweep(act, arr, 3, offset, peer_len)
+        ctx.sync()
+        w_ref, e_ref, want_a = orc.step_hebbian(L.from_id, L.to_id, w_ref, e_ref, want_a,
+                                                L.n_src, 0.9, 1e-3, sweeps=1)
+        out = host(layer.act_dst)
+        np.testing.assert_array_equal(out, want_a[L.n_src:])
+        for b in bufs:
+            hb = host(b)
+            np.testing.assert_array_equal(hb[offset:offset + n_dst], out)
+            assert np.isnan(hb[:offset]).all() and np.isnan(hb[offset + n_dst:]).all()
