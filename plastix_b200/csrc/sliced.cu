@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(kSlWarps * 32, 4) k_sweep_sliced(SlicedArgs a)
   const uint32_t len1 = a.act_src_len - 1u;
   const uint64_t pol_first = l2_policy_evict_first();
   const uint64_t pol_last = l2_policy_evict_last();
+  const uint64_t pol_normal = l2_policy_evict_normal();
   float4(*pre)[kSlLanes] =
       reinterpret_cast<float4(*)[kSlLanes]>(s_pre + (size_t)warp * kSlCapGroups * kSlLanes);
   bool bad = false;
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(kSlWarps * 32, 4) k_sweep_sliced(SlicedArgs a)
         const uint32_t g = g0 + h;
         const uint64_t k = base + 128ull * g + 4 * lane;
         if (g < my_groups) {
-          const uint4 y = ld_stream_v4(a.w + k, pol_last);
+          const uint4 y = ld_stream_v4(a.w + k, pol_normal);
           wv[h][0] = __uint_as_float(y.x); wv[h][1] = __uint_as_float(y.y);
           wv[h][2] = __uint_as_float(y.z); wv[h][3] = __uint_as_float(y.w);
           dd[h] = ld_dead4<DEAD>(a.dead, k);
