@@ -481,6 +481,19 @@ int plx_chunked_fold(plx_ctx* ctx, const plx_chunked* layout, const float* w,
                      const float* gathered, int apply_kind, const float* value,
                      float* out, float* partial);
 
+/* plx_chunked_fold of an iPC backward block (apply TANH_GRAD, value = x)
+ * with the value-node update of the same hidden units fused into its
+ * epilogue -- plx_ipc_value_update mode 1 (ipc_multilayer.cpp:239-245 and
+ * the pre-step :220-228): bu = (1 - tanh(x)^2) * acc; x += gamma * (-eps + bu);
+ * act = tanh(x). The bottom-up sum itself is not stored (the reference
+ * zeroes it after the update). x and act equal those of the two separate
+ * calls bit for bit. Valid where nothing reads x or act between the backward
+ * fold and the value update (an inference iteration; not the example's
+ * learning step, whose connection update reads act in between). */
+int plx_chunked_fold_ipc_value(plx_ctx* ctx, const plx_chunked* layout, const float* w,
+                               const float* gathered, float* x, const float* eps, float gamma,
+                               float* act, float* partial);
+
 /* Per-connection update over the layout with row_val[r] as the row value and
  * gathered[src] as the other side, PLX_UPDATE_* rules with the rounding of
  * plx_sweep_update (a weight updated here equals the same rule applied to the

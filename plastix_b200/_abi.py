@@ -115,6 +115,8 @@ _SIGNATURES = {
                                  c_void_p, c_void_p, c_void_p]),
     "plx_chunked_update": (c_int, [c_void_p, POINTER(Chunked), c_void_p, c_void_p, c_void_p,
                                    c_int, c_float]),
+    "plx_chunked_fold_ipc_value": (c_int, [c_void_p, POINTER(Chunked), c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_float, c_void_p, c_void_p]),
     "plx_sweep_forward_hebbian_gather": (c_int, [c_void_p, POINTER(Csr), c_void_p, c_void_p,
                                                  c_void_p, c_uint32, c_void_p, c_void_p,
                                                  c_void_p, c_void_p, c_float, c_float,

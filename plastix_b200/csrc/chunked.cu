@@ -220,6 +220,29 @@ __global__ void k_chunk_combine(const float* __restrict__ partial, uint32_t n_ro
   }
 }
 
+// The iPC bottom-up Apply (TANH_GRAD) of a hidden layer with the value-node
+// update of the same units folded into it (plx_ipc_value_update mode 1:
+// x += gamma * (-eps + bu); act = tanh(x)). bu is consumed here and never
+// stored: the reference zeroes it right after the update
+// (ipc_multilayer.cpp:239-245). Same operations and roundings as the two
+// separate kernels, so x and act are equal bit for bit.
+__global__ void k_chunk_combine_ipc_value(const float* __restrict__ partial, uint32_t n_rows,
+                                          uint32_t n_chunks, float* __restrict__ x,
+                                          const float* __restrict__ eps, float gamma,
+                                          float* __restrict__ act) {
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
+       r += gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (uint32_t c = 0; c < n_chunks; ++c)
+      acc = __fadd_rn(acc, partial[(uint64_t)c * n_rows + r]);
+    const float v = x[r];
+    const float bu = apply_value<PLX_APPLY_TANH_GRAD>(acc, v);
+    const float xv = __fadd_rn(v, __fmul_rn(gamma, __fadd_rn(-eps[r], bu)));
+    x[r] = xv;
+    act[r] = tanhf(xv);
+  }
+}
+
 // Per-connection update, same rules and rounding as plx_sweep_update:
 //   GRADIENT:   w -= (rate * row) * g      HEBBIAN: w += (rate * row) * g
 //   HEBBIAN_T:  w += (rate * g) * row
@@ -395,15 +418,9 @@ extern "C" int plx_chunked_gather(plx_ctx* ctx, uint64_t n_padded, const uint32_
   return PLX_OK;
 }
 
-extern "C" int plx_chunked_fold(plx_ctx* ctx, const plx_chunked* L, const float* w,
-                                const float* gathered, int apply_kind, const float* value,
-                                float* out, float* partial) {
-  PLX_CHECK_ARG(ctx, "ctx is required");
-  if (int rc = check_chunked(L)) return rc;
-  PLX_CHECK_ARG(w && gathered && out && partial, "w, gathered, out and partial are required");
-  PLX_CHECK_ARG(aligned16(w), "w must be 16-byte aligned");
-  PLX_CHECK_ARG(!apply_reads_value(apply_kind) || value, "this apply needs value");
-  PLX_TRY_CUDA(cudaSetDevice(ctx->device));
+// The chunk partials of a row sweep (the first half of both fold entries).
+static int chunk_partials(plx_ctx* ctx, const plx_chunked* L, const float* w,
+                          const float* gathered, float* partial) {
   ChunkArgs a{};
   a.seg_ptr = L->seg_ptr;
   a.src = L->src;
@@ -429,6 +446,21 @@ extern "C" int plx_chunked_fold(plx_ctx* ctx, const plx_chunked* L, const float*
   const dim3 grid = sweep_grid(ctx, L, &a.rows_per_cta);
   k_chunk_fold<<<grid, kCThreads, smem, ctx->stream>>>(a);
   PLX_LAUNCH_CHECK("k_chunk_fold");
+  return PLX_OK;
+}
+
+extern "C" int plx_chunked_fold(plx_ctx* ctx, const plx_chunked* L, const float* w,
+                                const float* gathered, int apply_kind, const float* value,
+                                float* out, float* partial) {
+  PLX_CHECK_ARG(ctx, "ctx is required");
+  if (int rc = check_chunked(L)) return rc;
+  PLX_CHECK_ARG(w && gathered && out && partial, "w, gathered, out and partial are required");
+  PLX_CHECK_ARG(aligned16(w), "w must be 16-byte aligned");
+  PLX_CHECK_ARG(!apply_reads_value(apply_kind) || value, "this apply needs value");
+  PLX_CHECK_ARG(apply_kind >= PLX_APPLY_IDENTITY && apply_kind <= PLX_APPLY_TANH_GRAD,
+                "unknown apply_kind %d", apply_kind);
+  PLX_TRY_CUDA(cudaSetDevice(ctx->device));
+  if (int rc = chunk_partials(ctx, L, w, gathered, partial)) return rc;
   const unsigned cg = (unsigned)std::max<uint64_t>(1, (L->n_rows + 255) / 256);
   switch (apply_kind) {
 #define PLX_CHUNK_APPLY(K)                                                              \
@@ -447,6 +479,23 @@ extern "C" int plx_chunked_fold(plx_ctx* ctx, const plx_chunked* L, const float*
       return set_error(PLX_ERR_ARG, "unknown apply_kind %d", apply_kind);
   }
   PLX_LAUNCH_CHECK("k_chunk_combine");
+  return PLX_OK;
+}
+
+extern "C" int plx_chunked_fold_ipc_value(plx_ctx* ctx, const plx_chunked* L, const float* w,
+                                          const float* gathered, float* x, const float* eps,
+                                          float gamma, float* act, float* partial) {
+  PLX_CHECK_ARG(ctx, "ctx is required");
+  if (int rc = check_chunked(L)) return rc;
+  PLX_CHECK_ARG(w && gathered && x && eps && act && partial,
+                "w, gathered, x, eps, act and partial are required");
+  PLX_CHECK_ARG(aligned16(w), "w must be 16-byte aligned");
+  PLX_TRY_CUDA(cudaSetDevice(ctx->device));
+  if (int rc = chunk_partials(ctx, L, w, gathered, partial)) return rc;
+  const unsigned cg = (unsigned)std::max<uint64_t>(1, (L->n_rows + 255) / 256);
+  k_chunk_combine_ipc_value<<<cg, 256, 0, ctx->stream>>>(partial, L->n_rows, L->n_chunks, x,
+                                                          eps, gamma, act);
+  PLX_LAUNCH_CHECK("k_chunk_combine_ipc_value");
   return PLX_OK;
 }
 

@@ -764,6 +764,14 @@ class ChunkedRows:
         call("plx_chunked_fold", self.ctx.handle, byref(self.struct), _ptr(self.weight),
              _ptr(gathered), apply, _ptr(value), _ptr(out), _ptr(self.partial))
 
+    def fold_ipc_value(self, gathered: torch.Tensor, x: torch.Tensor, eps: torch.Tensor,
+                       act: torch.Tensor, gamma: float) -> None:
+        """An iPC backward block (TANH_GRAD with value x) with the value-node
+        update of its rows fused in: x += gamma * (-eps + bu); act = tanh(x)."""
+        call("plx_chunked_fold_ipc_value", self.ctx.handle, byref(self.struct),
+             _ptr(self.weight), _ptr(gathered), _ptr(x), _ptr(eps), gamma, _ptr(act),
+             _ptr(self.partial))
+
     def update(self, gathered: torch.Tensor, row_val: torch.Tensor, kind: int,
                rate: float) -> None:
         call("plx_chunked_update", self.ctx.handle, byref(self.struct), _ptr(self.weight),
@@ -930,6 +938,14 @@ class PredictiveCodingNet:
 
     def iteration(self) -> None:
         self.forward()
+        if self.layout == "chunked":
+            # the value-node update runs in the backward folds' epilogue:
+            # nothing reads x or act between the two in an inference step
+            for l, ch in self.bwd.items():
+                ch.fold_ipc_value(self._layer(self.err, l + 1), self._layer(self.x, l),
+                                  self._layer(self.err, l), self._layer(self.act, l),
+                                  self.gamma)
+            return
         self.backward()
         self.value_update()
 

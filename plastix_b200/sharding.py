@@ -242,21 +242,17 @@ class ShardedPCNet:
                  None, None, 0.0, _ptr(self.own(self.act, l)), 0)
 
     def iteration(self) -> None:
-        from .runtime import _ptr, call
-
         A = self._abi
         self.allgather_layers(self.act)
         for l, ch in enumerate(self.fwd):
             ch.fold(self.layer(self.act, l), self.own(self.err, l + 1), A.APPLY_IPC_ERROR,
                     value=self.own(self.x, l + 1))
         self.allgather_layers(self.err)
+        # backward folds with the value-node update of the owned hidden
+        # units in their epilogue (every hidden layer has one backward block)
         for l, ch in self.bwd.items():
-            ch.fold(self.layer(self.err, l + 1), self.own(self.bu, l), A.APPLY_TANH_GRAD,
-                    value=self.own(self.x, l))
-        for l in range(1, self.L - 1):
-            call("plx_ipc_value_update", self.ctx.handle, self.m, _ptr(self.own(self.x, l)),
-                 _ptr(self.own(self.err, l)), _ptr(self.own(self.bu, l)), self.gamma,
-                 _ptr(self.own(self.act, l)), 1)
+            ch.fold_ipc_value(self.layer(self.err, l + 1), self.own(self.x, l),
+                              self.own(self.err, l), self.own(self.act, l), self.gamma)
 
     def update(self) -> None:
         A = self._abi

@@ -105,6 +105,33 @@ def test_chunked_fold_matches_oracle(ctx, orc, apply):
     np.testing.assert_allclose(host(out), want, rtol=1e-5, atol=2e-5)
 
 
+@pytest.mark.parametrize("n_src,n_rows,n", [(50_000, 3000, 3_000_000), (700, 5, 2000),
+                                            (CH * 3 + 1, 1, 40_000)])
+def test_fold_with_fused_value_update_equals_separate_calls(ctx, n_src, n_rows, n):
+    """The iPC backward fold with the value-node update in its epilogue
+    (plx_chunked_fold_ipc_value) leaves x and act equal bit for bit to the
+    separate fold (TANH_GRAD into bu) + plx_ipc_value_update (mode 1)."""
+    src, rows, w = layer(n_src, n_rows, n, seed=n_rows)
+    rng = np.random.default_rng(n)
+    err_src = rng.uniform(-1, 1, n_src).astype(np.float32)
+    x0 = rng.uniform(-2, 2, n_rows).astype(np.float32)
+    eps = rng.uniform(-1, 1, n_rows).astype(np.float32)
+    L = ChunkedRows(ctx, dev(src), dev(rows), dev(w), 0, n_src, n_src, n_rows)
+    # separate
+    x_a, act_a, bu = dev(x0), torch.zeros(n_rows, device="cuda"), torch.zeros(n_rows, device="cuda")
+    L.fold(dev(err_src), bu, _abi.APPLY_TANH_GRAD, value=x_a)
+    _abi.check(_abi.lib().plx_ipc_value_update(ctx.handle, n_rows, x_a.data_ptr(),
+                                               dev(eps).data_ptr(), bu.data_ptr(), 0.1,
+                                               act_a.data_ptr(), 1), "plx_ipc_value_update")
+    # fused
+    x_b, act_b = dev(x0), torch.zeros(n_rows, device="cuda")
+    L.fold_ipc_value(dev(err_src), x_b, dev(eps), act_b, 0.1)
+    ctx.sync()
+    np.testing.assert_array_equal(host(x_b), host(x_a))
+    np.testing.assert_array_equal(host(act_b), host(act_a))
+    assert np.all(host(bu) == 0)  # the separate update zeroes bu; the fused one never writes it
+
+
 @pytest.mark.parametrize("kind", [_abi.UPDATE_GRADIENT, _abi.UPDATE_HEBBIAN])
 def test_chunked_update_equals_csr_update(ctx, kind):
     n_src, n_rows, n = 40_000, 1500, 1_200_000
