@@ -209,9 +209,14 @@ __global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const 
 }
 
 // Apply of the units in [lo, hi) (only those at level `lvl` when lvl >= 0),
-// then the accumulator is reset.
+// then the accumulator is reset. With `mse` (the targets of the output units
+// [out_lo, out_hi)), MSELoss runs in the same thread right after an output
+// unit's Apply: BackwardAcc = pred - target (traits.hpp MSELoss, the
+// reference's DoCalculateLoss after DoForwardPass -- an output unit's
+// activation is final once its Apply has run).
 template <class Tr, class UV, class G>
-__global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
+__global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl, const float *mse,
+                            size_t out_lo, size_t out_hi) {
   using FP = typename Tr::ForwardPass;
   using Acc = typename FP::Accumulator;
   const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
@@ -219,6 +224,15 @@ __global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
   if (lvl >= 0 && GetLevel(U, I) != lvl) return;
   FP::Apply(U, I, *g, GetForwardAcc(U, I));
   GetForwardAcc(U, I) = Acc{};
+  if (mse && I >= out_lo && I < out_hi) GetBackwardAcc(U, I) = GetActivation(U, I) - mse[I - out_lo];
+}
+
+// MSELoss over the output units, one thread per unit (the loss is
+// elementwise, so this equals the reference's loop bit for bit).
+template <class UV>
+__global__ void k_loss_mse(UV U, size_t out_lo, size_t out_n, const float *t) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < out_n) GetBackwardAcc(U, out_lo + i) = GetActivation(U, out_lo + i) - t[i];
 }
 
 // Backward accumulation: unit I folds its outgoing connections into its
@@ -650,7 +664,8 @@ template <typename Traits> class Network {
       for (int L = 1; L <= NumLevels; ++L) {
         detail::k_fwd_acc_level<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
             UV(), CV(), d_g, d_in_ptr, d_in_conn, d_cursor, n, L);
-        detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, L);
+        detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
+            UV(), d_g, NumInput, n, L, MseTargets, OutputRange.Begin, OutputRange.End);
       }
     } else {
       using Acc = typename FP::Accumulator;
@@ -664,7 +679,8 @@ template <typename Traits> class Network {
         detail::k_fwd_acc<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), CV(), d_g,
                                                                           d_in_ptr, d_in_conn, n);
       }
-      detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(UV(), d_g, NumInput, n, -1);
+      detail::k_fwd_apply<Traits><<<detail::blocks(n), 256, 0, Stream>>>(
+          UV(), d_g, NumInput, n, -1, MseTargets, OutputRange.Begin, OutputRange.End);
     }
     cuda_check(cudaGetLastError(), "forward pass");
     EndDevice(true, true);
@@ -675,15 +691,18 @@ template <typename Traits> class Network {
     if constexpr (!std::is_same_v<typename Traits::Loss, NoLoss>) {
       if (Targets.empty()) return;
       BeginDevice();
-      if (Targets.size() > TargetCap) {
-        cuda_check(cudaStreamSynchronize(Stream), "targets");
-        if (d_targets) cudaFree(d_targets);
-        cuda_check(cudaMalloc(&d_targets, Targets.size() * sizeof(float)), "targets");
-        TargetCap = Targets.size();
+      UploadTargets(Targets);
+      if constexpr (std::is_same_v<typename Traits::Loss, MSELoss>) {
+        if (Targets.size() >= OutputRange.Size()) {
+          const size_t k = OutputRange.Size();
+          if (k)
+            detail::k_loss_mse<<<detail::blocks(k), 256, 0, Stream>>>(UV(), OutputRange.Begin, k,
+                                                                       d_targets);
+          cuda_check(cudaGetLastError(), "loss");
+          EndDevice(true, false);
+          return;
+        }
       }
-      cuda_check(cudaMemcpyAsync(d_targets, Targets.data(), Targets.size() * sizeof(float),
-                                 cudaMemcpyHostToDevice, Stream),
-                 "targets");
       detail::k_loss<Traits><<<1, 1, 0, Stream>>>(UV(), d_g, OutputRange, d_targets,
                                                   Targets.size());
       cuda_check(cudaGetLastError(), "loss");
@@ -820,8 +839,20 @@ template <typename Traits> class Network {
     if constexpr (detail::fused_hebbian_traits<Traits>()) {
       if (FusedStep(Inputs)) return;
     }
-    DoForwardPass(Inputs);
-    DoCalculateLoss(Targets);
+    // MSELoss rides in the forward pass's Apply epilogue (Pipeline, parallel
+    // passes): no separate loss launch, no second read of the outputs.
+    constexpr bool mse_in_apply = std::is_same_v<typename Traits::Loss, MSELoss> &&
+                                  Traits::Model == Propagation::Pipeline &&
+                                  detail::read_only_globals<Traits>();
+    if (mse_in_apply && !Targets.empty() && Targets.size() >= OutputRange.Size() &&
+        OutputRange.Begin >= NumInput) {
+      MseTargets = UploadTargets(Targets);
+      DoForwardPass(Inputs);
+      MseTargets = nullptr;
+    } else {
+      DoForwardPass(Inputs);
+      DoCalculateLoss(Targets);
+    }
     DoBackwardPass();
     DoUpdateUnitState();
     DoUpdateConnectionState();
@@ -1455,6 +1486,21 @@ template <typename Traits> class Network {
     CA.AllocateMany(k);
     DevConns = m + k;
   }
+
+  const float *UploadTargets(std::span<const float> Targets) {
+    if (Targets.size() > TargetCap) {
+      cuda_check(cudaStreamSynchronize(Stream), "targets");
+      if (d_targets) cudaFree(d_targets);
+      d_targets = nullptr;
+      cuda_check(cudaMalloc(&d_targets, Targets.size() * sizeof(float)), "targets");
+      TargetCap = Targets.size();
+    }
+    cuda_check(cudaMemcpyAsync(d_targets, Targets.data(), Targets.size() * sizeof(float),
+                               cudaMemcpyHostToDevice, Stream),
+               "targets");
+    return d_targets;
+  }
+  const float *MseTargets = nullptr;  // set while DoStep runs MSELoss in the Apply
 
   // Input activations to the device. Large inputs go through two pinned
   // staging buffers, so the host copy of step k + 1 overlaps the device work

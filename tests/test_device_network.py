@@ -16,6 +16,9 @@ the reference header library, against the reference-made fixtures:
   connection proposals, commit with InitConnection, Topological re-sort with
   RecomputeLevels) on a small and a medium network: every output, connection
   field and unit level bit for bit (the medium case through digests).
+* network_mse_fusion.cu -- the library MSELoss fused into the forward
+  Apply (Pipeline DoStep) and run per output in parallel, against a user
+  loss with the same body: bit for bit.
 
 On the CPU the programs are compiled (nvcc cross-compiles for sm_100a)."""
 import subprocess
@@ -51,9 +54,21 @@ def parse(out: str):
 
 
 @pytest.mark.parametrize("name", ["network_xor", "network_ipc", "network_swifttd",
-                                  "network_structural"])
+                                  "network_structural", "network_mse_fusion"])
 def test_device_network_programs_compile(tmp_path, name):
     assert compile_prog(name, tmp_path).exists()
+
+
+@pytest.mark.gpu
+def test_mse_loss_in_apply_epilogue_equals_user_loss(tmp_path):
+    """plastix::MSELoss run in the forward Apply epilogue (Pipeline DoStep)
+    or as a parallel kernel (DoCalculateLoss, Topological DoStep) leaves the
+    network bit for bit where a user loss with the same body (the generic
+    one-thread loss hook) leaves it."""
+    exe = compile_prog("network_mse_fusion", tmp_path)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.strip() == "ok"
 
 
 @pytest.mark.gpu
