@@ -400,16 +400,21 @@ def run_ours(args):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     up.wait_event(e0)
+    h0 = time.perf_counter()
     for i in range(args.steps):
         e2e_step(i)
     stream.wait_event(out_free[(args.steps - 1) & 1])  # the last read-back is inside
     e1.record(stream)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # enqueue cost per step
     barrier_sync()
     ems = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ems], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ems = float(t[0])
+        t = torch.tensor([host_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        host_ms = float(t[0])
     e2e_value = world * n_edges * args.steps / (ems / 1e3)
     ctx.sync()
 
@@ -458,7 +463,8 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": 4 * n_in * world,
-                "d2h_bytes_per_step": 4 * n_dst * world},
+                "d2h_bytes_per_step": 4 * n_dst * world,
+                "ms_per_step": ems / args.steps, "host_enqueue_ms_per_step": host_ms},
         "clocks": clocks,
         "gpu_launches": args.steps * (2 if p2p else 1),
     }
