@@ -65,14 +65,16 @@ def parse_args():
                    help="units per layer of the ipc workload (2^18 in the configuration)")
     p.add_argument("--ipc-fan-in", type=int, default=2048)
     p.add_argument("--workload",
-                   choices=["sweep", "swifttd", "ipc", "structural", "ceiling", "levels", "api"],
+                   choices=["sweep", "swifttd", "ipc", "structural", "ceiling", "levels", "api",
+                            "xor"],
                    default="sweep",
                    help="sweep: the single-layer fwd+Hebbian sweep (default, the headline); "
                         "swifttd: 4M-feature SwiftTD learner; ipc: 5-layer predictive-coding "
                         "net; structural: prune/regrow/re-sort/forward step; ceiling: the sweep "
                         "beside the same traffic without row folds and random gathers alone; "
                         "levels: RecomputeLevels + SortConnectionsByLevel at 2^24 connections; "
-                        "api: the sweep through plastix::Network<Traits>::DoStep")
+                        "api: the sweep through plastix::Network<Traits>::DoStep; "
+                        "xor: the XOR MLP training run (launch-bound, DoSteps/s)")
     return p.parse_args()
 
 
@@ -1045,11 +1047,65 @@ def bench_api(args):
     return 0
 
 
+def bench_xor(args):
+    """The XOR MLP (2 -> 8 -> 1 sigmoid, MSE, backward, gradient step at 0.5;
+    5,000 epochs of four DoSteps, each followed by GetOutput) through the
+    device Network: plastix_b200/apps/xor_train.cu, with DoStep replayed as a
+    CUDA graph (the value) and with every kernel launched (in the config).
+    A 24-connection network is launch- and latency-bound: the number is
+    DoSteps per second of wall time around the epoch loop, host inputs in and
+    the output read back every step. The baseline is the same program built
+    against the reference's headers (oracle/_ref/xor_train) on one core."""
+    from plastix_b200 import build
+
+    exe = build.app_path("xor_train")
+    if not exe.exists():
+        exe = build.build_app("xor_train")
+    epochs = 5000
+
+    def run(cmd):
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        if r.returncode != 0:
+            raise SystemExit(f"{cmd[0]} failed:\n{r.stdout}\n{r.stderr}")
+        return json.loads(r.stdout.strip().splitlines()[-1])
+
+    cpu = None
+    ref = ROOT / "oracle" / "_ref" / "xor_train"
+    if ref.exists() and not args.no_cpu_baseline:
+        best = min(run([str(ref), str(epochs)])["train_s"] for _ in range(3))
+        cpu = {"value": 4 * epochs / best, "unit": "steps/s", "cores": 1, "kind": "reference",
+               "sample": f"the whole run: {epochs} epochs, {4 * epochs} DoSteps (best of 3)"}
+    if args.impl == "reference":
+        if cpu is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/xor_train "
+                              "was not built (the reference tree was absent at build time)"}))
+            return 0
+        _line(args, "xor", cpu["value"], "steps/s", 1e3 / cpu["value"], {"workload": "xor"},
+              None, cpu, None, None, None)
+        return 0
+    sampler = ClockSampler(0)
+    g = run([str(exe), str(epochs), "graph"])
+    clocks = sampler.stop()
+    e = run([str(exe), str(epochs), "eager"])
+    steps = g["steps"]
+    value = steps / g["train_s"]
+    config = {"workload": "XOR MLP training through Network<Traits>::DoStep (2 -> 8 -> 1 "
+                          "sigmoid, MSE, backward, gradient descent, Topological)",
+              "epochs": epochs, "do_steps": steps, "graph_replay": True,
+              "eager_steps_per_s": e["steps"] / e["train_s"], "final_loss": g["final_loss"],
+              "xor_solved": g["pass"] and e["pass"]}
+    e2e = {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4}
+    _line(args, "xor", value, "steps/s", 1e3 * g["train_s"] / steps, config, None, cpu, e2e,
+          clocks, None)
+    return 0
+
+
 def run_other(args):
     if args.gpus != 1 and args.workload not in ("ipc", "structural"):
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
     return {"swifttd": bench_swifttd, "ipc": bench_ipc, "structural": bench_structural,
-            "ceiling": bench_ceiling, "levels": bench_levels, "api": bench_api}[args.workload](
+            "ceiling": bench_ceiling, "levels": bench_levels, "api": bench_api,
+            "xor": bench_xor}[args.workload](
                 args) or 0
 
 

@@ -539,6 +539,14 @@ static __global__ void k_level_ranges(const uint32_t *keys, size_t m, uint32_t *
 
 // Traits the fused single-layer sweep serves: Pipeline, DefaultForwardPass
 // with HebbianTraceUpdate, no other hook, float Weight and Trace fields.
+// Traits without structural hooks: every DoStep launches the same kernels.
+template <class T> constexpr bool fixed_structure() {
+  return std::is_same_v<typename T::PruneUnit, NoPruneUnit> &&
+         std::is_same_v<typename T::PruneConn, NoPruneConn> &&
+         std::is_same_v<typename T::AddUnit, NoAddUnit> &&
+         std::is_same_v<typename T::AddConn, NoAddConn>;
+}
+
 template <class T> struct IsHebbianTrace : std::false_type {};
 template <float D, float R> struct IsHebbianTrace<HebbianTraceUpdate<D, R>> : std::true_type {};
 template <class T> constexpr bool fused_hebbian_traits() {
@@ -839,6 +847,24 @@ template <typename Traits> class Network {
     if constexpr (detail::fused_hebbian_traits<Traits>()) {
       if (FusedStep(Inputs)) return;
     }
+    if constexpr (detail::fixed_structure<Traits>()) {
+      if (UseGraphs && GraphStep(Inputs, Targets)) return;
+      StepBody(Inputs, Targets);
+      if (UseGraphs) EagerKey = StepKey(Targets);
+    } else {
+      StepBody(Inputs, Targets);
+    }
+  }
+
+  // Replays of DoStep as a CUDA graph (on by default): a network whose traits
+  // have no structural hooks launches the same kernels every step, so after
+  // one ordinary step with the same device buffers the step is captured once
+  // and then launched as one graph -- only the input and target uploads stay
+  // outside it. Any change of a device buffer, the level count or the number
+  // of targets falls back to an ordinary step and a new capture.
+  void SetGraphReplay(bool On) { UseGraphs = On; }
+
+  void StepBody(std::span<const float> Inputs, std::span<const float> Targets) {
     // MSELoss rides in the forward pass's Apply epilogue (Pipeline, parallel
     // passes): no separate loss launch, no second read of the outputs.
     constexpr bool mse_in_apply = std::is_same_v<typename Traits::Loss, MSELoss> &&
@@ -909,6 +935,10 @@ template <typename Traits> class Network {
   }
   void SetStream(cudaStream_t s) {
     cuda_check(cudaStreamSynchronize(Stream), "stream");
+    if (OwnStream && s != OwnStream) {
+      cudaStreamDestroy(OwnStream);
+      OwnStream = nullptr;
+    }
     Stream = s;
     if (Ctx) plx_check(plx_ctx_set_stream(Ctx, s), "plx_ctx_set_stream");
   }
@@ -1488,6 +1518,7 @@ template <typename Traits> class Network {
   }
 
   const float *UploadTargets(std::span<const float> Targets) {
+    if (Capturing) return d_targets;  // uploaded before each replay
     if (Targets.size() > TargetCap) {
       cuda_check(cudaStreamSynchronize(Stream), "targets");
       if (d_targets) cudaFree(d_targets);
@@ -1509,7 +1540,7 @@ template <typename Traits> class Network {
   // that read it have completed.
   void UploadInputs(std::span<const float> Inputs) {
     const size_t k = std::min(Inputs.size(), NumInput);
-    if (!k) return;
+    if (!k || Capturing) return;
     const size_t bytes = k * sizeof(float);
     if (bytes < (size_t(256) << 10)) {
       cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], Inputs.data(), bytes,
@@ -1551,6 +1582,87 @@ template <typename Traits> class Network {
   };
   Staging Stage[2];
   int StageNext = 0;
+
+  // ---- DoStep as a CUDA graph -------------------------------------------------
+  // Everything a captured step depends on besides the field contents: device
+  // buffers, sizes, the level count, the index layout, the number of targets.
+  std::vector<uintptr_t> StepKey(std::span<const float> Targets) const {
+    std::vector<uintptr_t> k;
+    for (void *p : d_uf) k.push_back(reinterpret_cast<uintptr_t>(p));
+    for (void *p : d_cf) k.push_back(reinterpret_cast<uintptr_t>(p));
+    for (const void *p : {(const void *)d_g, (const void *)d_in_ptr, (const void *)d_out_ptr,
+                          (const void *)d_in_conn, (const void *)d_out_conn, (const void *)d_cursor,
+                          (const void *)d_ranges, (const void *)d_targets})
+      k.push_back(reinterpret_cast<uintptr_t>(p));
+    for (void *p : Scratch) k.push_back(reinterpret_cast<uintptr_t>(p));
+    for (size_t v : {UA.Size(), CA.Size(), (size_t)NumLevels, (size_t)DstMajor, Targets.size(),
+                     NumInput})
+      k.push_back(v);
+    return k;
+  }
+
+  bool GraphStep(std::span<const float> Inputs, std::span<const float> Targets) {
+    BeginDevice();
+    if (IndexStale || NeedsResort) return false;
+    const std::vector<uintptr_t> key = StepKey(Targets);
+    if (!(GraphExec && key == GraphKey)) {
+      if (key != EagerKey) return false;  // one ordinary step with these buffers first
+      if (!CaptureStep(Targets)) {
+        UseGraphs = false;
+        return false;
+      }
+      GraphKey = key;
+    }
+    UploadInputs(Inputs);
+    if constexpr (!std::is_same_v<typename Traits::Loss, NoLoss>)
+      if (!Targets.empty()) UploadTargets(Targets);
+    cuda_check(cudaGraphLaunch(GraphExec, Stream), "graph launch");
+    EndDevice(true, true);
+    ++Step;
+    return true;
+  }
+
+  // Captures StepBody (without its uploads) on the network's stream; false,
+  // with nothing left behind, if the capture or the instantiation fails.
+  bool CaptureStep(std::span<const float> Targets) {
+    if (!Stream) {  // the legacy default stream cannot be captured
+      cudaStream_t s = nullptr;
+      cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamDefault), "stream");
+      SetStream(s);
+      OwnStream = s;
+    }
+    if (GraphExec) cudaGraphExecDestroy(GraphExec);
+    GraphExec = nullptr;
+    if (cudaStreamBeginCapture(Stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    const size_t step0 = Step;
+    bool ok = true;
+    Capturing = true;
+    try {
+      StepBody({}, Targets);
+    } catch (...) {
+      ok = false;
+    }
+    Capturing = false;
+    Step = step0;
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(Stream, &g);
+    if (ok && e == cudaSuccess && g) ok = cudaGraphInstantiate(&GraphExec, g, 0) == cudaSuccess;
+    else ok = false;
+    if (g) cudaGraphDestroy(g);
+    if (!ok) {
+      GraphExec = nullptr;
+      cudaGetLastError();
+    }
+    return ok;
+  }
+
+  bool UseGraphs = true, Capturing = false;
+  cudaGraphExec_t GraphExec = nullptr;
+  std::vector<uintptr_t> GraphKey, EagerKey;
+  cudaStream_t OwnStream = nullptr;
 
   // ---- the fused single-layer step (HebbianTraceUpdate traits) -------------
   // The layer is re-laid once into warp-sliced rows (plx_sliced_*); each
@@ -1660,6 +1772,10 @@ template <typename Traits> class Network {
   void Release() {
     if (Stream) cudaStreamSynchronize(Stream);
     else cudaDeviceSynchronize();
+    if (GraphExec) cudaGraphExecDestroy(GraphExec);
+    GraphExec = nullptr;
+    if (OwnStream) cudaStreamDestroy(OwnStream);
+    OwnStream = nullptr;
     for (void *p : Fused.Mem)
       if (p) cudaFree(p);
     if (OutHost) cudaFreeHost(OutHost);

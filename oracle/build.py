@@ -16,6 +16,8 @@
   4)`` of ``include/plastix/plastix.hpp`` become calls into the harness, so
   networks of the benchmark sizes fit. The patched header copy lives in a
   temporary directory and is deleted after the build.
+* ``oracle/_ref/xor_train`` — ``plastix_b200/apps/xor_train.cu`` (the XOR
+  training run) built with g++ against the unchanged reference headers.
 """
 from __future__ import annotations
 
@@ -88,9 +90,32 @@ def build_reference() -> Path | None:
     return REF_SO
 
 
+XOR_SRC = HERE.parent / "plastix_b200" / "apps" / "xor_train.cu"
+REF_XOR = REF_DIR / "xor_train"
+
+
+def build_reference_xor() -> Path | None:
+    """``oracle/_ref/xor_train``: the XOR training program of
+    ``plastix_b200/apps/xor_train.cu`` compiled with g++ against the
+    reference's own, unchanged headers (and ``src/plastix.cpp``) -- the
+    reference's CPU implementation of that run, the benchmark's baseline."""
+    hpp = REF_ROOT / "include" / "plastix" / "plastix.hpp"
+    if not hpp.exists():
+        return REF_XOR if REF_XOR.exists() else None
+    deps = [XOR_SRC, Path(__file__)] + sorted((REF_ROOT / "include" / "plastix").glob("*.hpp"))
+    if _stale(REF_XOR, deps):
+        REF_DIR.mkdir(exist_ok=True)
+        cmd = ["g++", "-std=c++20", "-O2", "-x", "c++", f"-I{REF_ROOT / 'include'}",
+               str(XOR_SRC), "-x", "none", str(REF_ROOT / "src" / "plastix.cpp"), "-o",
+               str(REF_XOR)]
+        subprocess.run(cmd, check=True)
+    return REF_XOR
+
+
 def build() -> None:
     build_oracle()
     build_reference()
+    build_reference_xor()
 
 
 if __name__ == "__main__":

@@ -24,7 +24,8 @@ LIB = PKG / "libplastix_b200.so"
 PROBE_SRC = PKG / "probe" / "probe.cu"
 PROBE_LIB = PKG / "libplastix_probe.so"
 # Programs written against the reference's C++ API (include/plastix/*.hpp).
-APPS = {"network_sweep": PKG / "apps" / "network_sweep.cu"}
+APPS = {"network_sweep": PKG / "apps" / "network_sweep.cu",
+        "xor_train": PKG / "apps" / "xor_train.cu"}
 APP_FLAGS = ["-std=c++20", "--expt-relaxed-constexpr", "-O2", "--fmad=false", "-lineinfo",
              "-diag-suppress=20050", f"-I{ROOT / 'include'}"]
 

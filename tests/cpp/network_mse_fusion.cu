@@ -1,7 +1,8 @@
-// MSELoss inside the device Network<Traits>: the library's MSELoss runs in
-// the forward pass's Apply epilogue under DoStep (Pipeline) and as a parallel
-// per-output kernel under DoCalculateLoss; a user loss with the same body is
-// not recognised and runs as the generic one-thread loss hook. All of them
+// MSELoss and graph replay inside the device Network<Traits>: the library's
+// MSELoss runs in the forward pass's Apply epilogue under DoStep (Pipeline)
+// and as a parallel per-output kernel under DoCalculateLoss; a user loss with
+// the same body is not recognised and runs as the generic one-thread loss
+// hook; DoStep replays a captured CUDA graph unless told not to. All of them
 // must leave every weight, activation, gradient and backward accumulator
 // equal bit for bit. The network: 3 inputs -> 48 sigmoid hidden -> 20 sigmoid
 // outputs, backward pass and gradient step, 40 DoSteps on seeded inputs and
@@ -77,10 +78,12 @@ struct Snapshot {
   std::vector<float> w, act, grad, bwd;
 };
 
-// split: the step as separate Do* calls (DoCalculateLoss on its own).
-template <class T> Snapshot run(bool split) {
+// split: the step as separate Do* calls (DoCalculateLoss on its own);
+// graphs: DoStep may replay a captured CUDA graph (the default).
+template <class T> Snapshot run(bool split, bool graphs = true) {
   plastix::Network<T> Net(kIn, plastix::FullyConnected{kHidden, plastix::RandomUniformWeight{7}},
                           plastix::FullyConnected{kOut, plastix::RandomUniformWeight{8}});
+  Net.SetGraphReplay(graphs);
   uint32_t h = 12345u;
   auto next = [&h] {
     h = h * 1664525u + 1013904223u;
@@ -136,11 +139,19 @@ int main() {
                    run<Traits<MSELoss, Propagation::Pipeline>>(false), user);
     bad += compare("pipeline DoCalculateLoss (parallel loss)",
                    run<Traits<MSELoss, Propagation::Pipeline>>(true), user);
+    bad += compare("pipeline DoStep without graph replay",
+                   run<Traits<MSELoss, Propagation::Pipeline>>(false, false), user);
+    bad += compare("pipeline DoStep, user loss, without graph replay",
+                   run<Traits<UserMSE, Propagation::Pipeline>>(false, false), user);
   }
   {
     const Snapshot user = run<Traits<UserMSE, Propagation::Topological>>(false);
     bad += compare("topological DoStep (parallel loss)",
                    run<Traits<MSELoss, Propagation::Topological>>(false), user);
+    bad += compare("topological DoStep without graph replay",
+                   run<Traits<MSELoss, Propagation::Topological>>(false, false), user);
+    bad += compare("topological DoCalculateLoss (parallel loss)",
+                   run<Traits<MSELoss, Propagation::Topological>>(true), user);
   }
   if (!bad) std::printf("ok\n");
   return bad;
