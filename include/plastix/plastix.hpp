@@ -1526,62 +1526,62 @@ template <typename Traits> class Network {
       cuda_check(cudaMalloc(&d_targets, Targets.size() * sizeof(float)), "targets");
       TargetCap = Targets.size();
     }
-    cuda_check(cudaMemcpyAsync(d_targets, Targets.data(), Targets.size() * sizeof(float),
-                               cudaMemcpyHostToDevice, Stream),
-               "targets");
+    if (!Targets.empty())
+      StagedUpload(d_targets, Targets.data(), Targets.size() * sizeof(float), TargetStage);
     return d_targets;
   }
   const float *MseTargets = nullptr;  // set while DoStep runs MSELoss in the Apply
 
-  // Input activations to the device. Large inputs go through two pinned
-  // staging buffers, so the host copy of step k + 1 overlaps the device work
-  // of step k and the transfer runs at pinned-memory speed, piece by piece
-  // behind the host copy; each buffer is reused only after the transfers
-  // that read it have completed.
+  // Input activations to the device (skipped while a step is being captured:
+  // graph replays upload them before each launch).
   void UploadInputs(std::span<const float> Inputs) {
     const size_t k = std::min(Inputs.size(), NumInput);
     if (!k || Capturing) return;
-    const size_t bytes = k * sizeof(float);
-    if (bytes < (size_t(256) << 10)) {
-      cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], Inputs.data(), bytes,
-                                 cudaMemcpyHostToDevice, Stream),
-                 "inputs");
-      return;
-    }
-    Staging &b = Stage[StageNext];
-    StageNext ^= 1;
-    if (b.Bytes < bytes) {
-      if (b.Host) {
-        cuda_check(cudaEventSynchronize(b.Done), "inputs");
-        cudaFreeHost(b.Host);
-      }
-      cuda_check(cudaMallocHost(&b.Host, bytes), "inputs");
-      b.Bytes = bytes;
-      if (!b.Done) cuda_check(cudaEventCreateWithFlags(&b.Done, cudaEventDisableTiming), "inputs");
-    } else {
-      cuda_check(cudaEventSynchronize(b.Done), "inputs");
-    }
-    // in 1 MiB pieces: the transfer of piece i runs while piece i + 1 is
-    // copied into the staging buffer
-    constexpr size_t piece = size_t(1) << 20;
-    auto *src = reinterpret_cast<const char *>(Inputs.data());
-    auto *host = static_cast<char *>(b.Host);
-    auto *dev = static_cast<char *>(d_uf[core::kActivation]);
-    for (size_t off = 0; off < bytes; off += piece) {
-      const size_t len = std::min(piece, bytes - off);
-      std::memcpy(host + off, src + off, len);
-      cuda_check(cudaMemcpyAsync(dev + off, host + off, len, cudaMemcpyHostToDevice, Stream),
-                 "inputs");
-    }
-    cuda_check(cudaEventRecord(b.Done, Stream), "inputs");
+    StagedUpload(d_uf[core::kActivation], Inputs.data(), k * sizeof(float), InStage);
   }
   struct Staging {
     void *Host = nullptr;
     size_t Bytes = 0;
     cudaEvent_t Done = nullptr;
   };
-  Staging Stage[2];
-  int StageNext = 0;
+  struct StagingPair {
+    Staging B[2];
+    int Next = 0;
+  };
+  // Host -> device through two pinned staging buffers used in turn: the
+  // transfer is asynchronous at pinned-memory speed, the host copy of the
+  // next call overlaps the device work of this one, and a buffer is reused
+  // only once the transfers that read it have completed. Large transfers go
+  // in 1 MiB pieces, each sent while the next is copied into the buffer.
+  void StagedUpload(void *dst, const void *src_host, size_t bytes, StagingPair &pair) {
+    Staging &b = pair.B[pair.Next];
+    pair.Next ^= 1;
+    if (b.Bytes < bytes) {
+      if (b.Host) {
+        cuda_check(cudaEventSynchronize(b.Done), "upload");
+        cudaFreeHost(b.Host);
+        b.Host = nullptr;
+        b.Bytes = 0;
+      }
+      cuda_check(cudaMallocHost(&b.Host, std::max<size_t>(bytes, 256)), "upload");
+      b.Bytes = std::max<size_t>(bytes, 256);
+      if (!b.Done) cuda_check(cudaEventCreateWithFlags(&b.Done, cudaEventDisableTiming), "upload");
+    } else {
+      cuda_check(cudaEventSynchronize(b.Done), "upload");
+    }
+    constexpr size_t piece = size_t(1) << 20;
+    auto *src = static_cast<const char *>(src_host);
+    auto *host = static_cast<char *>(b.Host);
+    auto *dev = static_cast<char *>(dst);
+    for (size_t off = 0; off < bytes; off += piece) {
+      const size_t len = std::min(piece, bytes - off);
+      std::memcpy(host + off, src + off, len);
+      cuda_check(cudaMemcpyAsync(dev + off, host + off, len, cudaMemcpyHostToDevice, Stream),
+                 "upload");
+    }
+    cuda_check(cudaEventRecord(b.Done, Stream), "upload");
+  }
+  StagingPair InStage, TargetStage;
 
   // ---- DoStep as a CUDA graph -------------------------------------------------
   // Everything a captured step depends on besides the field contents: device
@@ -1780,11 +1780,12 @@ template <typename Traits> class Network {
       if (p) cudaFree(p);
     if (OutHost) cudaFreeHost(OutHost);
     OutHost = nullptr;
-    for (Staging &b : Stage) {
-      if (b.Host) cudaFreeHost(b.Host);
-      if (b.Done) cudaEventDestroy(b.Done);
-      b = Staging{};
-    }
+    for (StagingPair *pair : {&InStage, &TargetStage})
+      for (Staging &b : pair->B) {
+        if (b.Host) cudaFreeHost(b.Host);
+        if (b.Done) cudaEventDestroy(b.Done);
+        b = Staging{};
+      }
     for (void *p : d_uf) cudaFree(p);
     for (void *p : d_cf) cudaFree(p);
     for (void *p : {(void *)d_g, (void *)d_in_ptr, (void *)d_out_ptr, (void *)d_in_conn,
