@@ -51,6 +51,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-secondary", action="store_true",
+                   help="N = 1: skip the other workloads' summaries in the headline line")
     p.add_argument("--handoff", choices=["p2p", "nccl"], default="p2p",
                    help="N > 1: hand the destination slices to every GPU with the sweep's "
                         "own stores over NVLink (p2p) or with an NCCL all-gather after it")
@@ -470,8 +472,46 @@ def run_ours(args):
         "clocks": clocks,
         "gpu_launches": args.steps * (2 if p2p else 1),
     }
+    if world == 1 and not args.no_secondary:
+        ctx.sync()
+        line["secondary"] = run_secondary()
     print(json.dumps(line), flush=True)
     return 0
+
+
+# The other workloads, each run once in its own process after the headline
+# measurement (one GPU): their own lines, summarised into the headline's
+# "secondary" field, so that one default run records every configuration.
+SECONDARY = ("swifttd", "structural", "levels", "ipc", "api", "xor")
+
+
+def run_secondary() -> dict:
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT")}
+    out = {}
+    for name in SECONDARY:
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--workload", name, "--no-cpu-baseline",
+               "--warmup", "3"]
+        t0 = time.perf_counter()
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+            lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+            if r.returncode != 0 or not lines:
+                out[name] = {"error": (r.stderr or r.stdout)[-300:]}
+                continue
+            d = json.loads(lines[-1])
+            roof = d.get("roofline") or {}
+            e2e = d.get("e2e") or {}
+            clk = d.get("clocks") or {}
+            out[name] = {"metric": d.get("metric"), "value": d.get("value"), "unit": d.get("unit"),
+                         "ms_per_step": d.get("ms_per_step"),
+                         "roofline_frac": roof.get("frac"), "e2e": e2e.get("value"),
+                         "workload": (d.get("config") or {}).get("workload"),
+                         "sm_mhz": clk.get("sm_mhz"), "clock_reasons": clk.get("reasons"),
+                         "wall_s": round(time.perf_counter() - t0, 1)}
+        except Exception as exc:  # one failing workload must not lose the headline
+            out[name] = {"error": str(exc)[-300:]}
+    return out
 
 
 # ---------------------------------------------------------------------------

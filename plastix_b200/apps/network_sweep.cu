@@ -225,7 +225,7 @@ int bench(uint64_t n_src, uint64_t n_dst, uint64_t n, uint64_t seed, int steps, 
   const double e2e_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - h0).count();
   std::printf("{\"device_ms_per_step\": %.6f, \"e2e_ms_per_step\": %.6f, \"steps\": %d, "
-              "\"n_edges\": %llu, \"build_s\": %.2f, \"checksum\": %.6e}\n",
+              "\"n_edges\": %llu, \"build_s\": %.2f, \"checksum\": \"%.6e\"}\n",
               dev_ms / steps, e2e_ms / steps, steps, (unsigned long long)n, build_s, checksum);
   return 0;
 }
