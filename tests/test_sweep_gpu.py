@@ -214,7 +214,8 @@ def test_full_size_sweep_matches_oracle(ctx, orc):
     np.testing.assert_array_equal(host(layer.trace), ee)
 
 
-@pytest.mark.parametrize("case", ["dense", "gaps", "outside", "tail", "big"])
+@pytest.mark.parametrize("case", ["dense", "gaps", "outside", "tail", "big", "leading",
+                                  "none"])
 def test_row_ptr_equals_searchsorted(ctx, case):
     """plx_csr_row_ptr: row_ptr[r] = first connection whose ToId >= row_base + r
     (keys below the range count as before row 0, above it as after the last
@@ -234,6 +235,11 @@ def test_row_ptr_equals_searchsorted(ctx, case):
         keys = rng.integers(-800, n_rows + 800, 100_003)
     elif case == "tail":
         n_rows, keys = 7, rng.integers(0, 7, 1_026)
+    elif case == "leading":  # a million empty rows, then every key in the last rows
+        n_rows = 1_000_003
+        keys = rng.integers(n_rows - 3, n_rows, 40_000)
+    elif case == "none":
+        n_rows, keys = 300_000, np.zeros(0, np.int64)
     else:
         n_rows, keys = 1 << 23, rng.integers(0, 1 << 23, 1 << 24)
     to_id = np.sort(keys.astype(np.int64) + row_base).astype(np.uint32)
