@@ -380,6 +380,21 @@ int plx_radix_sort_u32(plx_ctx* ctx, uint64_t n, const uint32_t* keys_in,
                        uint32_t begin_bit, uint32_t end_bit, void* scratch,
                        size_t scratch_bytes);
 
+size_t plx_sort_tail_scratch_bytes(uint64_t n);
+
+/* plx_radix_sort_u32 for keys whose first *n_sorted entries are already in
+ * order (by bits [begin_bit, end_bit)) -- the connections a compaction kept,
+ * followed by regrown ones: the tail is radix-sorted and merged with the
+ * prefix (prefix first on equal keys). keys_out and perm_out equal
+ * plx_radix_sort_u32's bit for bit when the precondition holds. n_sorted is
+ * in DEVICE memory (plx_compact's count); this call waits for the stream to
+ * read it. keys_out and perm_out 16-byte aligned; n < 2^30. Replaces, for
+ * the re-sort after regrowth, the full sort of the reference's
+ * Gather-by-sorted-order (alloc.hpp:145-156). */
+int plx_sort_tail_u32(plx_ctx* ctx, uint64_t n, const uint64_t* n_sorted, const uint32_t* keys_in,
+                      uint32_t* keys_out, uint32_t* perm_out, uint32_t begin_bit,
+                      uint32_t end_bit, void* scratch, size_t scratch_bytes);
+
 size_t plx_sort_unique_u64_scratch_bytes(uint64_t n);
 
 /* Proposal commit of DoAddConnections (plastix.hpp:411-433): sorts n 64-bit

@@ -373,6 +373,19 @@ def radix_sort_u32(ctx: Context, keys: torch.Tensor, keys_out: torch.Tensor,
          begin_bit, end_bit, _ptr(s), s.numel())
 
 
+def sort_tail_u32(ctx: Context, keys: torch.Tensor, n_sorted: torch.Tensor,
+                  keys_out: torch.Tensor, perm_out: torch.Tensor, begin_bit: int = 0,
+                  end_bit: int = 32, *, scratch: Optional[Scratch] = None):
+    """``radix_sort_u32`` for keys whose first ``n_sorted`` (a one-element
+    int64 DEVICE tensor, e.g. a compaction's count) are already in order:
+    the tail is sorted and merged in; the same output bit for bit."""
+    n = int(keys.numel())
+    nbytes = _abi.lib().plx_sort_tail_scratch_bytes(n)
+    s = (scratch or Scratch(ctx.device)).get(nbytes)
+    call("plx_sort_tail_u32", ctx.handle, n, _ptr(n_sorted), _ptr(keys), _ptr(keys_out),
+         _ptr(perm_out), begin_bit, end_bit, _ptr(s), s.numel())
+
+
 def recompute_levels(ctx: Context, n_units: int, n_input: int, from_id: torch.Tensor,
                      to_id: torch.Tensor, level: torch.Tensor, *,
                      dead: Optional[torch.Tensor] = None, rounds: Optional[torch.Tensor] = None,
@@ -445,7 +458,8 @@ class StructuralLayer:
     """Sparse layer with structural plasticity, stepped entirely on the device:
     prune connections with |w| < threshold (order-preserving compaction, ages
     of survivors +1), regrow the same number with seeded random endpoints
-    (w = 0, age = 0), re-sort all connections by ToId (stable radix sort +
+    (w = 0, age = 0), re-sort all connections by ToId (the regrown tail
+    radix-sorted and merged with the still-sorted survivors: a stable sort +
     Gather), rebuild the row index and run the forward sweep. Sources are
     units [0, n_src), destinations [n_src, n_src + n_dst)."""
 
@@ -503,8 +517,10 @@ class StructuralLayer:
         regrow(ctx, self.count, self.f2, self.t2, self.w2, self.age2, src_base=0,
                n_src=self.n_src, dst_base=self.n_src, n_dst=self.n_dst, seed=self.seed,
                step_base=self.step_index * self.n)
-        radix_sort_u32(ctx, self.t2, self.keys_sorted, self.perm, 0, self.key_bits,
-                       scratch=self.scratch)
+        # survivors are still in destination order: sort the regrown tail
+        # and merge it in (the same permutation as a full stable sort)
+        sort_tail_u32(ctx, self.t2, self.count, self.keys_sorted, self.perm, 0, self.key_bits,
+                      scratch=self.scratch)
         gather(ctx, self.perm, [(self.f2, self.f), (self.t2, self.t), (self.w2, self.w),
                                 (self.age2, self.age)])
         self.csr = DstCsr.from_sorted_async(ctx, self.t, self.n_src, self.n_dst,

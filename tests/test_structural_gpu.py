@@ -7,7 +7,7 @@ import torch
 
 from plastix_b200 import _abi
 from plastix_b200.runtime import (StructuralLayer, compact, gather, radix_sort_u32,
-                                  regrow)
+                                  regrow, sort_tail_u32)
 
 pytestmark = pytest.mark.gpu
 
@@ -91,6 +91,41 @@ def test_radix_sort_ignores_bits_outside_range(ctx, orc):
     ctx.sync()
     want = orc.stable_sort_perm_u32((keys >> 4) & ((1 << 15) - 1))
     np.testing.assert_array_equal(host(perm).view(np.uint32), want.astype(np.uint32))
+
+
+@pytest.mark.parametrize("n,n_sorted,bits,lo,hi", [
+    (0, 0, 24, 0, 1), (1, 1, 24, 0, 1), (1, 0, 24, 0, 1), (5000, 5000, 24, 0, 1 << 24),
+    (5000, 0, 24, 0, 1 << 24), (100_003, 84_000, 24, 0, 1 << 24),   # 16 % regrown
+    (100_003, 99_999, 24, 0, 64),                                   # heavy key ties
+    (300_001, 1, 23, 0, 1 << 23), (1 << 21, 1_700_000, 32, 0, 2**32),
+    (77_777, 40_000, 0, 0, 1 << 20),                                # no key bits: identity
+    (4096 * 3 + 5, 2048 * 5 + 1, 12, 0, 4096)])                      # partition edges
+def test_sort_tail_equals_full_stable_sort(ctx, orc, n, n_sorted, bits, lo, hi):
+    """plx_sort_tail_u32 (a sorted prefix, the regrown tail radix-sorted and
+    merged in) gives the permutation and keys of the full stable sort, bit for
+    bit, for prefixes of every length, heavy ties and partial partitions."""
+    rng = np.random.default_rng(n + n_sorted + bits)
+    keys = rng.integers(lo, hi, n, dtype=np.uint64).astype(np.uint32)
+    mask = (1 << bits) - 1 if bits < 32 else 0xFFFFFFFF
+    pre = keys[:n_sorted]
+    keys[:n_sorted] = pre[np.argsort(pre & np.uint32(mask), kind="stable")]
+    count = torch.tensor([n_sorted], dtype=torch.int64, device="cuda")
+    keys_out = torch.zeros(max(n, 4), dtype=torch.int32, device="cuda")
+    perm = torch.zeros(max(n, 4), dtype=torch.int32, device="cuda")
+    k_in = dev(keys) if n else torch.zeros(4, dtype=torch.int32, device="cuda")[:0]
+    sort_tail_u32(ctx, k_in, count, keys_out, perm, 0, bits)
+    ctx.sync()
+    want = orc.stable_sort_perm_u32(keys & np.uint32(mask))
+    np.testing.assert_array_equal(host(perm)[:n].view(np.uint32), want.astype(np.uint32))
+    np.testing.assert_array_equal(host(keys_out)[:n].view(np.uint32), keys[want])
+
+
+def test_sort_tail_rejects_a_prefix_longer_than_the_keys(ctx):
+    keys = torch.zeros(10, dtype=torch.int32, device="cuda")
+    out = torch.zeros(12, dtype=torch.int32, device="cuda")
+    count = torch.tensor([11], dtype=torch.int64, device="cuda")
+    with pytest.raises(RuntimeError, match="exceeds"):
+        sort_tail_u32(ctx, keys, count, out, out.clone(), 0, 8)
 
 
 def test_gather_matches_reference_gather(ctx, orc):
