@@ -1109,6 +1109,7 @@ template <typename Traits> class Network {
   // ---- coherence of the host copies ---------------------------------------
   static void FetchUnitField(void *owner, size_t I) {
     auto *N = static_cast<Network *>(owner);
+    N->InputsToField();
     N->DownloadField(N->UA, N->d_uf, N->DevUnits, I);
   }
   static void FetchConnField(void *owner, size_t I) {
@@ -1165,7 +1166,10 @@ template <typename Traits> class Network {
   // Called before device work: host edits reach the device, and an edit of
   // the connection topology invalidates the connection index.
   void BeginDevice(bool fused_step = false) {
-    if (!fused_step) FieldsFromSlots();
+    if (!fused_step) {
+      FieldsFromSlots();
+      InputsToField();
+    }
     const uint64_t cdirty = CA.DirtyMask();
     if (cdirty) Fused.Ready = false;  // the slot copies no longer match
     const bool units_resized = UA.Size() != DevUnits;
@@ -1554,6 +1558,10 @@ template <typename Traits> class Network {
   // only once the transfers that read it have completed. Large transfers go
   // in 1 MiB pieces, each sent while the next is copied into the buffer.
   void StagedUpload(void *dst, const void *src_host, size_t bytes, StagingPair &pair) {
+    StagedUpload(dst, src_host, bytes, pair, Stream);
+  }
+  void StagedUpload(void *dst, const void *src_host, size_t bytes, StagingPair &pair,
+                    cudaStream_t on) {
     Staging &b = pair.B[pair.Next];
     pair.Next ^= 1;
     if (b.Bytes < bytes) {
@@ -1576,10 +1584,10 @@ template <typename Traits> class Network {
     for (size_t off = 0; off < bytes; off += piece) {
       const size_t len = std::min(piece, bytes - off);
       std::memcpy(host + off, src + off, len);
-      cuda_check(cudaMemcpyAsync(dev + off, host + off, len, cudaMemcpyHostToDevice, Stream),
+      cuda_check(cudaMemcpyAsync(dev + off, host + off, len, cudaMemcpyHostToDevice, on),
                  "upload");
     }
-    cuda_check(cudaEventRecord(b.Done, Stream), "upload");
+    cuda_check(cudaEventRecord(b.Done, on), "upload");
   }
   StagingPair InStage, TargetStage;
 
@@ -1674,6 +1682,11 @@ template <typename Traits> class Network {
   // fused step).
   struct FusedState {
     bool Eligible = false, Ready = false, SlotsNewer = false, AnyDead = true;
+    // double-buffered inputs of the fused step (UploadInputsAside)
+    float *In[2] = {nullptr, nullptr};
+    cudaEvent_t InReady[2] = {nullptr, nullptr}, Swept[2] = {nullptr, nullptr};
+    cudaStream_t Copy = nullptr;
+    int InNext = 0, InCur = -1;
     plx_sliced Sl{};
     // slot-order FromId, Dead, Weight, Trace; lane lengths, row offsets,
     // slice offsets, lane rows, slot -> connection permutation
@@ -1692,6 +1705,46 @@ template <typename Traits> class Network {
   }
   static constexpr size_t kW = ConnAllocator::template IndexOf<WeightTag>();
   static constexpr size_t kE = ConnAllocator::template IndexOf<TraceTag>();
+
+  // A full input vector of the fused step goes to one of two device buffers
+  // of its own, on a copy stream, so that its transfer overlaps the previous
+  // step's sweep; the sweep gathers from that buffer. A buffer is refilled
+  // only after the sweep that read it (event). The input units' Activation
+  // field is brought up to date from the buffer when anything else needs it
+  // (InputsToField).
+  int UploadInputsAside(std::span<const float> Inputs) {
+    const size_t bytes = NumInput * sizeof(float);
+    if (!Fused.Copy) {
+      cuda_check(cudaStreamCreateWithFlags(&Fused.Copy, cudaStreamNonBlocking), "inputs");
+      for (int b = 0; b < 2; ++b) {
+        cuda_check(cudaMalloc(&Fused.In[b], std::max<size_t>(bytes, 16)), "inputs");
+        cuda_check(cudaEventCreateWithFlags(&Fused.InReady[b], cudaEventDisableTiming), "inputs");
+        cuda_check(cudaEventCreateWithFlags(&Fused.Swept[b], cudaEventDisableTiming), "inputs");
+      }
+      // the copy stream starts behind everything already queued on Stream
+      cuda_check(cudaEventRecord(Fused.Swept[0], Stream), "inputs");
+      cuda_check(cudaEventRecord(Fused.Swept[1], Stream), "inputs");
+    }
+    const int b = Fused.InNext;
+    Fused.InNext ^= 1;
+    cuda_check(cudaStreamWaitEvent(Fused.Copy, Fused.Swept[b], 0), "inputs");
+    StagedUpload(Fused.In[b], Inputs.data(), bytes, InStage, Fused.Copy);
+    cuda_check(cudaEventRecord(Fused.InReady[b], Fused.Copy), "inputs");
+    cuda_check(cudaStreamWaitEvent(Stream, Fused.InReady[b], 0), "inputs");
+    return b;
+  }
+
+  // The last fused step's inputs into the Activation field of the input units.
+  void InputsToField() {
+    if constexpr (detail::fused_hebbian_traits<Traits>()) {
+      if (Fused.InCur < 0) return;
+      const int b = Fused.InCur;
+      Fused.InCur = -1;
+      cuda_check(cudaMemcpyAsync(d_uf[core::kActivation], Fused.In[b], NumInput * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, Stream),
+                 "inputs");
+    }
+  }
 
   void FieldsFromSlots() {
     if constexpr (detail::fused_hebbian_traits<Traits>()) {
@@ -1752,16 +1805,28 @@ template <typename Traits> class Network {
     if (IndexStale) RebuildIndex();
     if (!Fused.Eligible) return false;
     if (!Fused.Ready) BuildFused();
-    UploadInputs(Inputs);
     using U = typename Traits::UpdateConn;
     float *act = static_cast<float *>(d_uf[core::kActivation]);
+    const float *src = act;
+    int slot = -1;
+    if (Inputs.size() >= NumInput) {
+      slot = UploadInputsAside(Inputs);
+      src = Fused.In[slot];
+    } else {
+      InputsToField();
+      UploadInputs(Inputs);
+    }
     plx_check(plx_sweep_forward_hebbian_sliced(
                   PlxCtx(), &Fused.Sl, static_cast<uint32_t *>(Fused.Mem[0]),
-                  Fused.AnyDead ? static_cast<uint8_t *>(Fused.Mem[1]) : nullptr, act,
+                  Fused.AnyDead ? static_cast<uint8_t *>(Fused.Mem[1]) : nullptr, src,
                   (uint32_t)NumInput, static_cast<float *>(Fused.Mem[2]),
                   static_cast<float *>(Fused.Mem[3]), U::kDecay, U::kRate, act + NumInput,
                   nullptr, 0, 0, 0),
               "plx_sweep_forward_hebbian_sliced");
+    if (slot >= 0) {
+      cuda_check(cudaEventRecord(Fused.Swept[slot], Stream), "inputs");
+      Fused.InCur = slot;
+    }
     Fused.SlotsNewer = true;
     UA.MarkStale(UnitAllocator::AllFields());
     CA.MarkStale(ConnAllocator::AllFields());
@@ -1778,6 +1843,15 @@ template <typename Traits> class Network {
     OwnStream = nullptr;
     for (void *p : Fused.Mem)
       if (p) cudaFree(p);
+    if (Fused.Copy) {
+      cudaStreamSynchronize(Fused.Copy);
+      cudaStreamDestroy(Fused.Copy);
+      for (int b = 0; b < 2; ++b) {
+        cudaFree(Fused.In[b]);
+        cudaEventDestroy(Fused.InReady[b]);
+        cudaEventDestroy(Fused.Swept[b]);
+      }
+    }
     if (OutHost) cudaFreeHost(OutHost);
     OutHost = nullptr;
     for (StagingPair *pair : {&InStage, &TargetStage})

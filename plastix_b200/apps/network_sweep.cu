@@ -173,6 +173,11 @@ template <class Traits> int check(const std::string &dir, int steps, bool edit) 
     }
   }
   std::vector<float> o(out.begin(), out.end());
+  // the input units hold the last step's inputs (the fused route keeps them
+  // in a buffer of its own until the unit fields are read)
+  auto &U = Net.GetUnitAlloc();
+  for (uint64_t i = 0; i < n_src; ++i)
+    if (plastix::GetActivation(U, i) != act[i]) return 5;
   auto &C = Net.GetConnAlloc();
   std::vector<float> wo(n), eo(n);
   for (uint64_t i = 0; i < n; ++i) {
