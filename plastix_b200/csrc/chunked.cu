@@ -31,7 +31,7 @@ namespace {
 constexpr uint32_t kChunk = PLX_CHUNK_SOURCES;
 constexpr uint32_t kPad = 4;            // segment length granularity
 constexpr int kCThreads = 256;          // 8 warps
-constexpr int kCRowsPerWarp = 4;        // rows a warp works on together
+constexpr int kCRowsPerWarp = 8;        // rows a warp works on together
 
 __host__ __device__ inline uint32_t n_chunks_for(uint32_t n_src) {
   return (n_src + kChunk - 1) / kChunk;
