@@ -147,6 +147,18 @@ int plx_sweep_forward(plx_ctx* ctx, const plx_csr* csr, const uint32_t* from_id,
                       int apply_kind, float* act_dst, const float* value,
                       float* err_out);
 
+/* plx_sweep_forward over a CSR given by row_ptr alone (no plan), one thread
+ * per row folding its connections left to right -- the reference's order
+ * for every row length, so row values equal the reference's bit for bit.
+ * For layers of a few connections per row (the structural workload: two
+ * per destination), where it is the faster sweep and spares the plan.
+ * act_src_len bounds the gathered ids (an id past it reads 0 and sets the
+ * status word). */
+int plx_sweep_forward_rows(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                           const uint32_t* from_id, const float* weight, const uint8_t* dead,
+                           const float* act_src, uint32_t act_src_len, int apply_kind,
+                           float* act_dst, const float* value, float* err_out);
+
 /* Forward sweep fused with the per-connection Hebbian trace rule
  *   acc = sum w*act[src];  post = acc (identity Apply);
  *   trace' = decay*trace + act[src]*post;  w' = w + rate*trace'

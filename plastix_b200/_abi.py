@@ -99,6 +99,9 @@ _SIGNATURES = {
     "plx_radix_sort_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_radix_sort_u32": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p,
                                    c_uint32, c_uint32, c_void_p, ctypes.c_size_t]),
+    "plx_sweep_forward_rows": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p,
+                                       c_void_p, c_void_p, c_uint32, c_int, c_void_p, c_void_p,
+                                       c_void_p]),
     "plx_sort_tail_scratch_bytes": (ctypes.c_size_t, [c_uint64]),
     "plx_sort_tail_u32": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_uint32, c_uint32, c_void_p, ctypes.c_size_t]),

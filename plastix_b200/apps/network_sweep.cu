@@ -16,8 +16,9 @@
 //     destination activations), w.bin and e.bin (weights and traces in the
 //     given connection order).
 //   network_sweep check-edit <dir> <steps> [generic|fused]
-//     as check, and after the first step reads trace n/3 on the host and
-//     adds 0.25 to weight 0 and -0.5 to weight n/2 through GetConnAlloc().
+//     as check, and after the first step reads trace n/3 on the host, adds
+//     0.25 to weight 0 and -0.5 to weight n/2 and marks connections n/5 and
+//     n/7 dead, through GetConnAlloc().
 // The last argument picks the traits: "generic" (default) spells the rule
 // out as a user hook; "fused" uses plastix::HebbianTraceUpdate, which DoStep
 // runs as one fused sliced sweep.
@@ -170,6 +171,9 @@ template <class Traits> int check(const std::string &dir, int steps, bool edit) 
       (void)probe;
       plastix::GetWeight(C, 0) += 0.25f;
       plastix::GetWeight(C, n / 2) -= 0.5f;
+      // and two connections die (skipped by both passes from now on)
+      plastix::GetField<plastix::DeadTag>(C, n / 5) = true;
+      plastix::GetField<plastix::DeadTag>(C, n / 7) = true;
     }
   }
   std::vector<float> o(out.begin(), out.end());

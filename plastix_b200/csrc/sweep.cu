@@ -1285,6 +1285,38 @@ int launch_sweep(plx_ctx* ctx, const SweepArgs& args, const plx_csr* csr) {
                       DEAD>(ctx, targs);
 }
 
+// One thread per row, connections folded left to right (the reference's
+// order for every row length): for layers of a few connections per row,
+// where a warp per row or a tile plan costs more than it saves.
+template <int APPLY, bool DEAD>
+__global__ void k_rows_fold(const uint32_t* __restrict__ row_ptr, uint32_t n_rows,
+                            const uint32_t* __restrict__ src, const float* __restrict__ w,
+                            const uint8_t* __restrict__ dead, const float* __restrict__ act,
+                            uint32_t act_len, const float* __restrict__ value,
+                            float* __restrict__ act_dst, float* __restrict__ err_out,
+                            int32_t* status) {
+  bool bad = false;
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
+       r += gridDim.x * blockDim.x) {
+    const uint32_t b = __ldg(row_ptr + r), e = __ldg(row_ptr + r + 1);
+    float acc = 0.0f;
+    for (uint32_t k = b; k < e; ++k) {
+      if constexpr (DEAD)
+        if (__ldg(dead + k)) continue;
+      const uint32_t s = __ldg(src + k);
+      const bool ok = s < act_len;
+      bad |= !ok;
+      acc = __fadd_rn(acc, __fmul_rn(__ldg(w + k), ok ? __ldg(act + s) : 0.0f));
+    }
+    float v = 0.0f;
+    if constexpr (apply_reads_value(APPLY)) v = __ldg(value + r);
+    const float post = apply_value<APPLY>(acc, v);
+    if constexpr (APPLY == PLX_APPLY_IPC_ERROR) err_out[r] = post;
+    else act_dst[r] = post;
+  }
+  if (bad) record_status(status, kStatusBadIndex);
+}
+
 static int validate_csr(const plx_csr* csr) {
   PLX_CHECK_ARG(csr && csr->row_ptr && csr->plan, "csr, row_ptr and plan are required");
   PLX_CHECK_ARG(aligned16(csr->row_ptr), "row_ptr must be 16-byte aligned");
@@ -1430,6 +1462,48 @@ static int csr_plan(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
     out->row_base = 0;
     out->max_row = hdr[7];
   }
+  return PLX_OK;
+}
+
+extern "C" int plx_sweep_forward_rows(plx_ctx* ctx, const uint32_t* row_ptr, uint32_t n_rows,
+                                      const uint32_t* from_id, const float* weight,
+                                      const uint8_t* dead, const float* act_src,
+                                      uint32_t act_src_len, int apply_kind, float* act_dst,
+                                      const float* value, float* err_out) {
+  PLX_CHECK_ARG(ctx && row_ptr, "ctx and row_ptr are required");
+  if (apply_kind == PLX_APPLY_IPC_ERROR)
+    PLX_CHECK_ARG(value && err_out, "IPC_ERROR needs value and err_out");
+  else
+    PLX_CHECK_ARG(act_dst, "act_dst is required");
+  if (apply_kind == PLX_APPLY_SIGMOID_GRAD || apply_kind == PLX_APPLY_TANH_GRAD)
+    PLX_CHECK_ARG(value, "the gradient applies need value");
+  PLX_CHECK_ARG(apply_kind >= PLX_APPLY_IDENTITY && apply_kind <= PLX_APPLY_TANH_GRAD,
+                "unknown apply_kind %d", apply_kind);
+  PLX_TRY_CUDA(cudaSetDevice(ctx->device));
+  if (n_rows == 0) return PLX_OK;
+  const unsigned g = (unsigned)std::min<uint64_t>((n_rows + 255) / 256, 32ull * ctx->num_sms);
+  const uint32_t len = act_src ? act_src_len : 0;
+  switch (apply_kind) {
+#define PLX_ROWS_CASE(K)                                                                   \
+  case K:                                                                                  \
+    if (dead)                                                                              \
+      k_rows_fold<K, true><<<g, 256, 0, ctx->stream>>>(row_ptr, n_rows, from_id, weight,  \
+                                                       dead, act_src, len, value, act_dst, \
+                                                       err_out, ctx->d_status);            \
+    else                                                                                   \
+      k_rows_fold<K, false><<<g, 256, 0, ctx->stream>>>(row_ptr, n_rows, from_id, weight, \
+                                                        dead, act_src, len, value,         \
+                                                        act_dst, err_out, ctx->d_status);  \
+    break;
+    PLX_ROWS_CASE(PLX_APPLY_IDENTITY)
+    PLX_ROWS_CASE(PLX_APPLY_SIGMOID)
+    PLX_ROWS_CASE(PLX_APPLY_TANH)
+    PLX_ROWS_CASE(PLX_APPLY_IPC_ERROR)
+    PLX_ROWS_CASE(PLX_APPLY_SIGMOID_GRAD)
+    PLX_ROWS_CASE(PLX_APPLY_TANH_GRAD)
+#undef PLX_ROWS_CASE
+  }
+  PLX_LAUNCH_CHECK("k_rows_fold");
   return PLX_OK;
 }
 

@@ -144,6 +144,19 @@ def sweep_forward(ctx: Context, csr: DstCsr, from_id: torch.Tensor, weight: torc
          _ptr(value), _ptr(err_out))
 
 
+def sweep_forward_rows(ctx: Context, row_ptr: torch.Tensor, from_id: torch.Tensor,
+                       weight: torch.Tensor, act_src: torch.Tensor,
+                       act_dst: Optional[torch.Tensor] = None, *,
+                       apply: int = _abi.APPLY_IDENTITY, dead: Optional[torch.Tensor] = None,
+                       value: Optional[torch.Tensor] = None,
+                       err_out: Optional[torch.Tensor] = None) -> None:
+    """``sweep_forward`` over row offsets alone: one thread per row, a left
+    fold in connection order (for layers of a few connections per row)."""
+    call("plx_sweep_forward_rows", ctx.handle, _ptr(row_ptr), int(row_ptr.numel()) - 1,
+         _ptr(from_id), _ptr(weight), _ptr(dead), _ptr(act_src), int(act_src.numel()), apply,
+         _ptr(act_dst), _ptr(value), _ptr(err_out))
+
+
 def sweep_forward_hebbian(ctx: Context, csr: DstCsr, from_id: torch.Tensor,
                           act_src: torch.Tensor, w_in: torch.Tensor, w_out: torch.Tensor,
                           trace_in: torch.Tensor, trace_out: torch.Tensor,
@@ -460,8 +473,9 @@ class StructuralLayer:
     of survivors +1), regrow the same number with seeded random endpoints
     (w = 0, age = 0), re-sort all connections by ToId (the regrown tail
     radix-sorted and merged with the still-sorted survivors: a stable sort +
-    Gather), rebuild the row index and run the forward sweep. Sources are
-    units [0, n_src), destinations [n_src, n_src + n_dst)."""
+    Gather), rebuild the row offsets and run the forward sweep (one thread per
+    row: two connections per destination at the benchmark's shape). Sources
+    are units [0, n_src), destinations [n_src, n_src + n_dst)."""
 
     def __init__(self, ctx: Context, n_src: int, n_dst: int, from_id, to_id, weight, age,
                  *, threshold: float = 0.02, seed: int = 1):
@@ -484,7 +498,14 @@ class StructuralLayer:
         # on the bits its largest value needs
         self.key_bits = max(1, (n_src + n_dst - 1).bit_length())
         self.step_index = 0
-        self.csr = DstCsr.from_sorted_async(ctx, self.t, n_src, n_dst)
+        # a structural layer has a few connections per destination: its
+        # forward sweep is the row-per-thread fold over row offsets alone
+        self.row_ptr = torch.empty(n_dst + 1, dtype=torch.int32, device=dev)
+        self._index()
+
+    def _index(self):
+        call("plx_csr_row_ptr", self.ctx.handle, _ptr(self.t), self.n, self.n_src, self.n_dst,
+             _ptr(self.row_ptr))
 
     def _state_tensors(self):
         return {"from_id": self.f, "to_id": self.t, "weight": self.w, "age": self.age,
@@ -495,8 +516,7 @@ class StructuralLayer:
 
     def _load_meta(self, meta):
         self.step_index = int(meta["step_index"])
-        self.csr = DstCsr.from_sorted_async(self.ctx, self.t, self.n_src, self.n_dst,
-                                            self.csr.row_ptr, self.csr.plan)
+        self._index()
 
     def save(self, path) -> None:
         """Checkpoint: the connection fields, destination activations and the
@@ -523,9 +543,8 @@ class StructuralLayer:
                       scratch=self.scratch)
         gather(ctx, self.perm, [(self.f2, self.f), (self.t2, self.t), (self.w2, self.w),
                                 (self.age2, self.age)])
-        self.csr = DstCsr.from_sorted_async(ctx, self.t, self.n_src, self.n_dst,
-                                            self.csr.row_ptr, self.csr.plan)
-        sweep_forward(ctx, self.csr, self.f, self.w, act_src, self.act_dst)
+        self._index()
+        sweep_forward_rows(ctx, self.row_ptr, self.f, self.w, act_src, self.act_dst)
         self.step_index += 1
         return self.act_dst
 

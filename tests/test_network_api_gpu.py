@@ -52,9 +52,10 @@ def test_api_sweep_matches_oracle(tmp_path, orc, case, traits):
 @pytest.mark.gpu
 @pytest.mark.parametrize("traits", ["generic", "fused"])
 def test_api_host_edits_between_steps(tmp_path, orc, traits):
-    """Weights written and traces read on the host between DoSteps: the
-    fused route's slot-order copies are unpacked for the read and re-packed
-    after the write, so every step still matches the oracle bit for bit."""
+    """Weights written, connections killed and traces read on the host
+    between DoSteps: the fused route's slot-order copies are unpacked for the
+    read and re-packed (with the dead-aware kernel) after the writes, so every
+    step still matches the oracle bit for bit."""
     L = workloads.sparse_layer_rows(700, [0, 3, 150, 1, 900, 33] * 50, seed=11)
     _write_layer(tmp_path / "layer.bin", L)
     exe = build.build_app("network_sweep")
@@ -68,7 +69,10 @@ def test_api_host_edits_between_steps(tmp_path, orc, traits):
     w = w.copy()
     w[0] = np.float32(w[0] + np.float32(0.25))
     w[n // 2] = np.float32(w[n // 2] - np.float32(0.5))
-    w, e, a = orc.step_hebbian(L.from_id, L.to_id, w, e, a, L.n_src, 0.9, 1e-3, sweeps=2)
+    dead = np.zeros(n, np.uint8)
+    dead[[n // 5, n // 7]] = 1
+    w, e, a = orc.step_hebbian(L.from_id, L.to_id, w, e, a, L.n_src, 0.9, 1e-3, sweeps=2,
+                               dead=dead)
     np.testing.assert_array_equal(np.fromfile(tmp_path / "out.bin", np.float32), a[L.n_src:])
     np.testing.assert_array_equal(np.fromfile(tmp_path / "w.bin", np.float32), w)
     np.testing.assert_array_equal(np.fromfile(tmp_path / "e.bin", np.float32), e)

@@ -148,6 +148,51 @@ def test_forward_apply_kinds(ctx, orc, apply, with_dead, max_len):
                 exact_ok=apply in (_abi.APPLY_IDENTITY, _abi.APPLY_IPC_ERROR))
 
 
+@pytest.mark.parametrize("apply", [_abi.APPLY_IDENTITY, _abi.APPLY_IPC_ERROR,
+                                   _abi.APPLY_SIGMOID, _abi.APPLY_TANH])
+@pytest.mark.parametrize("with_dead", [False, True])
+def test_row_per_thread_forward(ctx, orc, apply, with_dead):
+    """plx_sweep_forward_rows (one thread per row, row offsets only): a left
+    fold in connection order, so identity and iPC-error rows equal the
+    oracle bit for bit at every row length (empty, 1, 2, 1000+), the other
+    applies within the device transcendental's tolerance."""
+    from plastix_b200.runtime import sweep_forward_rows
+    lens = [0, 1, 2, 2, 3, 1, 0, 2] * 300 + [1000, 257, 5000]
+    L = workloads.sparse_layer_rows(4000, lens, seed=31)
+    dead = (np.random.default_rng(8).random(L.from_id.size) < 0.1).astype(np.uint8) \
+        if with_dead else None
+    value = np.random.default_rng(5).random(L.n_dst, dtype=np.float32)
+    row_ptr = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    act_dst = torch.zeros(L.n_dst, device="cuda")
+    err = torch.zeros(L.n_dst, device="cuda")
+    sweep_forward_rows(ctx, dev(row_ptr), ids(L.from_id), dev(L.weight), dev(L.act_in), act_dst,
+                       apply=apply, dead=None if dead is None else dev(dead), value=dev(value),
+                       err_out=err)
+    ctx.sync()
+    act = np.concatenate([L.act_in, np.zeros(L.n_dst, np.float32)])
+    full_value = np.concatenate([np.zeros(L.n_src, np.float32), value])
+    want_act, want_err = orc.forward_pipeline(L.from_id, L.to_id, L.weight, act, L.n_src,
+                                              apply=apply, dead=dead, value=full_value)
+    got = host(err) if apply == _abi.APPLY_IPC_ERROR else host(act_dst)
+    want = want_err[L.n_src:] if apply == _abi.APPLY_IPC_ERROR else want_act[L.n_src:]
+    if apply in (_abi.APPLY_IDENTITY, _abi.APPLY_IPC_ERROR):
+        np.testing.assert_array_equal(got, want)
+    else:
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+def test_row_per_thread_forward_flags_bad_ids(ctx):
+    from plastix_b200.runtime import sweep_forward_rows
+    row_ptr = dev(np.array([0, 2, 3], np.int32))
+    from_id = ids(np.array([0, 7, 1], np.uint32))  # 7 is past the 4 sources
+    out = torch.zeros(2, device="cuda")
+    sweep_forward_rows(ctx, row_ptr, from_id, dev(np.ones(3, np.float32)),
+                       dev(np.arange(4, dtype=np.float32)), out)
+    with pytest.raises(RuntimeError):
+        ctx.sync()
+    np.testing.assert_array_equal(host(out), [0.0, 1.0])  # the bad id read 0
+
+
 @pytest.mark.parametrize("kind", [_abi.UPDATE_GRADIENT, _abi.UPDATE_HEBBIAN])
 def test_update_kinds(ctx, orc, kind):
     L = workloads.sparse_layer_rows(3000, list(np.random.default_rng(2).integers(0, 600, 700)),
