@@ -816,7 +816,9 @@ def bench_ipc(args):
 def bench_structural(args):
     """C3: 2^23 sources, 2^23 destinations, 2^24 connections dst-sorted,
     w N(0, 0.1^2), u8 age; prune |w| < 0.02 by compaction, regrow the same
-    number, radix-sort by destination, forward sweep. Under torchrun each rank
+    number, re-sort by destination (the regrown tail radix-sorted and merged
+    with the survivors), row offsets, forward sweep (one thread per row).
+    Under torchrun each rank
     holds its own destination shard of that size (weak scaling): compaction,
     regrowth (rank-keyed seed) and the re-sort are shard-local, so no
     collective touches the step; the barrier and the max over ranks only
