@@ -541,8 +541,10 @@ class StructuralLayer:
         # and merge it in (the same permutation as a full stable sort)
         sort_tail_u32(ctx, self.t2, self.count, self.keys_sorted, self.perm, 0, self.key_bits,
                       scratch=self.scratch)
-        gather(ctx, self.perm, [(self.f2, self.f), (self.t2, self.t), (self.w2, self.w),
-                                (self.age2, self.age)])
+        # the sorted keys are the re-sorted ToId field itself: only the other
+        # fields are gathered
+        self.t, self.keys_sorted = self.keys_sorted, self.t
+        gather(ctx, self.perm, [(self.f2, self.f), (self.w2, self.w), (self.age2, self.age)])
         self._index()
         sweep_forward_rows(ctx, self.row_ptr, self.f, self.w, act_src, self.act_dst)
         self.step_index += 1
