@@ -111,16 +111,22 @@ enum UpdKind : int { kUpdNone = 0, kUpdHebbTrace = 1, kUpdGrad = 2, kUpdHebb = 3
 // rows r with key(i-1) < r <= key(i), keys clamped to [-1, n_rows] (index
 // n_edges acts as key n_rows). Each thread takes four consecutive indices
 // with one 16-byte load (to_id is 16-byte aligned) plus the key before them.
-constexpr int64_t kRowGapMax = 64;  // empty rows one thread of k_row_ptr fills
+constexpr int64_t kRowGapMax = 64;  // empty rows one thread of k_row_ptr stores
 
 __device__ __forceinline__ int64_t row_key(uint32_t to, uint32_t row_base, uint32_t n_rows) {
   const int64_t k = (int64_t)to - (int64_t)row_base;
   return k < -1 ? -1 : (k > (int64_t)n_rows ? (int64_t)n_rows : k);
 }
 
+// A run of more empty rows than kRowGapMax is not stored by the thread that
+// finds it (it would store the run serially); it is appended to a list of
+// (first row, last row, value) runs that k_row_ptr_runs fills in parallel.
+// Runs that do not fit the list are stored serially after all.
+constexpr uint32_t kRowRunsCap = 4096;
+
 __global__ void k_row_ptr(const uint32_t* __restrict__ to_id, uint64_t n_edges,
                           uint32_t row_base, uint32_t n_rows,
-                          uint32_t* __restrict__ row_ptr) {
+                          uint32_t* __restrict__ row_ptr, uint32_t* __restrict__ runs) {
   const uint64_t i0 = 4 * (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x);
   if (i0 > n_edges) return;
   int64_t k[5];  // keys of i0 - 1 .. i0 + 3
@@ -142,31 +148,33 @@ __global__ void k_row_ptr(const uint32_t* __restrict__ to_id, uint64_t n_edges,
     const uint64_t i = i0 + j;
     if (i > n_edges) break;
     const int64_t hi = min(k[j + 1], (int64_t)n_rows - 1);
-    // a long run of empty rows is left to k_row_ptr_gaps (one thread would
-    // otherwise store it serially)
-    if (hi - k[j] <= kRowGapMax)
+    bool inline_store = hi - k[j] <= kRowGapMax;
+    if (!inline_store) {
+      const uint32_t slot = atomicAdd(runs, 1u);
+      if (slot < kRowRunsCap) {
+        uint32_t* run = runs + 1 + 3 * slot;
+        run[0] = (uint32_t)(k[j] + 1);
+        run[1] = (uint32_t)hi;
+        run[2] = (uint32_t)i;
+      } else {
+        inline_store = true;
+      }
+    }
+    if (inline_store)
       for (int64_t r = k[j] + 1; r <= hi; ++r) row_ptr[r] = (uint32_t)i;
     if (i == n_edges) row_ptr[n_rows] = (uint32_t)n_edges;
   }
 }
 
-// Rows inside long runs of empty rows (still holding the 0xFFFFFFFF fill):
-// row_ptr[r] = first connection whose ToId >= row_base + r, by binary search
-// over the sorted ToId.
-__global__ void k_row_ptr_gaps(const uint32_t* __restrict__ to_id, uint64_t n_edges,
-                               uint32_t row_base, uint32_t n_rows,
-                               uint32_t* __restrict__ row_ptr) {
-  for (uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; r < n_rows;
-       r += (uint64_t)gridDim.x * blockDim.x) {
-    if (row_ptr[r] != 0xFFFFFFFFu) continue;
-    const uint64_t want = (uint64_t)row_base + r;
-    uint64_t lo = 0, hi = n_edges;
-    while (lo < hi) {
-      const uint64_t mid = (lo + hi) / 2;
-      if ((uint64_t)__ldg(to_id + mid) < want) lo = mid + 1;
-      else hi = mid;
-    }
-    row_ptr[r] = (uint32_t)lo;
+// The listed runs of empty rows: rows [first, last] all start at `value`.
+// Every run is spread over the whole grid (one run can be millions of rows).
+__global__ void k_row_ptr_runs(const uint32_t* __restrict__ runs, uint32_t* __restrict__ row_ptr) {
+  const uint32_t n = min(runs[0], kRowRunsCap);
+  const uint64_t t0 = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint32_t q = 0; q < n; ++q) {
+    const uint32_t first = runs[1 + 3 * q], last = runs[2 + 3 * q], v = runs[3 + 3 * q];
+    for (uint64_t r = (uint64_t)first + t0; r <= last; r += stride) row_ptr[r] = v;
   }
 }
 
@@ -1354,16 +1362,15 @@ extern "C" int plx_csr_row_ptr(plx_ctx* ctx, const uint32_t* to_id,
   (void)n;
   PLX_CHECK_ARG(aligned16(to_id), "to_id must be 16-byte aligned");
   const uint64_t threads = n_edges / 4 + 1;  // indices 0 .. n_edges, four per thread
-  PLX_TRY_CUDA(cudaMemsetAsync(row_ptr, 0xFF, ((size_t)n_rows + 1) * sizeof(uint32_t),
-                               ctx->stream));
+  uint32_t* runs = nullptr;  // run count + kRowRunsCap (first, last, value) runs
+  if (int rc = ctx_counters(ctx, 1 + 3 * (size_t)kRowRunsCap, &runs)) return rc;
+  PLX_TRY_CUDA(cudaMemsetAsync(runs, 0, sizeof(uint32_t), ctx->stream));
   k_row_ptr<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(to_id, n_edges,
                                                                         row_base, n_rows,
-                                                                        row_ptr);
+                                                                        row_ptr, runs);
   PLX_LAUNCH_CHECK("k_row_ptr");
-  const unsigned g = (unsigned)std::min<uint64_t>(std::max<uint64_t>((n_rows + 255) / 256, 1),
-                                                  8ull * (uint64_t)ctx->num_sms);
-  k_row_ptr_gaps<<<g, 256, 0, ctx->stream>>>(to_id, n_edges, row_base, n_rows, row_ptr);
-  PLX_LAUNCH_CHECK("k_row_ptr_gaps");
+  k_row_ptr_runs<<<(unsigned)ctx->num_sms, 256, 0, ctx->stream>>>(runs, row_ptr);
+  PLX_LAUNCH_CHECK("k_row_ptr_runs");
   return PLX_OK;
 }
 
