@@ -790,6 +790,7 @@ def bench_ipc(args):
         return 0
     visits = iters * (E + Eb) + (E + Eb)
     per_sample = ms / steps
+    cpu = None if (world > 1 or args.no_cpu_baseline) else ipc_cpu_sample(F, iters, args.seed)
     line = {"metric": "connection-visits/s (ipc)", "value": visits / (per_sample / 1e3),
             "unit": "connection-visits/s", "n_gpus": world, "steps": steps,
             "warmup": min(args.warmup, 3), "ms_per_step": per_sample, "higher_is_better": True,
@@ -807,10 +808,51 @@ def bench_ipc(args):
                        "roofline_bytes": "forward: 6 B per connection (16-bit offset + weight)",
                        "l2": "inputs larger than L2"},
             "roofline": _roof(6 * E / world, fwd_ms, "ipc_forward_2G"),
-            "cpu_baseline": None, "e2e": None, "clocks": clocks, "gpu_launches": None,
+            "cpu_baseline": cpu, "e2e": None, "clocks": clocks, "gpu_launches": None,
             "forward_ms": fwd_ms}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def ipc_cpu_sample(fan_in, iters, seed, units=4096, layers=5):
+    """One iPC sample (clamp + pre-step, `iters` x (forward, backward, value
+    update), one weight update) of the same network scaled to `units` per
+    layer, through the oracle's C restatement on one host thread: the CPU
+    baseline of the iPC workload (the full network does not fit a bounded
+    CPU sample)."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(seed)
+    begin = [l * units for l in range(layers + 1)]
+    frm, to, w = [], [], []
+    for l in range(layers - 1):
+        to.append(np.repeat(np.arange(units, dtype=np.uint32) + np.uint32(begin[l + 1]), fan_in))
+        frm.append((rng.integers(0, units, units * fan_in) + begin[l]).astype(np.uint32))
+        w.append(rng.normal(0, 1 / np.sqrt(fan_in), units * fan_in).astype(np.float32))
+    frm, to, w = np.concatenate(frm), np.concatenate(to), np.concatenate(w)
+    n = begin[-1]
+    hidden = (begin[1], begin[-2])
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    inputs = rng.uniform(0, 1, units).astype(np.float32)
+    x[begin[-2]:] = rng.uniform(-1, 1, units).astype(np.float32)
+    t0 = time.perf_counter()
+    x[:units] = inputs
+    act = orc.ipc_prestep(x, inputs, hidden)
+    err = None
+    for _ in range(iters):
+        err = orc.ipc_forward(frm, to, w, act, x, units)
+        bu = orc.ipc_backward(frm, to, w, err, x, hidden)
+        orc.ipc_hidden_update(x, err, bu, act, 0.1, hidden)
+    w = orc.update_post(frm, to, act, err, w, 2, 0.005)
+    secs = time.perf_counter() - t0
+    e, eb = frm.size, (layers - 2) * units * fan_in
+    visits = iters * (e + eb) + e
+    return {"value": visits / secs, "unit": "connection-visits/s", "cores": 1, "kind": "port",
+            "sample": f"one sample of the network scaled to {units} units per layer "
+                      f"({e} connections, fan-in {fan_in}): {secs:.2f} s, oracle C "
+                      "restatement, one thread"}
 
 
 def bench_structural(args):
