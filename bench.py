@@ -919,12 +919,39 @@ def bench_structural(args):
     ctx.sync()
     if rank != 0:
         return 0
+    cpu = None if (world > 1 or args.no_cpu_baseline) else structural_cpu_sample(
+        n_src // 8, n_dst // 8, n // 8, args.seed)
     _line(args, "structural", world * n * steps / (ms / 1e3), "connections/s", ms / steps,
           {"workload": "structural plasticity step", "n_src": n_src, "n_dst_per_gpu": n_dst,
            "connections_per_gpu": n, "prune": "|w| < 0.02", "steps": steps,
            "parallelism": f"destination shards x{world}, shard-local (no collective)"},
-          None, None, None, clocks, None, extra={"n_gpus": world})
+          None, cpu, None, clocks, None, extra={"n_gpus": world})
     return 0
+
+
+def structural_cpu_sample(n_src, n_dst, n, seed, steps=3):
+    """The structural step (prune by compaction, regrowth, stable re-sort by
+    destination, forward) through the oracle's C restatement on one host
+    thread, on the workload scaled by 1/8: the CPU baseline."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(seed)
+    t = np.sort(rng.integers(0, n_dst, n)).astype(np.uint32) + np.uint32(n_src)
+    f = rng.integers(0, n_src, n).astype(np.uint32)
+    w = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    age = rng.integers(0, 256, n).astype(np.uint8)
+    act = np.concatenate([rng.random(n_src, dtype=np.float32), np.zeros(n_dst, np.float32)])
+    t0 = time.perf_counter()
+    for s in range(steps):
+        f, t, w, age, _ = orc.structural_step(f, t, w, age, n_src, n_dst, 0.02, 11, s * n)
+        orc.forward_pipeline(f, t, w, act, n_src)
+    secs = time.perf_counter() - t0
+    return {"value": n * steps / secs, "unit": "connections/s", "cores": 1, "kind": "port",
+            "sample": f"{steps} steps on the workload scaled by 1/8 ({n} connections, "
+                      f"{n_src} + {n_dst} units): {secs:.2f} s, oracle C restatement, "
+                      "one thread"}
 
 
 def _probe_lib():
