@@ -1161,8 +1161,9 @@ def bench_api(args):
 def bench_xor(args):
     """The XOR MLP (2 -> 8 -> 1 sigmoid, MSE, backward, gradient step at 0.5;
     5,000 epochs of four DoSteps, each followed by GetOutput) through the
-    device Network: plastix_b200/apps/xor_train.cu, with DoStep replayed as a
-    CUDA graph (the value) and with every kernel launched (in the config).
+    device Network: plastix_b200/apps/xor_train.cu, with DoStep as one kernel
+    of one CTA (the value), replayed as a CUDA graph and with every pass
+    launched (both in the config).
     A 24-connection network is launch- and latency-bound: the number is
     DoSteps per second of wall time around the epoch loop, host inputs in and
     the output read back every step. The baseline is the same program built
@@ -1195,16 +1196,19 @@ def bench_xor(args):
               None, cpu, None, None, None)
         return 0
     sampler = ClockSampler(0)
-    g = run([str(exe), str(epochs), "graph"])
+    g = run([str(exe), str(epochs), "single"])
     clocks = sampler.stop()
+    r = run([str(exe), str(epochs), "graph"])
     e = run([str(exe), str(epochs), "eager"])
     steps = g["steps"]
     value = steps / g["train_s"]
     config = {"workload": "XOR MLP training through Network<Traits>::DoStep (2 -> 8 -> 1 "
                           "sigmoid, MSE, backward, gradient descent, Topological)",
-              "epochs": epochs, "do_steps": steps, "graph_replay": True,
+              "epochs": epochs, "do_steps": steps, "step": "one kernel of one CTA per DoStep",
+              "graph_replay_steps_per_s": r["steps"] / r["train_s"],
               "eager_steps_per_s": e["steps"] / e["train_s"], "final_loss": g["final_loss"],
-              "xor_solved": g["pass"] and e["pass"]}
+              "final_losses_equal": g["final_loss"] == r["final_loss"] == e["final_loss"],
+              "xor_solved": g["pass"] and r["pass"] and e["pass"]}
     e2e = {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4}
     _line(args, "xor", value, "steps/s", 1e3 * g["train_s"] / steps, config, None, cpu, e2e,
           clocks, None)

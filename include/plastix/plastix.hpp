@@ -123,11 +123,9 @@ inline unsigned blocks(size_t n) { return (unsigned)std::max<size_t>(1, (n + 255
 // Pipeline forward accumulation: unit I folds its incoming connections in
 // index order (in_conn lists them per destination, ascending).
 template <class Tr, class UV, class CV, class G>
-__global__ void k_fwd_acc(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
-                          size_t n) {
+__device__ __forceinline__ void fwd_acc_unit(UV &U, CV &C, G *g, const uint32_t *in_ptr,
+                                             const uint32_t *in_conn, size_t I) {
   using FP = typename Tr::ForwardPass;
-  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= n) return;
   auto acc = GetForwardAcc(U, I);
   for (uint32_t k = in_ptr[I]; k < in_ptr[I + 1]; ++k) {
     const uint32_t c = in_conn[k];
@@ -135,6 +133,12 @@ __global__ void k_fwd_acc(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32
     acc = FP::Combine(acc, FP::Map(U, I, GetField<FromIdTag>(C, c), C, c, *g));
   }
   GetForwardAcc(U, I) = acc;
+}
+template <class Tr, class UV, class CV, class G>
+__global__ void k_fwd_acc(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
+                          size_t n) {
+  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I < n) fwd_acc_unit<Tr>(U, C, g, in_ptr, in_conn, I);
 }
 
 // Pipeline forward accumulation for connections stored destination-major
@@ -185,11 +189,10 @@ __global__ void __launch_bounds__(kTileWarps * 32)
 // SrcLevel is L - 1. Connections are sorted by SrcLevel, so each unit's
 // incoming list is too; `cur` is the unit's position in it.
 template <class Tr, class UV, class CV, class G>
-__global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
-                                uint32_t *cur, size_t n, int L) {
+__device__ __forceinline__ void fwd_acc_level_unit(UV &U, CV &C, G *g, const uint32_t *in_ptr,
+                                                   const uint32_t *in_conn, uint32_t *cur,
+                                                   size_t I, int L) {
   using FP = typename Tr::ForwardPass;
-  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= n) return;
   uint32_t k = cur[I];
   const uint32_t e = in_ptr[I + 1];
   if (k >= e) return;
@@ -207,6 +210,12 @@ __global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const 
   cur[I] = k;
   if (any) GetForwardAcc(U, I) = acc;
 }
+template <class Tr, class UV, class CV, class G>
+__global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const uint32_t *in_conn,
+                                uint32_t *cur, size_t n, int L) {
+  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I < n) fwd_acc_level_unit<Tr>(U, C, g, in_ptr, in_conn, cur, I, L);
+}
 
 // Apply of the units in [lo, hi) (only those at level `lvl` when lvl >= 0),
 // then the accumulator is reset. With `mse` (the targets of the output units
@@ -215,16 +224,20 @@ __global__ void k_fwd_acc_level(UV U, CV C, G *g, const uint32_t *in_ptr, const 
 // reference's DoCalculateLoss after DoForwardPass -- an output unit's
 // activation is final once its Apply has run).
 template <class Tr, class UV, class G>
-__global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl, const float *mse,
-                            size_t out_lo, size_t out_hi) {
+__device__ __forceinline__ void fwd_apply_unit(UV &U, G *g, size_t I, int lvl, const float *mse,
+                                               size_t out_lo, size_t out_hi) {
   using FP = typename Tr::ForwardPass;
   using Acc = typename FP::Accumulator;
-  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= hi) return;
   if (lvl >= 0 && GetLevel(U, I) != lvl) return;
   FP::Apply(U, I, *g, GetForwardAcc(U, I));
   GetForwardAcc(U, I) = Acc{};
   if (mse && I >= out_lo && I < out_hi) GetBackwardAcc(U, I) = GetActivation(U, I) - mse[I - out_lo];
+}
+template <class Tr, class UV, class G>
+__global__ void k_fwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl, const float *mse,
+                            size_t out_lo, size_t out_hi) {
+  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I < hi) fwd_apply_unit<Tr>(U, g, I, lvl, mse, out_lo, out_hi);
 }
 
 // MSELoss over the output units, one thread per unit (the loss is
@@ -240,11 +253,9 @@ __global__ void k_loss_mse(UV U, size_t out_lo, size_t out_n, const float *t) {
 // Topological level L, ascending over those whose SrcLevel is L
 // (plastix.hpp:170-181).
 template <class Tr, class UV, class CV, class G>
-__global__ void k_bwd_acc(UV U, CV C, G *g, const uint32_t *out_ptr, const uint32_t *out_conn,
-                          size_t n, int L) {
+__device__ __forceinline__ void bwd_acc_unit(UV &U, CV &C, G *g, const uint32_t *out_ptr,
+                                             const uint32_t *out_conn, size_t I, int L) {
   using BP = typename Tr::BackwardPass;
-  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= n) return;
   const uint32_t b = out_ptr[I], e = out_ptr[I + 1];
   if (b == e) return;
   auto acc = GetBackwardAcc(U, I);
@@ -256,16 +267,25 @@ __global__ void k_bwd_acc(UV U, CV C, G *g, const uint32_t *out_ptr, const uint3
   }
   GetBackwardAcc(U, I) = acc;
 }
+template <class Tr, class UV, class CV, class G>
+__global__ void k_bwd_acc(UV U, CV C, G *g, const uint32_t *out_ptr, const uint32_t *out_conn,
+                          size_t n, int L) {
+  const size_t I = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I < n) bwd_acc_unit<Tr>(U, C, g, out_ptr, out_conn, I, L);
+}
 
 template <class Tr, class UV, class G>
-__global__ void k_bwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
+__device__ __forceinline__ void bwd_apply_unit(UV &U, G *g, size_t I, int lvl) {
   using BP = typename Tr::BackwardPass;
   using Acc = typename BP::Accumulator;
-  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (I >= hi) return;
   if (lvl >= 0 && GetLevel(U, I) != lvl) return;
   BP::Apply(U, I, *g, GetBackwardAcc(U, I));
   GetBackwardAcc(U, I) = Acc{};
+}
+template <class Tr, class UV, class G>
+__global__ void k_bwd_apply(UV U, G *g, size_t lo, size_t hi, int lvl) {
+  const size_t I = lo + blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (I < hi) bwd_apply_unit<Tr>(U, g, I, lvl);
 }
 
 // ---- passes in one thread: the reference's loops verbatim in order ---------
@@ -345,20 +365,108 @@ __global__ void k_update_unit(UV U, G *g, size_t n, bool seq) {
 // Per-connection update: parallel over connections, or one thread in index
 // order for sequential semantics.
 template <class Tr, bool Incoming, class UV, class CV, class G>
-__global__ void k_update_conn(UV U, CV C, G *g, size_t n, bool sequential) {
+__device__ __forceinline__ void update_conn_one(UV &U, CV &C, G *g, size_t c) {
   using UP = typename Tr::UpdateConn;
+  if (GetField<DeadTag>(C, c)) return;
+  const size_t to = GetField<ToIdTag>(C, c), from = GetField<FromIdTag>(C, c);
+  if constexpr (Incoming) UP::UpdateIncomingConnection(U, to, from, C, c, *g);
+  else UP::UpdateOutgoingConnection(U, from, to, C, c, *g);
+}
+template <class Tr, bool Incoming, class UV, class CV, class G>
+__global__ void k_update_conn(UV U, CV C, G *g, size_t n, bool sequential) {
   const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t step = sequential ? 1 : (size_t)gridDim.x * blockDim.x;
   if (sequential && first != 0) return;
-  for (size_t c = first; c < n; c += step) {
-    if (GetField<DeadTag>(C, c)) continue;
-    const size_t to = GetField<ToIdTag>(C, c), from = GetField<FromIdTag>(C, c);
-    if constexpr (Incoming) UP::UpdateIncomingConnection(U, to, from, C, c, *g);
-    else UP::UpdateOutgoingConnection(U, from, to, C, c, *g);
-  }
+  for (size_t c = first; c < n; c += step) update_conn_one<Tr, Incoming>(U, C, g, c);
 }
 
 template <class Tr, class G> __global__ void k_reset(G *g) { Tr::ResetGlobal::Reset(*g); }
+
+// ---- a whole DoStep in one CTA (small networks) ------------------------------
+// For networks of a few thousand units and connections every pass is a
+// handful of microseconds of launch latency and almost no work; one CTA runs
+// the passes of DoStep in the order and with the per-unit / per-connection
+// functions of the kernels above, a barrier where those are separate launches.
+constexpr unsigned kSmallThreads = 512;
+constexpr size_t kSmallUnits = 4096, kSmallConns = size_t(1) << 16;
+
+struct SmallStepArgs {
+  const uint32_t *in_ptr, *in_conn, *out_ptr, *out_conn;
+  uint32_t *cur;
+  size_t n_input, n, m;
+  int levels;
+  const float *mse;     // targets when MSELoss runs in the forward Apply
+  const float *loss_t;  // targets of a separate loss pass
+  size_t n_t;
+  int loss_kind;        // 0 none, 1 MSELoss per output, 2 the loss policy in one thread
+  UnitRange out;
+};
+
+template <class Tr, class UV, class CV, class G>
+__global__ void __launch_bounds__(kSmallThreads) k_step_small(UV U, CV C, G *g, SmallStepArgs a) {
+  constexpr bool topo = Tr::Model == Propagation::Topological;
+  const size_t t0 = threadIdx.x, bs = blockDim.x;
+  // DoForwardPass
+  if constexpr (topo) {
+    for (size_t I = t0; I < a.n; I += bs) a.cur[I] = a.in_ptr[I];
+    __syncthreads();
+    for (int L = 1; L <= a.levels; ++L) {
+      for (size_t I = t0; I < a.n; I += bs)
+        fwd_acc_level_unit<Tr>(U, C, g, a.in_ptr, a.in_conn, a.cur, I, L);
+      __syncthreads();
+      for (size_t I = a.n_input + t0; I < a.n; I += bs)
+        fwd_apply_unit<Tr>(U, g, I, L, a.mse, a.out.Begin, a.out.End);
+      __syncthreads();
+    }
+  } else {
+    for (size_t I = t0; I < a.n; I += bs) fwd_acc_unit<Tr>(U, C, g, a.in_ptr, a.in_conn, I);
+    __syncthreads();
+    for (size_t I = a.n_input + t0; I < a.n; I += bs)
+      fwd_apply_unit<Tr>(U, g, I, -1, a.mse, a.out.Begin, a.out.End);
+    __syncthreads();
+  }
+  // DoCalculateLoss
+  if (a.loss_kind == 1) {
+    for (size_t i = t0; i < a.out.Size(); i += bs)
+      GetBackwardAcc(U, a.out.Begin + i) = GetActivation(U, a.out.Begin + i) - a.loss_t[i];
+  } else if (a.loss_kind == 2) {
+    if constexpr (!std::is_same_v<typename Tr::Loss, NoLoss>)
+      if (t0 == 0) Tr::Loss::CalculateLoss(U, a.out, std::span<const float>(a.loss_t, a.n_t), *g);
+  }
+  __syncthreads();
+  // DoBackwardPass
+  if constexpr (!std::is_same_v<typename Tr::BackwardPass, NoBackwardPass>) {
+    if constexpr (topo) {
+      for (int L = a.levels; L >= 1; --L) {
+        for (size_t I = t0; I < a.n; I += bs)
+          bwd_acc_unit<Tr>(U, C, g, a.out_ptr, a.out_conn, I, L);
+        __syncthreads();
+        for (size_t I = a.n_input + t0; I < a.n; I += bs) bwd_apply_unit<Tr>(U, g, I, L);
+        __syncthreads();
+      }
+    } else {
+      for (size_t I = t0; I < a.n; I += bs) bwd_acc_unit<Tr>(U, C, g, a.out_ptr, a.out_conn, I, -1);
+      __syncthreads();
+      for (size_t I = t0; I < a.n; I += bs) bwd_apply_unit<Tr>(U, g, I, -1);
+      __syncthreads();
+    }
+  }
+  // DoUpdateUnitState
+  if constexpr (!std::is_same_v<typename Tr::UpdateUnit, NoUpdateUnit>) {
+    for (size_t I = t0; I < a.n; I += bs) Tr::UpdateUnit::Update(U, I, *g);
+    __syncthreads();
+  }
+  // DoUpdateConnectionState
+  if constexpr (!std::is_same_v<typename Tr::UpdateConn, NoUpdateConn>) {
+    for (size_t c = t0; c < a.m; c += bs) update_conn_one<Tr, true>(U, C, g, c);
+    __syncthreads();
+    for (size_t c = t0; c < a.m; c += bs) update_conn_one<Tr, false>(U, C, g, c);
+    __syncthreads();
+  }
+  // DoResetGlobalState
+  if constexpr (!std::is_same_v<typename Tr::ResetGlobal, NoResetGlobalState>)
+    if (t0 == 0) Tr::ResetGlobal::Reset(*g);
+}
 
 // ---- structure --------------------------------------------------------------
 
@@ -848,6 +956,7 @@ template <typename Traits> class Network {
       if (FusedStep(Inputs)) return;
     }
     if constexpr (detail::fixed_structure<Traits>()) {
+      if (UseSmallStep && SmallStep(Inputs, Targets)) return;
       if (UseGraphs && GraphStep(Inputs, Targets)) return;
       StepBody(Inputs, Targets);
       if (UseGraphs) EagerKey = StepKey(Targets);
@@ -863,6 +972,11 @@ template <typename Traits> class Network {
   // outside it. Any change of a device buffer, the level count or the number
   // of targets falls back to an ordinary step and a new capture.
   void SetGraphReplay(bool On) { UseGraphs = On; }
+
+  // Small networks (up to 4,096 units and 65,536 connections, read-only
+  // globals, parallel connection updates): DoStep is one kernel of one CTA
+  // that runs every pass in order (on by default; before graph replay).
+  void SetSingleKernelStep(bool On) { UseSmallStep = On; }
 
   void StepBody(std::span<const float> Inputs, std::span<const float> Targets) {
     // MSELoss rides in the forward pass's Apply epilogue (Pipeline, parallel
@@ -1609,6 +1723,49 @@ template <typename Traits> class Network {
     return k;
   }
 
+  bool SmallStep(std::span<const float> Inputs, std::span<const float> Targets) {
+    if constexpr (!detail::read_only_globals<Traits>() ||
+                  detail::sequential_conn_update<Traits>()) {
+      return false;
+    } else {
+      const size_t n = UA.Size(), m = CA.Size();
+      if (n > detail::kSmallUnits || m > detail::kSmallConns) return false;
+      BeginDevice();
+      if (IndexStale || NeedsResort) return false;
+      UploadInputs(Inputs);
+      detail::SmallStepArgs a{};
+      a.in_ptr = d_in_ptr;
+      a.in_conn = d_in_conn;
+      a.out_ptr = d_out_ptr;
+      a.out_conn = d_out_conn;
+      a.cur = d_cursor;
+      a.n_input = NumInput;
+      a.n = n;
+      a.m = m;
+      a.levels = NumLevels;
+      a.out = OutputRange;
+      using L = typename Traits::Loss;
+      if constexpr (!std::is_same_v<L, NoLoss>) {
+        if (!Targets.empty()) {
+          const float *t = UploadTargets(Targets);
+          const bool mse = std::is_same_v<L, MSELoss> && Targets.size() >= OutputRange.Size();
+          if (mse && Traits::Model == Propagation::Pipeline && OutputRange.Begin >= NumInput) {
+            a.mse = t;  // in the Apply epilogue, as StepBody does
+          } else {
+            a.loss_t = t;
+            a.n_t = Targets.size();
+            a.loss_kind = mse ? 1 : 2;
+          }
+        }
+      }
+      detail::k_step_small<Traits><<<1, detail::kSmallThreads, 0, Stream>>>(UV(), CV(), d_g, a);
+      cuda_check(cudaGetLastError(), "step");
+      EndDevice(true, true);
+      ++Step;
+      return true;
+    }
+  }
+
   bool GraphStep(std::span<const float> Inputs, std::span<const float> Targets) {
     BeginDevice();
     if (IndexStale || NeedsResort) return false;
@@ -1667,7 +1824,7 @@ template <typename Traits> class Network {
     return ok;
   }
 
-  bool UseGraphs = true, Capturing = false;
+  bool UseGraphs = true, UseSmallStep = true, Capturing = false;
   cudaGraphExec_t GraphExec = nullptr;
   std::vector<uintptr_t> GraphKey, EagerKey;
   cudaStream_t OwnStream = nullptr;

@@ -3,11 +3,12 @@
 // epoch, each followed by GetOutput -- the mlp-xor example's loop) written
 // against the reference's C++ API. The same source builds two ways:
 //   * with nvcc against this repository's headers: the device Network, whose
-//     DoStep replays a captured CUDA graph (argument "graph", the default) or
-//     launches every kernel of the step (argument "eager");
+//     DoStep runs as one kernel of one CTA (argument "single", the default
+//     for a network this small), replays a captured CUDA graph ("graph") or
+//     launches every kernel of the step ("eager");
 //   * with a host C++ compiler against the reference's own headers: the
 //     reference's CPU implementation (the baseline of the benchmark).
-// Usage: xor_train <epochs> [graph|eager]
+// Usage: xor_train <epochs> [single|graph|eager]
 // Prints one JSON object: training wall time (host clock around the epoch
 // loop only), steps, the last epoch's loss and whether all four XOR cases
 // are classified correctly afterwards.
@@ -73,14 +74,17 @@ struct XorTraits : plastix::DefaultNetworkTraits<> {
 
 int main(int argc, char **argv) {
   const long epochs = argc > 1 ? std::atol(argv[1]) : 5000;
-  const bool graph = !(argc > 2 && std::strcmp(argv[2], "eager") == 0);
+  const char *mode = argc > 2 ? argv[2] : "single";
   plastix::Network<XorTraits> Net(2, plastix::FullyConnected{8, plastix::RandomUniformWeight{1234}},
                                   plastix::FullyConnected{1, plastix::RandomUniformWeight{1234}});
 #ifdef __CUDACC__
-  Net.SetGraphReplay(graph);
-  const char *impl = graph ? "device, graph replay" : "device, eager launches";
+  Net.SetSingleKernelStep(std::strcmp(mode, "single") == 0);
+  Net.SetGraphReplay(std::strcmp(mode, "graph") == 0);
+  const char *impl = std::strcmp(mode, "single") == 0  ? "device, one kernel per step"
+                     : std::strcmp(mode, "graph") == 0 ? "device, graph replay"
+                                                       : "device, every pass launched";
 #else
-  (void)graph;
+  (void)mode;
   const char *impl = "reference (host)";
 #endif
   const float In[4][2] = {{0, 0}, {0, 1}, {1, 0}, {1, 1}};

@@ -1,8 +1,9 @@
-// MSELoss and graph replay inside the device Network<Traits>: the library's
-// MSELoss runs in the forward pass's Apply epilogue under DoStep (Pipeline)
-// and as a parallel per-output kernel under DoCalculateLoss; a user loss with
-// the same body is not recognised and runs as the generic one-thread loss
-// hook; DoStep replays a captured CUDA graph unless told not to. All of them
+// MSELoss and the ways DoStep runs inside the device Network<Traits>: the
+// library's MSELoss runs in the forward pass's Apply epilogue under DoStep
+// (Pipeline) and as a parallel per-output kernel under DoCalculateLoss; a
+// user loss with the same body is not recognised and runs as the generic
+// one-thread loss hook; DoStep runs as one kernel of one CTA (small
+// networks), as a replayed CUDA graph, or launching every pass. All of them
 // must leave every weight, activation, gradient and backward accumulator
 // equal bit for bit. The network: 3 inputs -> 48 sigmoid hidden -> 20 sigmoid
 // outputs, backward pass and gradient step, 40 DoSteps on seeded inputs and
@@ -78,12 +79,18 @@ struct Snapshot {
   std::vector<float> w, act, grad, bwd;
 };
 
-// split: the step as separate Do* calls (DoCalculateLoss on its own);
-// graphs: DoStep may replay a captured CUDA graph (the default).
-template <class T> Snapshot run(bool split, bool graphs = true) {
+enum Mode { kSplit, kSingleKernel, kGraph, kEager };
+
+// kSplit: the step as separate Do* calls (DoCalculateLoss on its own);
+// kSingleKernel: DoStep as one kernel (the default for a network this
+// small); kGraph: DoStep replayed as a captured CUDA graph; kEager: DoStep
+// launching every pass.
+template <class T> Snapshot run(Mode mode) {
   plastix::Network<T> Net(kIn, plastix::FullyConnected{kHidden, plastix::RandomUniformWeight{7}},
                           plastix::FullyConnected{kOut, plastix::RandomUniformWeight{8}});
-  Net.SetGraphReplay(graphs);
+  Net.SetSingleKernelStep(mode == kSingleKernel);
+  Net.SetGraphReplay(mode == kGraph);
+  const bool split = mode == kSplit;
   uint32_t h = 12345u;
   auto next = [&h] {
     h = h * 1664525u + 1013904223u;
@@ -133,25 +140,29 @@ int main() {
   using plastix::MSELoss;
   using plastix::Propagation;
   int bad = 0;
+  const char *names[] = {"split Do* calls", "single-kernel DoStep", "graph-replayed DoStep",
+                         "eager DoStep"};
+  auto check = [&](const char *model, const Snapshot &want, const Snapshot &got, const char *loss,
+                   int mode) {
+    char what[160];
+    std::snprintf(what, sizeof what, "%s, %s loss, %s", model, loss, names[mode]);
+    bad += compare(what, got, want);
+  };
   {
-    const Snapshot user = run<Traits<UserMSE, Propagation::Pipeline>>(false);
-    bad += compare("pipeline DoStep (loss in the Apply epilogue)",
-                   run<Traits<MSELoss, Propagation::Pipeline>>(false), user);
-    bad += compare("pipeline DoCalculateLoss (parallel loss)",
-                   run<Traits<MSELoss, Propagation::Pipeline>>(true), user);
-    bad += compare("pipeline DoStep without graph replay",
-                   run<Traits<MSELoss, Propagation::Pipeline>>(false, false), user);
-    bad += compare("pipeline DoStep, user loss, without graph replay",
-                   run<Traits<UserMSE, Propagation::Pipeline>>(false, false), user);
+    const Snapshot want = run<Traits<UserMSE, Propagation::Pipeline>>(kSplit);
+    for (int m : {kSplit, kSingleKernel, kGraph, kEager}) {
+      check("pipeline", want, run<Traits<MSELoss, Propagation::Pipeline>>(Mode(m)), "library", m);
+      check("pipeline", want, run<Traits<UserMSE, Propagation::Pipeline>>(Mode(m)), "user", m);
+    }
   }
   {
-    const Snapshot user = run<Traits<UserMSE, Propagation::Topological>>(false);
-    bad += compare("topological DoStep (parallel loss)",
-                   run<Traits<MSELoss, Propagation::Topological>>(false), user);
-    bad += compare("topological DoStep without graph replay",
-                   run<Traits<MSELoss, Propagation::Topological>>(false, false), user);
-    bad += compare("topological DoCalculateLoss (parallel loss)",
-                   run<Traits<MSELoss, Propagation::Topological>>(true), user);
+    const Snapshot want = run<Traits<UserMSE, Propagation::Topological>>(kSplit);
+    for (int m : {kSplit, kSingleKernel, kGraph, kEager}) {
+      check("topological", want, run<Traits<MSELoss, Propagation::Topological>>(Mode(m)),
+            "library", m);
+      check("topological", want, run<Traits<UserMSE, Propagation::Topological>>(Mode(m)), "user",
+            m);
+    }
   }
   if (!bad) std::printf("ok\n");
   return bad;
